@@ -1,0 +1,148 @@
+/*
+ * ssla_b200 — C ABI of the B200 (sm_100a) kernels behind SSLA's gated-linear-attention
+ * hot path.  Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, enqueues its kernels on that stream without synchronising, and returns an
+ * int status (SSLA_OK or a negative code; ssla_last_error() gives the message).
+ *
+ * Layouts follow the reference operators: packed variable-length sequences
+ * [T_total, H, D] with int64 cu_seqlens[N+1] (ops/gla/chunk.py:1131-1150,
+ * ops/common/scan.py:148-158).  All tensors are dense row-major (contiguous).
+ * The reference is pure Python/Triton; each declaration names the reference
+ * function whose kernels it replaces (path within the haohq19/ssla project).
+ */
+#ifndef SSLA_B200_H_
+#define SSLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ssla_stream_t; /* == cudaStream_t */
+
+/* status codes */
+#define SSLA_OK 0
+#define SSLA_ERR_INVALID_ARG -1
+#define SSLA_ERR_CUDA -2
+#define SSLA_ERR_WORKSPACE -3
+#define SSLA_ERR_UNSUPPORTED -4
+
+/* element type codes */
+#define SSLA_F32 0
+#define SSLA_BF16 1
+#define SSLA_F16 2
+
+/* ------------------------------------------------------------------ library */
+int ssla_abi_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* ssla_last_error(void);
+
+/* ------------------------------------------------------------------ scan
+ * h_t = g_t * h_{t-1} + u_t per channel, h_{-1} = 0, over each sequence of u,g [T,C].
+ * Replaces ops/common/scan.py:11-43 (sequential_scan_fwd) and SequentialScan.forward
+ * (ops/common/scan.py:92-114).  fp32 arithmetic, one rounding per multiply and add.
+ */
+int ssla_scan_fwd(const void* u, int dtype_u, const void* g, int dtype_g, void* h, int dtype_h,
+                  const int64_t* cu_seqlens, int64_t n_seqs, int64_t T, int64_t C,
+                  ssla_stream_t stream);
+/* Reverse pass: du = dh, dg = dh * h_{t-1}, dh_{t-1} = dh_t * g_t (+ do_{t-1}).
+ * Replaces ops/common/scan.py:46-86 (sequential_scan_bwd) and SequentialScan.backward
+ * (ops/common/scan.py:116-137). */
+int ssla_scan_bwd(const void* dout, int dtype_do, const void* g, int dtype_g, const void* h,
+                  int dtype_h, void* du, int dtype_du, void* dg, int dtype_dg,
+                  const int64_t* cu_seqlens, int64_t n_seqs, int64_t T, int64_t C,
+                  ssla_stream_t stream);
+
+/* ------------------------------------------------------------------ scalar GLA
+ * Per-channel scalar state: S_t = exp(g_t) S_{t-1} + k_t v_t, o_t = scale q_t S_t.
+ * q,k,v,g,o [T,H]; h0/ht [N,H] fp32 (nullable).  Replaces chunk_gla_scalar
+ * (ops/gla/chunk_scalar.py:1044-1092) with the recurrence of
+ * ops/gla/naive_scalar.py:7-66. */
+int ssla_gla_scalar_fwd(const void* q, const void* k, const void* v, const void* g, int dtype,
+                        int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
+                        int64_t H, float scale, const float* h0, void* o, float* ht,
+                        ssla_stream_t stream);
+/* dq,dk,dv in `dtype`, dg fp32 [T,H], dh0 fp32 [N,H] (nullable), dht nullable.
+ * Replaces ChunkGLAScalarFunction.backward (ops/gla/chunk_scalar.py:1025-1041). */
+int ssla_gla_scalar_bwd(const void* q, const void* k, const void* v, const void* g, int dtype,
+                        int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
+                        int64_t H, float scale, const float* h0, const void* dout,
+                        const float* dht, void* dq, void* dk, void* dv, float* dg, float* dh0,
+                        ssla_stream_t stream);
+
+/* ------------------------------------------------------------------ recurrent GLA
+ * Token-by-token GLA with a [K,V] fp32 state per (sequence, head):
+ *   S_t = diag(exp(g_t)) S_{t-1} + k_t v_t^T,   o_t = (scale q_t)^T S_t.
+ * q,k,g [T,H,K], v,o [T,H,V] (o in `dtype`); h0/ht [N,H,K,V] fp32, each nullable.
+ * Semantics of naive_gla_recurrent (ops/gla/naive.py:50-111); exposed as
+ * fused_recurrent_gla with chunk_gla's signature (ops/gla/chunk.py:1120-1129). */
+int ssla_recurrent_gla_fwd(const void* q, const void* k, const void* v, const void* g, int dtype,
+                           int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
+                           int64_t H, int64_t K, int64_t V, float scale, const float* h0,
+                           void* o, float* ht, ssla_stream_t stream);
+
+/* ------------------------------------------------------------------ chunked GLA
+ * chunk_gla forward / backward (ops/gla/chunk.py:906-1053, ops/common/chunk_h.py:242-347).
+ * Layout: q,k,g [T,H,K]; v,o,do [T,H,V]; h0,ht,dht,dh0 [N,H,K,V] fp32 (nullable).
+ * `states` [max_chunks,H,K,V] fp32 receives the state at the start of every 64-token
+ * chunk (written by fwd, read by bwd); max_chunks = ssla_chunk_gla_max_chunks(N,T).
+ * `workspace` is caller-allocated device scratch of ssla_chunk_gla_workspace_bytes().
+ * dq,dk,dv are written in `dtype`; dg in fp32 (the reference returns dg in fp32,
+ * ops/gla/chunk.py:1116).  K, V <= 64. */
+int64_t ssla_chunk_gla_max_chunks(int64_t n_seqs, int64_t T);
+size_t ssla_chunk_gla_workspace_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K,
+                                      int64_t V);
+int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, const void* g, int dtype,
+                       int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
+                       int64_t H, int64_t K, int64_t V, float scale, const float* h0, void* o,
+                       float* ht, float* states, void* workspace, size_t workspace_bytes,
+                       ssla_stream_t stream);
+int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* g, int dtype,
+                       int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
+                       int64_t H, int64_t K, int64_t V, float scale, const float* states,
+                       const void* dout, const float* dht, void* dq, void* dk, void* dv,
+                       float* dg, float* dh0, void* workspace, size_t workspace_bytes,
+                       ssla_stream_t stream);
+
+/* ------------------------------------------------------------------ segments
+ * Reductions of rows of src [R,C] into out [S,C] by a row->segment index [R] (int64).
+ * Semantics of torch_scatter.scatter_max / scatter_mean / scatter_sum (dim=0) as called
+ * by layers/sparse_pooling.py:33: max with argmax (smallest row index among ties,
+ * R for empty segments, value 0 for empty segments); sum accumulated in fp32 in
+ * ascending row order; mean = sum / max(count,1).  Deterministic, no atomics on data.
+ *
+ * Sorted path: `index` non-decreasing; `seg_offsets` [S+1] int64 is produced by
+ * ssla_segment_offsets_sorted.  Unsorted path: ssla_segment_csr builds a CSR
+ * (offsets + rows in ascending order per segment) from any index. */
+int ssla_segment_offsets_sorted(const int64_t* index, int64_t R, int64_t S, int64_t* seg_offsets,
+                                ssla_stream_t stream);
+size_t ssla_segment_csr_workspace_bytes(int64_t R, int64_t S);
+int ssla_segment_csr(const int64_t* index, int64_t R, int64_t S, int64_t* seg_offsets,
+                     int64_t* rows, void* workspace, size_t workspace_bytes,
+                     ssla_stream_t stream);
+/* op: 0 = sum, 1 = mean, 2 = max.  rows == NULL means identity (sorted input).
+ * arg (int64 [S,C]) is written for max when non-NULL. */
+#define SSLA_REDUCE_SUM 0
+#define SSLA_REDUCE_MEAN 1
+#define SSLA_REDUCE_MAX 2
+int ssla_segment_reduce(const void* src, int dtype, const int64_t* seg_offsets, const int64_t* rows,
+                        int64_t R, int64_t S, int64_t C, int op, void* out, int64_t* arg,
+                        ssla_stream_t stream);
+/* out[r,:] = src[index[r],:]  (row gather; inverse of pooling, layers/sparse_pooling.py) */
+int ssla_gather_rows(const void* src, int dtype, const int64_t* index, int64_t R, int64_t C,
+                     void* out, ssla_stream_t stream);
+/* out[d,:] = sum over p with index[p]==d of src[p,:], fp32 sum in ascending p; zero rows
+ * for unused d.  Deterministic replacement of utils/async_utils.py:243-264
+ * (zeros(E,C).index_add_(0, idx, src)). */
+size_t ssla_index_add_rows_workspace_bytes(int64_t P, int64_t D);
+int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_t P, int64_t D,
+                        int64_t C, void* out, void* workspace, size_t workspace_bytes,
+                        ssla_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSLA_B200_H_ */

@@ -1,0 +1,755 @@
+// Chunked gated linear attention, forward and backward (chunk_gla, ops/gla/chunk.py:906-1116).
+//
+// Algorithm (per sequence, per head, chunks of 64 tokens, gc = in-chunk cumulative log-decay,
+// gL = gc of the chunk's last token, h = state at the chunk start):
+//   o_i     = scale (q_i * exp(gc_i)) h + sum_{j<=i} A_ij v_j
+//   A_ij    = scale sum_k q_ik k_jk exp(gc_ik - gc_jk)                        (j <= i)
+//   h_next  = exp(gL) * h + sum_j (k_j * exp(gL - gc_j))^T v_j
+// The reference runs the state recurrence as one serial program per (sequence, head-block)
+// (ops/common/chunk_h.py:13-128), i.e. 8-32 programs for its benchmark.  Here it is split in
+// two levels so all 148 SMs stay busy:
+//   1. local_state: every chunk computes its increment dS = sum_j (k_j exp(gL-gc_j))^T v_j
+//      and decay exp(gL) independently;
+//   2. state_scan: h_{c+1} = exp(gL_c) * h_c + dS_c is element-wise in (k, v), so one thread
+//      per state element walks the chunks of its sequence (N*H*K*V threads);
+//   3. output: every chunk computes o from h_c (chunk-parallel).
+// The backward mirrors this with the adjoint state (chunk_bwd_dh, ops/common/chunk_h.py:131-239)
+// and one fused per-chunk kernel for dq, dk, dv, dg (ops/gla/chunk.py:253-641).
+//
+// Numerics: exp(gc_i - gc_j) is factorised per 16-row sub-chunk around a reference row
+// (the sub-chunk scheme of ops/gla/chunk.py:23-176), so every factor stays bounded; a
+// sub-chunk whose decay span could overflow the factorisation falls back to exact
+// per-element exponents.  This file is the CUDA-core (fp32 FMA) implementation: it is used
+// for fp32 inputs, where results must match an fp32 reference to ~1e-6, and for shapes the
+// tensor-core kernels (chunk_gla_tc.cu) do not cover.
+#include "chunk_gla.cuh"
+
+namespace ssla {
+namespace chunk {
+namespace {
+
+constexpr int NTHR = 256;
+
+// --------------------------------------------------------------------------- prep + scans
+__global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __restrict__ cu,
+                                                             int64_t N, int64_t* __restrict__ off) {
+  __shared__ int64_t warp_sums[32];
+  __shared__ int64_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < N; base += 1024) {
+    const int64_t n = base + tid;
+    int64_t x = 0;
+    if (n < N) {
+      const int64_t len = cu[n + 1] - cu[n];
+      x = (len + BT - 1) / BT;
+    }
+    int64_t incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int64_t w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int64_t before = carry + (warp > 0 ? warp_sums[warp - 1] : 0);
+    if (n < N) off[n] = before + incl - x;
+    __syncthreads();
+    if (tid == 1023) carry = before + incl;
+    __syncthreads();
+  }
+  if (tid == 0) off[N] = carry;
+}
+
+__global__ void __launch_bounds__(256) state_scan_kernel(
+    const float* __restrict__ dS, const float* __restrict__ decay,
+    const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
+    const float* __restrict__ init, float* __restrict__ per_chunk, float* __restrict__ fin,
+    bool reverse) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t KV = (int64_t)K * V;
+  if (idx >= N * H * KV) return;
+  const int64_t seq = idx / (H * KV);
+  const int64_t rem = idx - seq * H * KV;
+  const int head = (int)(rem / KV);
+  const int64_t kv = rem - head * KV;
+  const int k = (int)(kv / V);
+  const int64_t c0 = chunk_off[seq], c1 = chunk_off[seq + 1];
+  float x = init ? init[idx] : 0.f;
+  if (!reverse) {
+#pragma unroll 4
+    for (int64_t c = c0; c < c1; ++c) {
+      const int64_t e = (c * H + head) * KV + kv;
+      per_chunk[e] = x;
+      x = fmaf(decay[(c * H + head) * K + k], x, dS[e]);
+    }
+  } else {
+#pragma unroll 4
+    for (int64_t c = c1 - 1; c >= c0; --c) {
+      const int64_t e = (c * H + head) * KV + kv;
+      per_chunk[e] = x;
+      x = fmaf(decay[(c * H + head) * K + k], x, dS[e]);
+    }
+  }
+  if (fin) fin[idx] = x;
+}
+
+// --------------------------------------------------------------------------- tile helpers
+template <int P> struct L { static constexpr int LD = P + 1; };
+constexpr int LDA = BT + 1;
+
+// [BT, P] fp32 tile of rows t0.. (row stride H*D), zero-padded beyond `len` rows / D cols.
+template <typename T, int P>
+__device__ __forceinline__ void load_tile(float* s, const T* __restrict__ src, int64_t t0, int len,
+                                          int H, int head, int D) {
+  constexpr int LD = L<P>::LD;
+  for (int e = threadIdx.x; e < BT * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    float x = 0.f;
+    if (r < len && c < D) x = ldf(src + ((t0 + r) * H + head) * (int64_t)D + c);
+    s[r * LD + c] = x;
+  }
+}
+
+// [P, P] fp32 state tile from [.., K, V] global (zero pad).
+template <int P>
+__device__ __forceinline__ void load_state(float* s, const float* __restrict__ src, int K, int V) {
+  constexpr int LD = L<P>::LD;
+  for (int e = threadIdx.x; e < P * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    s[r * LD + c] = (r < K && c < V) ? src[(int64_t)r * V + c] : 0.f;
+  }
+}
+
+// In-place inclusive cumulative sum over the BT rows of each column (one warp per column).
+template <int P>
+__device__ __forceinline__ void col_cumsum(float* s) {
+  constexpr int LD = L<P>::LD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int c = warp; c < P; c += nw) {
+    const float a = s[(2 * lane) * LD + c], b = s[(2 * lane + 1) * LD + c];
+    float x = a + b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    float excl = __shfl_up_sync(0xffffffffu, x, 1);
+    if (lane == 0) excl = 0.f;
+    s[(2 * lane) * LD + c] = excl + a;
+    s[(2 * lane + 1) * LD + c] = excl + a + b;
+  }
+}
+
+// C[m][n] = sum_l a(l,m) * b(l,n), M x N outputs in 4x4 register tiles over the block.
+template <int M, int N, class FA, class FB, class FE>
+__device__ __forceinline__ void mm4(int Lr, FA a, FB b, FE epi) {
+  constexpr int TN = N / 4, TILES = (M / 4) * TN;
+  for (int tile = threadIdx.x; tile < TILES; tile += blockDim.x) {
+    const int m0 = (tile / TN) * 4, n0 = (tile - (tile / TN) * TN) * 4;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int l = 0; l < Lr; ++l) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { av[i] = a(l, m0 + i); bv[i] = b(l, n0 + i); }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) epi(m0 + i, n0 + j, acc[i][j]);
+  }
+}
+
+// Per sub-chunk r: reference row value ref[r][c] = gc[16r+7][c], and whether the factorised
+// exponent form is safe for (a) rows of r against columns <= end(r) (A, dq) and (b) columns
+// of r against rows >= start(r) (dk).
+template <int P>
+__device__ __forceinline__ void sub_chunk_refs(const float* sg, float* ref, int* exact_q,
+                                               int* exact_k) {
+  constexpr int LD = L<P>::LD;
+  __shared__ float lo[NC][P], hi[NC][P];
+  if (threadIdx.x < NC) { exact_q[threadIdx.x] = 0; exact_k[threadIdx.x] = 0; }
+  for (int e = threadIdx.x; e < NC * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    float mn = sg[(r * BC) * LD + c], mx = mn;
+    for (int i = 1; i < BC; ++i) {
+      const float x = sg[(r * BC + i) * LD + c];
+      mn = fminf(mn, x);
+      mx = fmaxf(mx, x);
+    }
+    lo[r][c] = mn;
+    hi[r][c] = mx;
+    ref[r * P + c] = sg[(r * BC + BC / 2 - 1) * LD + c];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < NC * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    const float rf = ref[r * P + c];
+    float mn = lo[r][c], mxl = hi[r][c];
+    for (int s = 0; s < r; ++s) mn = fminf(mn, lo[s][c]);
+    for (int s = r + 1; s < NC; ++s) mxl = fmaxf(mxl, hi[s][c]);
+    if (hi[r][c] - rf > kSpanLimit || rf - mn > kSpanLimit) atomicOr(&exact_q[r], 1);
+    if (mxl - rf > kSpanLimit || rf - lo[r][c] > kSpanLimit) atomicOr(&exact_k[r], 1);
+  }
+  __syncthreads();
+}
+
+// --------------------------------------------------------------------------- local state
+// mode 0: dS = sum_t (k_t exp(gL - gc_t))^T v_t       (forward state increment)
+// mode 1: dS = sum_t (scale q_t exp(gc_t))^T do_t      (backward adjoint increment)
+template <typename T, typename Tg, int P>
+__global__ void __launch_bounds__(NTHR) local_state_kernel(
+    int mode, const T* __restrict__ a_src, const T* __restrict__ b_src, const Tg* __restrict__ g,
+    const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off, int64_t N, int H,
+    int K, int V, float scale, float* __restrict__ dS, float* __restrict__ decay) {
+  constexpr int LD = L<P>::LD;
+  extern __shared__ float sm[];
+  float* sg = sm;
+  float* sa = sg + BT * LD;
+  float* sb = sa + BT * LD;
+  __shared__ float sL[P];
+  const int64_t cid = blockIdx.x;
+  const int head = blockIdx.y;
+  int64_t seq, t0;
+  int len;
+  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  load_tile<Tg, P>(sg, g, t0, len, H, head, K);
+  load_tile<T, P>(sa, a_src, t0, len, H, head, K);
+  load_tile<T, P>(sb, b_src, t0, len, H, head, V);
+  __syncthreads();
+  col_cumsum<P>(sg);
+  __syncthreads();
+  if (threadIdx.x < P) sL[threadIdx.x] = sg[(BT - 1) * LD + threadIdx.x];
+  __syncthreads();
+  for (int e = threadIdx.x; e < BT * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    const float gc = sg[r * LD + c];
+    sa[r * LD + c] *= (mode == 0) ? expf(sL[c] - gc) : scale * expf(gc);
+  }
+  __syncthreads();
+  float* out = dS + (cid * H + head) * (int64_t)K * V;
+  mm4<P, P>(
+      BT, [&](int l, int m) { return sa[l * LD + m]; }, [&](int l, int n) { return sb[l * LD + n]; },
+      [&](int m, int n, float x) {
+        if (m < K && n < V) out[(int64_t)m * V + n] = x;
+      });
+  if (threadIdx.x < K) decay[(cid * H + head) * K + threadIdx.x] = expf(sL[threadIdx.x]);
+}
+
+// --------------------------------------------------------------------------- forward output
+template <typename T, typename Tg, int P>
+__global__ void __launch_bounds__(NTHR) fwd_o_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off,
+    int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
+    T* __restrict__ o) {
+  constexpr int LD = L<P>::LD;
+  extern __shared__ float sm[];
+  float* sq = sm;
+  float* sk = sq + BT * LD;
+  float* sg = sk + BT * LD;
+  float* sv = sg + BT * LD;
+  float* sh = sv + BT * LD;
+  float* sW = sh + P * LD;
+  float* sQh = sW + BT * LD;
+  float* sO = sQh + BT * LD;
+  float* sA = sO + BT * LD;
+  __shared__ float ref[NC * P];
+  __shared__ int exact_q[NC], exact_k[NC];
+  const int64_t cid = blockIdx.x;
+  const int head = blockIdx.y;
+  int64_t seq, t0;
+  int len;
+  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  load_tile<T, P>(sq, q, t0, len, H, head, K);
+  load_tile<T, P>(sk, k, t0, len, H, head, K);
+  load_tile<Tg, P>(sg, g, t0, len, H, head, K);
+  load_tile<T, P>(sv, v, t0, len, H, head, V);
+  load_state<P>(sh, states + (cid * H + head) * (int64_t)K * V, K, V);
+  for (int e = threadIdx.x; e < BT * LDA; e += blockDim.x) sA[e] = 0.f;
+  __syncthreads();
+  col_cumsum<P>(sg);
+  __syncthreads();
+  sub_chunk_refs<P>(sg, ref, exact_q, exact_k);
+  for (int e = threadIdx.x; e < BT * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    const float gc = sg[r * LD + c], xq = sq[r * LD + c] * scale;
+    sW[r * LD + c] = xq * expf(gc);
+    sQh[r * LD + c] = xq * expf(gc - ref[(r / BC) * P + c]);
+  }
+  __syncthreads();
+  // inter-chunk part: sO = (scale q exp(gc)) h
+  mm4<BT, P>(
+      P, [&](int l, int m) { return sW[m * LD + l]; }, [&](int l, int n) { return sh[l * LD + n]; },
+      [&](int m, int n, float x) { sO[m * LD + n] = x; });
+  // intra-chunk scores, one 16-row sub-chunk at a time
+  for (int r = 0; r < NC; ++r) {
+    __syncthreads();
+    const int jend = (r + 1) * BC;  // columns 0..jend-1
+    for (int e = threadIdx.x; e < jend * P; e += blockDim.x) {
+      const int j = e / P, c = e - j * P;
+      sW[j * LD + c] = sk[j * LD + c] * expf(ref[r * P + c] - sg[j * LD + c]);
+    }
+    __syncthreads();
+    const bool ex = exact_q[r] != 0;
+    for (int e = threadIdx.x; e < BC * jend; e += blockDim.x) {
+      const int ii = e / jend, j = e - ii * jend, i = r * BC + ii;
+      if (j > i) continue;
+      float acc = 0.f;
+      if (!ex) {
+        for (int c = 0; c < P; ++c) acc = fmaf(sQh[i * LD + c], sW[j * LD + c], acc);
+      } else {
+        for (int c = 0; c < P; ++c)
+          acc = fmaf(sq[i * LD + c] * scale, sk[j * LD + c] * expf(sg[i * LD + c] - sg[j * LD + c]), acc);
+      }
+      sA[i * LDA + j] = acc;
+    }
+  }
+  __syncthreads();
+  T* out = o + (t0 * H + head) * (int64_t)V;
+  const int64_t ostride = (int64_t)H * V;
+  mm4<BT, P>(
+      BT, [&](int l, int m) { return sA[m * LDA + l]; }, [&](int l, int n) { return sv[l * LD + n]; },
+      [&](int m, int n, float x) {
+        if (m < len && n < V) stf(out + m * ostride + n, sO[m * LD + n] + x);
+      });
+}
+
+// --------------------------------------------------------------------------- backward
+template <typename T, typename Tg, int P>
+__global__ void __launch_bounds__(NTHR) bwd_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off,
+    int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
+    const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg) {
+  constexpr int LD = L<P>::LD;
+  extern __shared__ float sm[];
+  float* sq = sm;
+  float* sk = sq + BT * LD;
+  float* sg = sk + BT * LD;
+  float* sv = sg + BT * LD;
+  float* sdo = sv + BT * LD;
+  float* sh = sdo + BT * LD;
+  float* sdh = sh + P * LD;
+  float* sW = sdh + P * LD;
+  float* sDQ = sW + BT * LD;  // holds q-hat while the scores are rebuilt
+  float* sDK = sDQ + BT * LD;
+  float* sA = sDK + BT * LD;
+  float* sdA = sA + BT * LDA;
+  __shared__ float ref[NC * P];
+  __shared__ float sL[P], sLg[P];
+  __shared__ int exact_q[NC], exact_k[NC];
+  const int64_t cid = blockIdx.x;
+  const int head = blockIdx.y;
+  int64_t seq, t0;
+  int len;
+  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  load_tile<T, P>(sq, q, t0, len, H, head, K);
+  load_tile<T, P>(sk, k, t0, len, H, head, K);
+  load_tile<Tg, P>(sg, g, t0, len, H, head, K);
+  load_tile<T, P>(sv, v, t0, len, H, head, V);
+  load_tile<T, P>(sdo, dout, t0, len, H, head, V);
+  const int64_t soff = (cid * H + head) * (int64_t)K * V;
+  load_state<P>(sh, states + soff, K, V);
+  load_state<P>(sdh, dstates + soff, K, V);
+  for (int e = threadIdx.x; e < BT * LDA; e += blockDim.x) { sA[e] = 0.f; sdA[e] = 0.f; }
+  __syncthreads();
+  col_cumsum<P>(sg);
+  __syncthreads();
+  if (threadIdx.x < P) sL[threadIdx.x] = sg[(BT - 1) * LD + threadIdx.x];
+  sub_chunk_refs<P>(sg, ref, exact_q, exact_k);  // ends with __syncthreads
+  const float* sQh = sDQ;
+  for (int e = threadIdx.x; e < BT * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    sDQ[r * LD + c] = sq[r * LD + c] * scale * expf(sg[r * LD + c] - ref[(r / BC) * P + c]);
+  }
+  // ---- scores A (recomputed) and dA = do v^T (lower triangle)
+  for (int r = 0; r < NC; ++r) {
+    __syncthreads();
+    const int jend = (r + 1) * BC;
+    for (int e = threadIdx.x; e < jend * P; e += blockDim.x) {
+      const int j = e / P, c = e - j * P;
+      sW[j * LD + c] = sk[j * LD + c] * expf(ref[r * P + c] - sg[j * LD + c]);
+    }
+    __syncthreads();
+    const bool ex = exact_q[r] != 0;
+    for (int e = threadIdx.x; e < BC * jend; e += blockDim.x) {
+      const int ii = e / jend, j = e - ii * jend, i = r * BC + ii;
+      if (j > i) continue;
+      float acc = 0.f, dacc = 0.f;
+      if (!ex) {
+        for (int c = 0; c < P; ++c) acc = fmaf(sQh[i * LD + c], sW[j * LD + c], acc);
+      } else {
+        for (int c = 0; c < P; ++c)
+          acc = fmaf(sq[i * LD + c] * scale, sk[j * LD + c] * expf(sg[i * LD + c] - sg[j * LD + c]), acc);
+      }
+      for (int c = 0; c < P; ++c) dacc = fmaf(sdo[i * LD + c], sv[j * LD + c], dacc);
+      sA[i * LDA + j] = acc;
+      sdA[i * LDA + j] = dacc;
+    }
+  }
+  __syncthreads();
+  // ---- dv = A^T do + (k exp(gL - gc)) dh_next
+  for (int e = threadIdx.x; e < BT * P; e += blockDim.x) {
+    const int r = e / P, c = e - r * P;
+    sW[r * LD + c] = sk[r * LD + c] * expf(sL[c] - sg[r * LD + c]);
+  }
+  __syncthreads();
+  {
+    T* out = dv + (t0 * H + head) * (int64_t)V;
+    const int64_t st = (int64_t)H * V;
+    mm4<BT, P>(
+        BT + P,
+        [&](int l, int m) { return l < BT ? sA[l * LDA + m] : sW[m * LD + (l - BT)]; },
+        [&](int l, int n) { return l < BT ? sdo[l * LD + n] : sdh[(l - BT) * LD + n]; },
+        [&](int m, int n, float x) {
+          if (m < len && n < V) stf(out + m * st + n, x);
+        });
+  }
+  __syncthreads();
+  // ---- dq inter: scale exp(gc) * (do h^T);  dk inter: exp(gL - gc) * (v dh^T)
+  mm4<BT, P>(
+      P, [&](int l, int m) { return sdo[m * LD + l]; }, [&](int l, int n) { return sh[n * LD + l]; },
+      [&](int m, int n, float x) { sDQ[m * LD + n] = x * scale * expf(sg[m * LD + n]); });
+  mm4<BT, P>(
+      P, [&](int l, int m) { return sv[m * LD + l]; }, [&](int l, int n) { return sdh[n * LD + l]; },
+      [&](int m, int n, float x) { sDK[m * LD + n] = x * expf(sL[n] - sg[m * LD + n]); });
+  __syncthreads();
+  // gate gradient of the chunk's total decay: exp(gL) sum_v h dh + sum_j k_j dk_inter_j
+  if (threadIdx.x < P) {
+    const int c = threadIdx.x;
+    float a = 0.f, b = 0.f;
+    for (int vv = 0; vv < P; ++vv) a = fmaf(sh[c * LD + vv], sdh[c * LD + vv], a);
+    for (int j = 0; j < BT; ++j) b = fmaf(sk[j * LD + c], sDK[j * LD + c], b);
+    sLg[c] = expf(sL[c]) * a + b;
+  }
+  // ---- dq intra (rows of sub-chunk r against columns <= end(r))
+  for (int r = 0; r < NC; ++r) {
+    __syncthreads();
+    const int jend = (r + 1) * BC;
+    for (int e = threadIdx.x; e < jend * P; e += blockDim.x) {
+      const int j = e / P, c = e - j * P;
+      sW[j * LD + c] = sk[j * LD + c] * expf(ref[r * P + c] - sg[j * LD + c]);
+    }
+    __syncthreads();
+    if (!exact_q[r]) {
+      mm4<BC, P>(
+          jend, [&](int l, int m) { return sdA[(r * BC + m) * LDA + l]; },
+          [&](int l, int n) { return sW[l * LD + n]; },
+          [&](int m, int n, float x) {
+            const int i = r * BC + m;
+            sDQ[i * LD + n] += scale * x * expf(sg[i * LD + n] - ref[r * P + n]);
+          });
+    } else {
+      for (int e = threadIdx.x; e < BC * P; e += blockDim.x) {
+        const int ii = e / P, c = e - ii * P, i = r * BC + ii;
+        float acc = 0.f;
+        for (int j = 0; j <= i; ++j)
+          acc = fmaf(sdA[i * LDA + j], sk[j * LD + c] * expf(sg[i * LD + c] - sg[j * LD + c]), acc);
+        sDQ[i * LD + c] += scale * acc;
+      }
+    }
+  }
+  // ---- dk intra (columns of sub-chunk s against rows >= start(s))
+  for (int s = 0; s < NC; ++s) {
+    __syncthreads();
+    const int i0 = s * BC;
+    for (int e = threadIdx.x; e < (BT - i0) * P; e += blockDim.x) {
+      const int i = i0 + e / P, c = e - (e / P) * P;
+      sW[i * LD + c] = sq[i * LD + c] * scale * expf(sg[i * LD + c] - ref[s * P + c]);
+    }
+    __syncthreads();
+    if (!exact_k[s]) {
+      mm4<BC, P>(
+          BT - i0, [&](int l, int m) { return sdA[(i0 + l) * LDA + (i0 + m)]; },
+          [&](int l, int n) { return sW[(i0 + l) * LD + n]; },
+          [&](int m, int n, float x) {
+            const int j = i0 + m;
+            sDK[j * LD + n] += x * expf(ref[s * P + n] - sg[j * LD + n]);
+          });
+    } else {
+      for (int e = threadIdx.x; e < BC * P; e += blockDim.x) {
+        const int jj = e / P, c = e - jj * P, j = i0 + jj;
+        float acc = 0.f;
+        for (int i = j; i < BT; ++i)
+          acc = fmaf(sdA[i * LDA + j], sq[i * LD + c] * expf(sg[i * LD + c] - sg[j * LD + c]), acc);
+        sDK[j * LD + c] += scale * acc;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- write dq, dk; dg = reverse in-chunk cumsum of (q dq - k dk) (+ decay term at the end)
+  {
+    const int64_t st = (int64_t)H * K;
+    T* oq = dq + (t0 * H + head) * (int64_t)K;
+    T* ok = dk + (t0 * H + head) * (int64_t)K;
+    for (int e = threadIdx.x; e < len * P; e += blockDim.x) {
+      const int r = e / P, c = e - r * P;
+      if (c < K) {
+        stf(oq + r * st + c, sDQ[r * LD + c]);
+        stf(ok + r * st + c, sDK[r * LD + c]);
+      }
+    }
+    float* og = dg + (t0 * H + head) * (int64_t)K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int c = warp; c < K; c += nw) {
+      // rows 2*lane, 2*lane+1; reverse inclusive scan over rows
+      float x0 = sq[(2 * lane) * LD + c] * sDQ[(2 * lane) * LD + c] -
+                 sk[(2 * lane) * LD + c] * sDK[(2 * lane) * LD + c];
+      float x1 = sq[(2 * lane + 1) * LD + c] * sDQ[(2 * lane + 1) * LD + c] -
+                 sk[(2 * lane + 1) * LD + c] * sDK[(2 * lane + 1) * LD + c];
+      if (lane == 31) x1 += sLg[c];
+      float x = x0 + x1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, x, o);
+        if (lane + o < 32) x += y;
+      }
+      float after = __shfl_down_sync(0xffffffffu, x, 1);  // sum over rows > 2*lane+1
+      if (lane == 31) after = 0.f;
+      const float r1 = after + x1, r0 = r1 + x0;
+      if (2 * lane < len) og[(2 * lane) * st + c] = r0;
+      if (2 * lane + 1 < len) og[(2 * lane + 1) * st + c] = r1;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- launchers
+template <int P> constexpr size_t smem_local() { return 3 * BT * L<P>::LD * 4; }
+template <int P> constexpr size_t smem_fwd_o() {
+  return (7 * BT * L<P>::LD + P * L<P>::LD + BT * LDA) * 4;
+}
+template <int P> constexpr size_t smem_bwd() {
+  return (8 * BT * L<P>::LD + 2 * P * L<P>::LD + 2 * BT * LDA) * 4;
+}
+
+template <typename T, typename Tg, int P>
+int run_local(int mode, const void* a_src, const void* b_src, const void* g, const int64_t* cu,
+              const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+              float* dS, float* decay, cudaStream_t s) {
+  auto kern = local_state_kernel<T, Tg, P>;
+  const size_t smem = smem_local<P>();
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>(mode, (const T*)a_src, (const T*)b_src,
+                                                 (const Tg*)g, cu, off, N, H, K, V, scale, dS, decay);
+  SSLA_CHECK_LAUNCH("chunk_gla local_state");
+  return SSLA_OK;
+}
+
+template <typename T, typename Tg, int P>
+int run_fwd_o(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
+              const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+              const float* states, void* o, cudaStream_t s) {
+  auto kern = fwd_o_kernel<T, Tg, P>;
+  const size_t smem = smem_fwd_o<P>();
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v,
+                                                 (const Tg*)g, cu, off, N, H, K, V, scale, states,
+                                                 (T*)o);
+  SSLA_CHECK_LAUNCH("chunk_gla fwd_o");
+  return SSLA_OK;
+}
+
+template <typename T, typename Tg, int P>
+int run_bwd(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
+            const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+            const float* states, const float* dstates, const void* dout, void* dq, void* dk,
+            void* dv, float* dg, cudaStream_t s) {
+  auto kern = bwd_kernel<T, Tg, P>;
+  const size_t smem = smem_bwd<P>();
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K, V, scale, states,
+      dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg);
+  SSLA_CHECK_LAUNCH("chunk_gla bwd");
+  return SSLA_OK;
+}
+
+inline int pad_of(int64_t K, int64_t V) {
+  const int64_t m = K > V ? K : V;
+  return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 0));
+}
+
+#define SSLA_DISPATCH_PAD(P_, ...)                       \
+  [&]() -> int {                                         \
+    switch (P_) {                                        \
+      case 16: { constexpr int P = 16; return __VA_ARGS__(); } \
+      case 32: { constexpr int P = 32; return __VA_ARGS__(); } \
+      default: { constexpr int P = 64; return __VA_ARGS__(); } \
+    }                                                    \
+  }()
+
+// dtype_g is either the input dtype or fp32.
+#define SSLA_DISPATCH_QG(dtype, dtype_g, T, Tg, ...)                                   \
+  SSLA_DISPATCH_DTYPE(dtype, T, [&] {                                                  \
+    if (dtype_g == SSLA_F32) { using Tg = float; return __VA_ARGS__(); }               \
+    using Tg = T;                                                                      \
+    return __VA_ARGS__();                                                              \
+  })
+
+}  // namespace
+
+int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t* chunk_off, cudaStream_t s) {
+  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, chunk_off);
+  SSLA_CHECK_LAUNCH("chunk_gla chunk_offsets");
+  return SSLA_OK;
+}
+
+int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_off, int64_t N,
+                      int64_t H, int64_t K, int64_t V, const float* init, float* per_chunk,
+                      float* final_state, bool reverse, cudaStream_t s) {
+  const int64_t threads = N * H * K * V;
+  if (threads == 0) return SSLA_OK;
+  state_scan_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(dS, decay, chunk_off, N, (int)H, (int)K,
+                                                           (int)V, init, per_chunk, final_state,
+                                                           reverse);
+  SSLA_CHECK_LAUNCH("chunk_gla state_scan");
+  return SSLA_OK;
+}
+
+}  // namespace chunk
+}  // namespace ssla
+
+using namespace ssla;
+using namespace ssla::chunk;
+
+static int check_common(const char* name, int dtype, int dtype_g, int64_t N, int64_t T, int64_t H,
+                        int64_t K, int64_t V) {
+  SSLA_CHECK_ARG(dtype_ok(dtype), "%s: bad dtype", name);
+  SSLA_CHECK_ARG(dtype_g == dtype || dtype_g == SSLA_F32, "%s: g must have q's dtype or fp32", name);
+  SSLA_CHECK_ARG(N >= 0 && T >= 0 && H >= 0, "%s: negative size", name);
+  SSLA_CHECK_ARG((K >= 1 && V >= 1 && K <= 64 && V <= 64) || tc_supported(dtype, dtype_g, K, V),
+                 "%s: K=%lld V=%lld not supported (1 <= K, V <= 64 in this build)", name,
+                 (long long)K, (long long)V);
+  return SSLA_OK;
+}
+
+extern "C" int64_t ssla_chunk_gla_max_chunks(int64_t n_seqs, int64_t T) {
+  return max_chunks(n_seqs, T);
+}
+
+extern "C" size_t ssla_chunk_gla_workspace_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K,
+                                                 int64_t V) {
+  return workspace_bytes(n_seqs, T, H, K, V);
+}
+
+extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, const void* g,
+                                  int dtype, int dtype_g, const int64_t* cu_seqlens,
+                                  int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
+                                  float scale, const float* h0, void* o, float* ht,
+                                  float* states, void* workspace, size_t workspace_bytes_,
+                                  ssla_stream_t stream) {
+  int rc = check_common("ssla_chunk_gla_fwd", dtype, dtype_g, n_seqs, T, H, K, V);
+  if (rc) return rc;
+  if (n_seqs == 0 || H == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(cu_seqlens && states && workspace, "ssla_chunk_gla_fwd: null pointer");
+  SSLA_CHECK_ARG(T == 0 || (q && k && v && g && o), "ssla_chunk_gla_fwd: null pointer");
+  if (workspace_bytes_ < workspace_bytes(n_seqs, T, H, K, V)) {
+    set_error("ssla_chunk_gla_fwd: workspace of %zu bytes < %zu needed", workspace_bytes_,
+              workspace_bytes(n_seqs, T, H, K, V));
+    return SSLA_ERR_WORKSPACE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  Workspace w = carve(workspace, n_seqs, T, H, K, V);
+  const int64_t MC = max_chunks(n_seqs, T);
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, w.chunk_off, s))) return rc;
+  const bool tc = tc_supported(dtype, dtype_g, K, V);
+  if (MC > 0) {
+    if (tc) {
+      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale,
+                          w.dS, w.decay, s);
+    } else {
+      rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+        return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+          return run_local<T_, Tg, P>(0, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H,
+                                      (int)K, (int)V, scale, w.dS, w.decay, s);
+        });
+      });
+    }
+    if (rc) return rc;
+  }
+  if ((rc = launch_state_scan(w.dS, w.decay, w.chunk_off, n_seqs, H, K, V, h0, states, ht, false, s)))
+    return rc;
+  if (MC == 0) return SSLA_OK;
+  if (tc)
+    return tc_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale,
+                    states, o, s);
+  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+      return run_fwd_o<T_, Tg, P>(q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H, (int)K,
+                                  (int)V, scale, states, o, s);
+    });
+  });
+}
+
+extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* g,
+                                  int dtype, int dtype_g, const int64_t* cu_seqlens,
+                                  int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
+                                  float scale, const float* states, const void* dout,
+                                  const float* dht, void* dq, void* dk, void* dv, float* dg,
+                                  float* dh0, void* workspace, size_t workspace_bytes_,
+                                  ssla_stream_t stream) {
+  int rc = check_common("ssla_chunk_gla_bwd", dtype, dtype_g, n_seqs, T, H, K, V);
+  if (rc) return rc;
+  if (n_seqs == 0 || H == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(cu_seqlens && states && workspace, "ssla_chunk_gla_bwd: null pointer");
+  SSLA_CHECK_ARG(T == 0 || (q && k && v && g && dout && dq && dk && dv && dg),
+                 "ssla_chunk_gla_bwd: null pointer");
+  if (workspace_bytes_ < workspace_bytes(n_seqs, T, H, K, V)) {
+    set_error("ssla_chunk_gla_bwd: workspace of %zu bytes < %zu needed", workspace_bytes_,
+              workspace_bytes(n_seqs, T, H, K, V));
+    return SSLA_ERR_WORKSPACE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  Workspace w = carve(workspace, n_seqs, T, H, K, V);
+  const int64_t MC = max_chunks(n_seqs, T);
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, w.chunk_off, s))) return rc;
+  const bool tc = tc_supported(dtype, dtype_g, K, V);
+  if (MC > 0) {
+    if (tc) {
+      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, cu_seqlens, w.chunk_off, n_seqs, MC, H,
+                          scale, w.dS, w.decay, s);
+    } else {
+      rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+        return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+          return run_local<T_, Tg, P>(1, q, dout, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H,
+                                      (int)K, (int)V, scale, w.dS, w.decay, s);
+        });
+      });
+    }
+    if (rc) return rc;
+  }
+  if ((rc = launch_state_scan(w.dS, w.decay, w.chunk_off, n_seqs, H, K, V, dht, w.dstates, dh0, true,
+                              s)))
+    return rc;
+  if (MC == 0) return SSLA_OK;
+  if (tc)
+    return tc_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale, states,
+                  w.dstates, dout, dq, dk, dv, dg, s);
+  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+      return run_bwd<T_, Tg, P>(q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H, (int)K,
+                                (int)V, scale, states, w.dstates, dout, dq, dk, dv, dg, s);
+    });
+  });
+}

@@ -1,0 +1,346 @@
+// Deterministic segment reductions, row gathers and index_add for sparse pooling and the
+// sparse-token routing (layers/sparse_pooling.py:14-51 with torch_scatter.scatter_max /
+// scatter_mean; utils/async_utils.py:243-264 index_add_).
+//
+// The reference reduces with torch_scatter / index_add_, whose GPU kernels use atomics and
+// so sum in an unspecified order.  Here every reduction walks the rows of a segment in
+// ascending row order with an fp32 accumulator, which reproduces the CPU PyTorch /
+// torch_scatter result bit for bit for fp32 data:
+//   * sorted indices (the pooling case: unique_consecutive inverse ids are non-decreasing):
+//     segment boundaries come from one pass over the index, no sort at all;
+//   * arbitrary indices: a counting sort builds a CSR (count -> exclusive scan -> scatter),
+//     and each segment's row list is then put in ascending order by a warp-level rank sort,
+//     so the result never depends on atomic arrival order.
+// Rows are moved 16 B (fp32) or 8 B (16-bit) per thread; consecutive threads cover
+// consecutive channel vectors of the same row.
+#include <float.h>
+
+#include "common.cuh"
+#include "vec.cuh"
+
+namespace ssla {
+namespace {
+
+inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// off[s] = first row r with index[r] >= s, for s in [0, S]; index non-decreasing.
+__global__ void offsets_sorted_kernel(const int64_t* __restrict__ index, int64_t R, int64_t S,
+                                      int64_t* __restrict__ off) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r > R) return;
+  int64_t prev = r == 0 ? -1 : index[r - 1];
+  int64_t cur = r == R ? S : index[r];
+  if (prev < -1) prev = -1;
+  if (cur > S) cur = S;
+  for (int64_t s = prev + 1; s <= cur; ++s) off[s] = r;
+}
+
+__global__ void count_kernel(const int64_t* __restrict__ index, int64_t R, int64_t S,
+                             int* __restrict__ counts) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  const int64_t s = index[r];
+  if (s >= 0 && s < S) atomicAdd(&counts[s], 1);
+}
+
+// Block-wise exclusive scan of int counts into int64 offsets (+ per-block totals).
+__global__ void __launch_bounds__(1024) scan_blocks_kernel(const int* __restrict__ counts,
+                                                           int64_t S, int64_t* __restrict__ off,
+                                                           int64_t* __restrict__ block_sums) {
+  __shared__ int64_t ws[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t i = (int64_t)blockIdx.x * 1024 + tid;
+  const int64_t x = i < S ? counts[i] : 0;
+  int64_t incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) ws[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = ws[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    ws[lane] = w;
+  }
+  __syncthreads();
+  const int64_t before = warp > 0 ? ws[warp - 1] : 0;
+  if (i < S) off[i] = before + incl - x;
+  if (tid == 1023) block_sums[blockIdx.x] = before + incl;
+}
+
+// Sequential exclusive scan of the (few) block totals, then off[S] = number of rows.
+__global__ void scan_totals_kernel(int64_t* __restrict__ block_sums, int64_t nb, int64_t S,
+                                   int64_t* __restrict__ off) {
+  if (threadIdx.x != 0) return;
+  int64_t acc = 0;
+  for (int64_t b = 0; b < nb; ++b) {
+    const int64_t x = block_sums[b];
+    block_sums[b] = acc;
+    acc += x;
+  }
+  off[S] = acc;
+}
+
+__global__ void add_block_base_kernel(int64_t* __restrict__ off, int64_t S,
+                                      const int64_t* __restrict__ block_sums,
+                                      int* __restrict__ counts) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= S) return;
+  off[i] += block_sums[i / 1024];
+  counts[i] = 0;  // reused as the fill cursor
+}
+
+__global__ void fill_kernel(const int64_t* __restrict__ index, int64_t R, int64_t S,
+                            const int64_t* __restrict__ off, int* __restrict__ cursor,
+                            int64_t* __restrict__ tmp) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  const int64_t s = index[r];
+  if (s < 0 || s >= S) return;
+  const int64_t pos = off[s] + atomicAdd(&cursor[s], 1);
+  tmp[pos] = r;
+}
+
+// One warp per segment: rows[off[s] + rank(x)] = x, rank = #{y in segment : y < x}.
+__global__ void rank_sort_kernel(const int64_t* __restrict__ off, int64_t S,
+                                 const int64_t* __restrict__ tmp, int64_t* __restrict__ rows) {
+  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= S) return;
+  const int64_t b = off[s], e = off[s + 1], n = e - b;
+  if (n <= 32) {
+    const int64_t x = lane < n ? tmp[b + lane] : INT64_MAX;
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const int64_t y = __shfl_sync(0xffffffffu, x, j);
+      rank += (y < x);
+    }
+    if (lane < n) rows[b + rank] = x;
+  } else {
+    for (int64_t i = lane; i < n; i += 32) {
+      const int64_t x = tmp[b + i];
+      int64_t rank = 0;
+      for (int64_t j = 0; j < n; ++j) rank += (tmp[b + j] < x);
+      rows[b + rank] = x;
+    }
+  }
+}
+
+template <typename T> __device__ __forceinline__ float lowest_of();
+template <> __device__ __forceinline__ float lowest_of<float>() { return -FLT_MAX; }
+template <> __device__ __forceinline__ float lowest_of<__nv_bfloat16>() { return -3.38953139e38f; }
+template <> __device__ __forceinline__ float lowest_of<__half>() { return -65504.f; }
+
+// Thread per (segment, VEC channels).  op: 0 sum, 1 mean, 2 max.
+template <typename T, int VEC, int OP>
+__global__ void __launch_bounds__(256) reduce_kernel(const T* __restrict__ src,
+                                                     const int64_t* __restrict__ off,
+                                                     const int64_t* __restrict__ rows, int64_t R,
+                                                     int64_t S, int64_t C, T* __restrict__ out,
+                                                     int64_t* __restrict__ arg) {
+  const int64_t CV = C / VEC;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= S * CV) return;
+  const int64_t s = idx / CV;
+  const int64_t c = (idx - s * CV) * VEC;
+  const int64_t b = off[s], e = off[s + 1];
+  float acc[VEC];
+  int64_t am[VEC];
+  const float lo = lowest_of<T>();
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    acc[i] = OP == 2 ? lo : 0.f;
+    am[i] = R;
+  }
+  for (int64_t p = b; p < e; ++p) {
+    const int64_t r = rows ? rows[p] : p;
+    float x[VEC];
+    Vec<T, VEC>::load(src + r * C + c, x);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      if (OP == 2) {
+        if (x[i] > acc[i]) { acc[i] = x[i]; am[i] = r; }
+      } else {
+        acc[i] = __fadd_rn(acc[i], x[i]);
+      }
+    }
+  }
+  if (OP == 1) {
+    const float cnt = (float)(e - b > 0 ? e - b : 1);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = __fdiv_rn(acc[i], cnt);
+  }
+  if (OP == 2) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i)
+      if (acc[i] == lo) acc[i] = 0.f;
+    if (arg) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) arg[s * C + c + i] = am[i];
+    }
+  }
+  Vec<T, VEC>::store(out + s * C + c, acc);
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) gather_kernel(const T* __restrict__ src,
+                                                     const int64_t* __restrict__ index, int64_t R,
+                                                     int64_t C, T* __restrict__ out) {
+  const int64_t CV = C / VEC;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= R * CV) return;
+  const int64_t r = idx / CV;
+  const int64_t c = (idx - r * CV) * VEC;
+  float x[VEC];
+  Vec<T, VEC>::load(src + index[r] * C + c, x);
+  Vec<T, VEC>::store(out + r * C + c, x);
+}
+
+template <typename T>
+int run_reduce(const void* src, const int64_t* off, const int64_t* rows, int64_t R, int64_t S,
+               int64_t C, int op, void* out, int64_t* arg, cudaStream_t s) {
+  const bool v4 = C % 4 == 0 && aligned_to(src, 4 * sizeof(T)) && aligned_to(out, 4 * sizeof(T));
+  const int64_t threads = S * (v4 ? C / 4 : C);
+  if (threads == 0) return SSLA_OK;
+  const int grid = ceil_div(threads, 256);
+#define SSLA_RED(VEC, OP) \
+  reduce_kernel<T, VEC, OP><<<grid, 256, 0, s>>>((const T*)src, off, rows, R, S, C, (T*)out, arg)
+  if (v4) {
+    if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
+  } else {
+    if (op == 0) SSLA_RED(1, 0); else if (op == 1) SSLA_RED(1, 1); else SSLA_RED(1, 2);
+  }
+#undef SSLA_RED
+  SSLA_CHECK_LAUNCH("ssla_segment_reduce");
+  return SSLA_OK;
+}
+
+int build_csr(const int64_t* index, int64_t R, int64_t S, int64_t* off, int64_t* rows, void* ws,
+              cudaStream_t s) {
+  char* p = (char*)ws;
+  int* counts = (int*)p;
+  p += a256(4 * (size_t)S);
+  const int64_t nb = (S + 1023) / 1024;
+  int64_t* block_sums = (int64_t*)p;
+  p += a256(8 * (size_t)(nb + 1));
+  int64_t* tmp = (int64_t*)p;
+  if (S > 0) {
+    if (cudaMemsetAsync(counts, 0, 4 * (size_t)S, s) != cudaSuccess) {
+      set_error("ssla_segment_csr: memset failed");
+      return SSLA_ERR_CUDA;
+    }
+    if (R > 0) count_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, counts);
+    scan_blocks_kernel<<<(unsigned)nb, 1024, 0, s>>>(counts, S, off, block_sums);
+  }
+  scan_totals_kernel<<<1, 32, 0, s>>>(block_sums, nb, S, off);
+  if (S > 0) {
+    add_block_base_kernel<<<ceil_div(S, 256), 256, 0, s>>>(off, S, block_sums, counts);
+    if (R > 0) {
+      fill_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, off, counts, tmp);
+      rank_sort_kernel<<<ceil_div(S * 32, 256), 256, 0, s>>>(off, S, tmp, rows);
+    }
+  }
+  SSLA_CHECK_LAUNCH("ssla_segment_csr");
+  return SSLA_OK;
+}
+
+size_t csr_ws_bytes(int64_t R, int64_t S) {
+  const int64_t nb = (S + 1023) / 1024;
+  return a256(4 * (size_t)S) + a256(8 * (size_t)(nb + 1)) + a256(8 * (size_t)R);
+}
+
+}  // namespace
+}  // namespace ssla
+
+using namespace ssla;
+
+extern "C" int ssla_segment_offsets_sorted(const int64_t* index, int64_t R, int64_t S,
+                                           int64_t* seg_offsets, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(R >= 0 && S >= 0, "ssla_segment_offsets_sorted: negative size");
+  SSLA_CHECK_ARG(seg_offsets && (R == 0 || index), "ssla_segment_offsets_sorted: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  offsets_sorted_kernel<<<ceil_div(R + 1, 256), 256, 0, s>>>(index, R, S, seg_offsets);
+  SSLA_CHECK_LAUNCH("ssla_segment_offsets_sorted");
+  return SSLA_OK;
+}
+
+extern "C" size_t ssla_segment_csr_workspace_bytes(int64_t R, int64_t S) { return csr_ws_bytes(R, S); }
+
+extern "C" int ssla_segment_csr(const int64_t* index, int64_t R, int64_t S, int64_t* seg_offsets,
+                                int64_t* rows, void* workspace, size_t workspace_bytes,
+                                ssla_stream_t stream) {
+  SSLA_CHECK_ARG(R >= 0 && S >= 0, "ssla_segment_csr: negative size");
+  SSLA_CHECK_ARG(seg_offsets && workspace && (R == 0 || (index && rows)),
+                 "ssla_segment_csr: null pointer");
+  if (workspace_bytes < csr_ws_bytes(R, S)) {
+    set_error("ssla_segment_csr: workspace of %zu bytes < %zu needed", workspace_bytes,
+              csr_ws_bytes(R, S));
+    return SSLA_ERR_WORKSPACE;
+  }
+  return build_csr(index, R, S, seg_offsets, rows, workspace, (cudaStream_t)stream);
+}
+
+extern "C" int ssla_segment_reduce(const void* src, int dtype, const int64_t* seg_offsets,
+                                   const int64_t* rows, int64_t R, int64_t S, int64_t C, int op,
+                                   void* out, int64_t* arg, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(dtype_ok(dtype), "ssla_segment_reduce: bad dtype");
+  SSLA_CHECK_ARG(op >= 0 && op <= 2, "ssla_segment_reduce: bad op %d", op);
+  SSLA_CHECK_ARG(R >= 0 && S >= 0 && C >= 0, "ssla_segment_reduce: negative size");
+  if (S == 0 || C == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(seg_offsets && out && (R == 0 || src), "ssla_segment_reduce: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  return SSLA_DISPATCH_DTYPE(dtype, T,
+                             [&] { return run_reduce<T>(src, seg_offsets, rows, R, S, C, op, out, arg, s); });
+}
+
+extern "C" int ssla_gather_rows(const void* src, int dtype, const int64_t* index, int64_t R,
+                                int64_t C, void* out, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(dtype_ok(dtype), "ssla_gather_rows: bad dtype");
+  SSLA_CHECK_ARG(R >= 0 && C >= 0, "ssla_gather_rows: negative size");
+  if (R == 0 || C == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(src && index && out, "ssla_gather_rows: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  return SSLA_DISPATCH_DTYPE(dtype, T, [&] {
+    const bool v4 = C % 4 == 0 && aligned_to(src, 4 * sizeof(T)) && aligned_to(out, 4 * sizeof(T));
+    const int64_t threads = R * (v4 ? C / 4 : C);
+    if (v4)
+      gather_kernel<T, 4><<<ceil_div(threads, 256), 256, 0, s>>>((const T*)src, index, R, C, (T*)out);
+    else
+      gather_kernel<T, 1><<<ceil_div(threads, 256), 256, 0, s>>>((const T*)src, index, R, C, (T*)out);
+    SSLA_CHECK_LAUNCH("ssla_gather_rows");
+    return SSLA_OK;
+  });
+}
+
+extern "C" size_t ssla_index_add_rows_workspace_bytes(int64_t P, int64_t D) {
+  return a256(8 * (size_t)(D + 1)) + a256(8 * (size_t)P) + csr_ws_bytes(P, D);
+}
+
+extern "C" int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_t P,
+                                   int64_t D, int64_t C, void* out, void* workspace,
+                                   size_t workspace_bytes, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(dtype_ok(dtype), "ssla_index_add_rows: bad dtype");
+  SSLA_CHECK_ARG(P >= 0 && D >= 0 && C >= 0, "ssla_index_add_rows: negative size");
+  if (D == 0 || C == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(out && workspace && (P == 0 || (src && index)), "ssla_index_add_rows: null pointer");
+  const size_t need = ssla_index_add_rows_workspace_bytes(P, D);
+  if (workspace_bytes < need) {
+    set_error("ssla_index_add_rows: workspace of %zu bytes < %zu needed", workspace_bytes, need);
+    return SSLA_ERR_WORKSPACE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  char* p = (char*)workspace;
+  int64_t* off = (int64_t*)p;
+  p += a256(8 * (size_t)(D + 1));
+  int64_t* rows = (int64_t*)p;
+  p += a256(8 * (size_t)P);
+  int rc = build_csr(index, P, D, off, rows, p, s);
+  if (rc) return rc;
+  return SSLA_DISPATCH_DTYPE(dtype, T, [&] { return run_reduce<T>(src, off, rows, P, D, C, 0, out, nullptr, s); });
+}
