@@ -1,0 +1,97 @@
+"""Deterministic segment reductions, row gathers and index_add on the ssla_b200 C ABI.
+
+Replaces the ``torch_scatter.scatter_max`` / ``scatter_mean`` calls of sparse pooling
+(layers/sparse_pooling.py:5,33) and the ``index_add_`` gather-back of the MoS routing
+(utils/async_utils.py:243-264).  Sums accumulate in fp32 in ascending row order, so fp32
+results equal the CPU PyTorch / torch_scatter results bit for bit; max returns the first
+maximal row as argmax (the number of rows for empty segments) and 0 for empty segments.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _lib
+
+SUM, MEAN, MAX = 0, 1, 2
+
+
+def _i64(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.int64).contiguous()
+
+
+def segment_offsets_sorted(index: torch.Tensor, num_segments: int) -> torch.Tensor:
+    """``[S+1]`` offsets of a non-decreasing row->segment index."""
+    _lib.require_cuda(index, what="segment_offsets_sorted")
+    index = _i64(index)
+    off = torch.empty(num_segments + 1, device=index.device, dtype=torch.int64)
+    _lib.check(
+        _lib.load().ssla_segment_offsets_sorted(index.data_ptr(), index.numel(), num_segments,
+                                                off.data_ptr(), _lib.stream_of(index)),
+        "segment_offsets_sorted",
+    )
+    return off
+
+
+def segment_csr(index: torch.Tensor, num_segments: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(offsets [S+1], rows [R]) for an arbitrary index; rows ascending within each segment."""
+    _lib.require_cuda(index, what="segment_csr")
+    index = _i64(index)
+    R = index.numel()
+    L = _lib.load()
+    off = torch.empty(num_segments + 1, device=index.device, dtype=torch.int64)
+    rows = torch.empty(max(R, 1), device=index.device, dtype=torch.int64)
+    nb = L.ssla_segment_csr_workspace_bytes(R, num_segments)
+    ws = torch.empty(max(nb, 1), device=index.device, dtype=torch.uint8)
+    _lib.check(L.ssla_segment_csr(index.data_ptr(), R, num_segments, off.data_ptr(), rows.data_ptr(),
+                                  ws.data_ptr(), nb, _lib.stream_of(index)), "segment_csr")
+    return off, rows
+
+
+def segment_reduce(src: torch.Tensor, offsets: torch.Tensor, rows: Optional[torch.Tensor], op: int,
+                   want_arg: bool = False):
+    """Reduce rows of ``src [R, C]`` per segment described by ``offsets`` (and ``rows``)."""
+    _lib.require_cuda(src, offsets, what="segment_reduce")
+    src = src.contiguous()
+    if src.dim() != 2:
+        raise ValueError(f"segment_reduce expects src [R, C], got {tuple(src.shape)}")
+    R, C = src.shape
+    S = offsets.numel() - 1
+    out = torch.empty((S, C), device=src.device, dtype=src.dtype)
+    arg = torch.empty((S, C), device=src.device, dtype=torch.int64) if (op == MAX and want_arg) else None
+    _lib.check(
+        _lib.load().ssla_segment_reduce(src.data_ptr(), _lib.dtype_code(src), offsets.data_ptr(),
+                                        _lib.ptr(rows), R, S, C, op, out.data_ptr(), _lib.ptr(arg),
+                                        _lib.stream_of(src)),
+        "segment_reduce",
+    )
+    return out, arg
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """``src[index]`` for 2-D src (row gather)."""
+    _lib.require_cuda(src, index, what="gather_rows")
+    src = src.contiguous()
+    index = _i64(index)
+    out = torch.empty((index.numel(), src.shape[1]), device=src.device, dtype=src.dtype)
+    _lib.check(_lib.load().ssla_gather_rows(src.data_ptr(), _lib.dtype_code(src), index.data_ptr(),
+                                            index.numel(), src.shape[1], out.data_ptr(),
+                                            _lib.stream_of(src)), "gather_rows")
+    return out
+
+
+def index_add_rows(src: torch.Tensor, index: torch.Tensor, num_rows: int) -> torch.Tensor:
+    """``zeros(num_rows, C).index_add_(0, index, src)`` with a fixed (ascending-row) sum order."""
+    _lib.require_cuda(src, index, what="index_add_rows")
+    src = src.contiguous()
+    index = _i64(index)
+    P, C = src.shape
+    L = _lib.load()
+    out = torch.empty((num_rows, C), device=src.device, dtype=src.dtype)
+    nb = L.ssla_index_add_rows_workspace_bytes(P, num_rows)
+    ws = torch.empty(max(nb, 1), device=src.device, dtype=torch.uint8)
+    _lib.check(L.ssla_index_add_rows(src.data_ptr(), _lib.dtype_code(src), index.data_ptr(), P, num_rows,
+                                     C, out.data_ptr(), ws.data_ptr(), nb, _lib.stream_of(src)),
+               "index_add_rows")
+    return out
