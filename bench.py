@@ -1,0 +1,323 @@
+"""Headline benchmark: chunk_gla forward+backward tokens/s.
+
+Workload per rank and step: B=8 sequences x T=2048 tokens, H=4, K=V=64, bf16 q/k/v/g,
+fp32 initial state, upstream gradients do (bf16) and dht (fp32); one step = the full
+chunk_gla forward plus backward (o, final state, dq, dk, dv, dg, dh0).  Synthetic seeded
+inputs with the config's distributions (q,k,v ~ N(0,1), g = logsigmoid(N(0,1))/16,
+h0 ~ N(0, 0.1)).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+* ``value``: device-timed tokens/s with inputs resident in HBM, through the C ABI with
+  preallocated outputs/workspace.  L2 (126 MB) is flushed by a 256 MB write before every
+  timed step (the 33.5 MB of inputs fit in L2); each step is timed with CUDA events on the
+  launching stream and the per-step times are summed.
+* ``e2e``: the same metric through the public API (``chunk_gla`` + autograd backward) with
+  inputs copied host->device from pinned memory and all results copied back every step.
+* Multi-GPU (torchrun): sequences are independent, so every rank runs its own B=8 shard
+  (weak scaling, no data-path collective); time = max over ranks.
+* ``--impl reference``: the reference's CPU path for this operator (the naive PyTorch
+  recurrence + autograd of ops/gla/naive.py:50-111, restated in ``oracle``) on the host
+  cores, on a bounded sample of the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, H, T, K, V = 8, 4, 2048, 64, 64
+TOKENS = B * T
+# algorithmic bytes per fwd+bwd step: fwd reads q,k,v,g (bf16) + h0 (fp32), writes o (bf16)
+# + ht (fp32); bwd reads q,k,v,g,do (bf16) + h0,dht (fp32), writes dq,dk,dv (bf16), dg (fp32),
+# dh0 (fp32)
+_E = TOKENS * H * K
+_S = B * H * K * V * 4
+FWD_BYTES = 4 * _E * 2 + _S + _E * 2 + _S
+BWD_BYTES = 5 * _E * 2 + 2 * _S + 3 * _E * 2 + _E * 4 + _S
+ALG_BYTES = FWD_BYTES + BWD_BYTES
+ALG_FLOPS = 12 * 2 * K * V * TOKENS * H
+METRIC = "chunk-GLA fwd+bwd tokens/s"
+LAUNCHES_PER_STEP = 8  # fwd: chunk offsets, local state, state scan, output; bwd: the same four
+
+
+def make_inputs(seed: int, device="cpu"):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, T, K, generator=gen)
+    k = torch.randn(B, H, T, K, generator=gen)
+    v = torch.randn(B, H, T, V, generator=gen)
+    g = F.logsigmoid(torch.randn(B, H, T, K, generator=gen)) / 16
+    cv = lambda x: x.permute(0, 2, 1, 3).reshape(B * T, H, -1).to(torch.bfloat16).contiguous()
+    q, k, v, g = map(cv, (q, k, v, g))
+    h0 = torch.randn(B, H, K, V, generator=gen) * 0.1
+    do = torch.randn(B * T, H, V, generator=gen).to(torch.bfloat16)
+    dht = torch.randn(B, H, K, V, generator=gen)
+    cu = torch.arange(B + 1) * T
+    return dict(q=q, k=k, v=v, g=g, h0=h0, do=do, dht=dht, cu=cu)
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"ssla_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()]
+        except OSError:
+            return None
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 6]
+        if not rows:
+            return None
+        sm = sorted(float(r[0]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, x in zip(names, r[2:6]) if x.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][1]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline_sample(threads: int, seq_len: int = 2048, n_seqs: int = 4):
+    """Reference CPU path (naive recurrence + autograd) on one bounded sample: ``n_seqs``
+    sequences of ``seq_len`` tokens with the workload's H, K, V.  Returns tokens/s."""
+    from oracle.gla import naive_gla_recurrent
+
+    torch.set_num_threads(threads)
+    d = make_inputs(1)
+    rows = []
+    for n in range(n_seqs):
+        rows += list(range(n * T, n * T + seq_len))
+    sl = torch.tensor(rows)
+    leaves = [d[n][sl].float().requires_grad_() for n in ("q", "k", "v", "g")]
+    h0 = d["h0"][:n_seqs].clone().requires_grad_()
+    cu = torch.arange(n_seqs + 1) * seq_len
+    t0 = time.perf_counter()
+    o, ht = naive_gla_recurrent(*leaves, cu, initial_state=h0, output_final_state=True)
+    torch.autograd.backward([o, ht], [d["do"][sl].float(), d["dht"][:n_seqs]])
+    dt = time.perf_counter() - t0
+    return n_seqs * seq_len / dt, (f"{n_seqs} sequences x {seq_len} tokens, H={H}, K=V={K}, "
+                                   "fp32 naive recurrence fwd+bwd (bf16 inputs upcast)")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    times = []
+    n_tok = 512
+    for i in range(args.warmup + args.steps):
+        tps, sample = cpu_baseline_sample(threads, seq_len=n_tok, n_seqs=1)
+        if i >= args.warmup:
+            times.append(n_tok / tps)
+    v = n_tok * len(times) / sum(times)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "chunk_gla fwd+bwd, B=8 H=4 T=2048 K=V=64 (BASELINE config 2)",
+                       "sample_per_step": sample},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+
+    from ssla_b200 import _lib
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    L = _lib.load()
+    host = make_inputs(1000 + rank)
+    d = {n: t.to(dev) for n, t in host.items()}
+    N = B
+    MC = L.ssla_chunk_gla_max_chunks(N, B * T)
+    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, B * T, H, K, V)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    states = torch.empty(MC, H, K, V, device=dev)
+    o = torch.empty_like(d["v"])
+    ht = torch.empty(B, H, K, V, device=dev)
+    dq, dk, dv = torch.empty_like(d["q"]), torch.empty_like(d["k"]), torch.empty_like(d["v"])
+    dg = torch.empty(B * T, H, K, device=dev)
+    dh0 = torch.empty(B, H, K, V, device=dev)
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    scale = K ** -0.5
+    BF = _lib.BF16
+
+    def step():
+        _lib.check(L.ssla_chunk_gla_fwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
+                                        d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(), N, B * T, H, K, V,
+                                        scale, d["h0"].data_ptr(), o.data_ptr(), ht.data_ptr(),
+                                        states.data_ptr(), ws.data_ptr(), ws_bytes, sp), "fwd")
+        _lib.check(L.ssla_chunk_gla_bwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
+                                        d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(), N, B * T, H, K, V,
+                                        scale, states.data_ptr(), d["do"].data_ptr(), d["dht"].data_ptr(),
+                                        dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
+                                        dh0.data_ptr(), ws.data_ptr(), ws_bytes, sp), "bwd")
+
+    def timed(fn, n):
+        tot = 0.0
+        for _ in range(n):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / 1e3
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    # ---- device-resident timing through the C ABI
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    with Clocks(local) as clk:
+        secs = timed(step, args.steps)
+    barrier()
+    secs = max_over_ranks(secs)
+    ms = 1e3 * secs / args.steps
+    value = world * TOKENS * args.steps / secs
+
+    # ---- forward and backward separately (roofline of each half)
+    fwd_only = lambda: _lib.check(L.ssla_chunk_gla_fwd(
+        d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(),
+        N, B * T, H, K, V, scale, d["h0"].data_ptr(), o.data_ptr(), ht.data_ptr(), states.data_ptr(),
+        ws.data_ptr(), ws_bytes, sp), "fwd")
+    fwd_s = max_over_ranks(timed(fwd_only, args.steps)) / args.steps
+    bwd_s = secs / args.steps - fwd_s
+
+    # ---- end to end through the public API, host buffers in pinned memory
+    pin = {n: host[n].pin_memory() for n in ("q", "k", "v", "g", "h0", "do", "dht")}
+    out_host = {n: torch.empty(s, dtype=dt).pin_memory() for n, s, dt in (
+        ("o", host["v"].shape, torch.bfloat16), ("dq", host["q"].shape, torch.bfloat16),
+        ("dk", host["k"].shape, torch.bfloat16), ("dv", host["v"].shape, torch.bfloat16),
+        ("dg", host["g"].shape, torch.bfloat16), ("ht", (B, H, K, V), torch.float32),
+        ("dh0", (B, H, K, V), torch.float32))}
+    h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    d2h = sum(t.numel() * t.element_size() for t in out_host.values())
+    cu_dev = d["cu"]
+
+    def e2e_step():
+        x = {n: t.to(dev, non_blocking=True) for n, t in pin.items()}
+        leaves = [x[n].requires_grad_() for n in ("q", "k", "v", "g")]
+        h0 = x["h0"].requires_grad_()
+        oo, hh = chunk_gla(*leaves, cu_dev, initial_state=h0, output_final_state=True)
+        torch.autograd.backward([oo, hh], [x["do"], x["dht"]])
+        for n, t in (("o", oo), ("ht", hh), ("dq", leaves[0].grad), ("dk", leaves[1].grad),
+                     ("dv", leaves[2].grad), ("dg", leaves[3].grad), ("dh0", h0.grad)):
+            out_host[n].copy_(t.detach(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e2e_secs = max_over_ranks(timed(e2e_step, args.steps))
+    e2e_value = world * TOKENS * args.steps / e2e_secs
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    hbm, which = peaks()
+    fwd_gbs = FWD_BYTES / fwd_s / 1e9
+    step_gbs = ALG_BYTES / (secs / args.steps) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        threads = os.cpu_count() or 1
+        tps, sample = cpu_baseline_sample(threads)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "chunk_gla fwd+bwd, B=8 H=4 T=2048 K=V=64 bf16, h0+dht (BASELINE config 2)",
+                   "per_rank_tokens": TOKENS, "l2": "flushed (256 MB write) before every timed step",
+                   "parallelism": f"independent sequence shards x{world}"},
+        "roofline": {"bound": "hbm", "scope": "whole fwd+bwd step (all launches)",
+                     "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
+                     "peak_source": which, "traffic": None, "alg_bytes_per_step": ALG_BYTES,
+                     "forward": {"achieved": fwd_gbs, "frac": fwd_gbs / hbm, "ms": fwd_s * 1e3},
+                     "backward_ms": bwd_s * 1e3, "tensor_flops_per_step": ALG_FLOPS},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+"""GPU parity of the GLA kernels (chunk_gla, fused_recurrent_gla, chunk_gla_scalar) against the
+CPU oracle.  Tolerances (RMS relative error, utils/ela_utils.py:63-85 style): 1e-5 for fp32
+inputs, 2e-2 for bf16 inputs, as the north-star bar states."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import GOLDEN, rel_err
+from oracle import gla as og
+
+pytestmark = pytest.mark.gpu
+FP32_TOL, BF16_TOL = 1e-5, 2e-2
+
+
+def make(T, H, K, V, cu, dtype, seed=0, h0=True, gscale=16.0):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(T, H, K, generator=gen)
+    k = torch.randn(T, H, K, generator=gen) * K ** -0.5
+    v = torch.randn(T, H, V, generator=gen)
+    g = F.logsigmoid(torch.randn(T, H, K, generator=gen)) / gscale
+    N = len(cu) - 1
+    hz = torch.randn(N, H, K, V, generator=gen) * 0.1 if h0 else None
+    do = torch.randn(T, H, V, generator=gen)
+    dht = torch.randn(N, H, K, V, generator=gen)
+    q, k, v, g, do = (x.to(dtype) for x in (q, k, v, g, do))
+    return q, k, v, g, hz, do, dht, torch.tensor(cu)
+
+
+def ref_fwd_bwd(q, k, v, g, h0, do, dht, cu):
+    leaves = [x.detach().double().requires_grad_() for x in (q, k, v, g)]
+    h0d = h0.double().requires_grad_() if h0 is not None else None
+    o, ht = og.chunk_gla_ref(*leaves, cu, initial_state=h0d, output_final_state=True)
+    loss = (o.double() * do.double()).sum() + (ht.double() * dht.double()).sum()
+    loss.backward()
+    grads = [x.grad for x in leaves] + [h0d.grad if h0d is not None else None]
+    return o.detach(), ht.detach(), grads
+
+
+def run_gpu(fn, q, k, v, g, h0, do, dht, cu):
+    dev = "cuda"
+    qq, kk, vv, gg = (x.to(dev).requires_grad_() for x in (q, k, v, g))
+    h0g = h0.to(dev).requires_grad_() if h0 is not None else None
+    o, ht = fn(qq, kk, vv, gg, cu.to(dev), initial_state=h0g, output_final_state=True)
+    torch.autograd.backward([o, ht], [do.to(dev), dht.to(dev)])
+    grads = [qq.grad, kk.grad, vv.grad, gg.grad, h0g.grad if h0g is not None else None]
+    return o.detach().cpu(), ht.detach().cpu(), [x.cpu() if x is not None else None for x in grads]
+
+
+CASES = [
+    (64, 2, 32, 32, [0, 20, 64]),
+    (200, 3, 64, 64, [0, 1, 2, 66, 130, 200]),  # length-1 sequences, ragged chunks
+    (257, 2, 16, 48, [0, 257]),  # K != V, one long sequence
+    (95, 4, 32, 16, [0, 0, 31, 31, 95]),  # empty sequences
+    (12, 1, 64, 64, [0, 5, 12]),  # shorter than one chunk
+]
+
+
+@pytest.mark.parametrize("T,H,K,V,cu", CASES)
+def test_chunk_gla_fp32(T, H, K, V, cu):
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    args = make(T, H, K, V, cu, torch.float32, seed=T)
+    o_r, ht_r, g_r = ref_fwd_bwd(*args)
+    o, ht, g = run_gpu(chunk_gla, *args)
+    assert rel_err(o, o_r) < FP32_TOL
+    assert rel_err(ht, ht_r) < FP32_TOL
+    for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g, g_r):
+        assert rel_err(a, b) < FP32_TOL, name
+
+
+@pytest.mark.parametrize("T,H,K,V,cu", CASES[:3])
+def test_chunk_gla_bf16(T, H, K, V, cu):
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    args = make(T, H, K, V, cu, torch.bfloat16, seed=T + 1)
+    o_r, ht_r, g_r = ref_fwd_bwd(*args)
+    o, ht, g = run_gpu(chunk_gla, *args)
+    assert o.dtype == torch.bfloat16 and ht.dtype == torch.float32
+    assert rel_err(o, o_r) < BF16_TOL
+    assert rel_err(ht, ht_r) < BF16_TOL
+    for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g, g_r):
+        assert rel_err(a, b) < BF16_TOL, name
+
+
+def test_chunk_gla_golden_reference_kernels():
+    """Against the reference's own chunk_gla (Triton, interpreted) outputs and gradients."""
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    d = torch.load(GOLDEN / "chunk_gla_interp.pt")
+    o, ht, g = run_gpu(chunk_gla, d["q"], d["k"], d["v"], d["g"], d["h0"], d["do"], d["dht"], d["cu"])
+    assert rel_err(o, d["o"]) < FP32_TOL and rel_err(ht, d["ht"]) < FP32_TOL
+    for name, a in zip(("dq", "dk", "dv", "dg", "dh0"), g):
+        assert rel_err(a, d[name]) < FP32_TOL, name
+
+
+def test_c1_anchor_both_operators():
+    from ssla_b200.ops.gla import chunk_gla, fused_recurrent_gla
+
+    d = torch.load(GOLDEN / "c1_naive_recurrent.pt")
+    args = [d[n].cuda() for n in ("q", "k", "v", "g")]
+    for fn in (chunk_gla, fused_recurrent_gla):
+        o, ht = fn(*args, d["cu"].cuda(), output_final_state=True)
+        assert rel_err(o, d["o"]) < FP32_TOL
+        assert rel_err(ht, d["ht"]) < FP32_TOL
+
+
+def test_chunk_gla_strong_decay_exact_path():
+    """Decays large enough that the factorised exponent form would overflow: the kernels must
+    switch to exact per-element exponents (no inf/nan)."""
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    args = list(make(128, 2, 32, 32, [0, 128], torch.float32, seed=5, gscale=0.08))
+    o_r, ht_r, g_r = ref_fwd_bwd(*args)
+    o, ht, g = run_gpu(chunk_gla, *args)
+    assert torch.isfinite(o).all()
+    assert rel_err(o, o_r) < FP32_TOL and rel_err(ht, ht_r) < FP32_TOL
+    for a, b in zip(g, g_r):
+        assert rel_err(a, b) < 1e-4
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, FP32_TOL), (torch.bfloat16, BF16_TOL)])
+@pytest.mark.parametrize("K,V", [(32, 32), (64, 64), (16, 32), (20, 24)])
+def test_fused_recurrent_vs_naive(dtype, tol, K, V):
+    from ssla_b200.ops.gla import fused_recurrent_gla
+
+    cu = [0, 1, 9, 40, 41]
+    q, k, v, g, h0, do, dht, cu = make(41, 3, K, V, cu, dtype, seed=K + V)
+    o_r, ht_r = og.naive_gla_recurrent(q.float(), k.float(), v.float(), g.float(), cu, initial_state=h0,
+                                       output_final_state=True)
+    o, ht = fused_recurrent_gla(q.cuda(), k.cuda(), v.cuda(), g.cuda(), cu.cuda(), initial_state=h0.cuda(),
+                                output_final_state=True)
+    assert o.dtype == dtype
+    assert rel_err(o, o_r) < tol and rel_err(ht, ht_r) < tol
+
+
+def test_fused_recurrent_streaming_equals_one_call():
+    """Carrying the final state between T=1 calls (the streaming use of config 3) equals one
+    call over the whole sequence."""
+    from ssla_b200.ops.gla import fused_recurrent_gla
+
+    N, H, K, V, T = 512, 4, 32, 32, 6
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(N, T, H, K, generator=gen).cuda()
+    k = torch.randn(N, T, H, K, generator=gen).cuda()
+    v = torch.randn(N, T, H, V, generator=gen).cuda()
+    g = F.logsigmoid(torch.randn(N, T, H, K, generator=gen)).cuda() / 16
+    cu_all = torch.arange(N + 1).cuda() * T
+    flat = lambda x: x.reshape(N * T, H, -1)
+    o_all, h_all = fused_recurrent_gla(flat(q), flat(k), flat(v), flat(g), cu_all, output_final_state=True)
+    state = None
+    cu1 = torch.arange(N + 1).cuda()
+    outs = []
+    for t in range(T):
+        o, state = fused_recurrent_gla(q[:, t], k[:, t], v[:, t], g[:, t], cu1, initial_state=state,
+                                       output_final_state=True)
+        outs.append(o)
+    o_steps = torch.stack(outs, 1).reshape(N * T, H, V)
+    assert rel_err(o_steps, o_all) < 1e-6 and rel_err(state, h_all) < 1e-6
+
+
+def test_fused_recurrent_backward():
+    from ssla_b200.ops.gla import fused_recurrent_gla
+
+    args = make(100, 2, 32, 32, [0, 37, 100], torch.float32, seed=9)
+    o_r, ht_r, g_r = ref_fwd_bwd(*args)
+    o, ht, g = run_gpu(fused_recurrent_gla, *args)
+    assert rel_err(o, o_r) < FP32_TOL
+    for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g, g_r):
+        assert rel_err(a, b) < FP32_TOL, name
+
+
+def test_chunk_gla_scalar_vs_naive():
+    from ssla_b200.ops.gla import chunk_gla_scalar
+
+    d = torch.load(GOLDEN / "gla_scalar_naive.pt")
+    leaves = [d[n].clone().requires_grad_() for n in ("q", "k", "v", "g", "h0")]
+    o_r, ht_r = og.naive_gla_recurrent_scalar(*leaves[:4], d["cu"], initial_state=leaves[4],
+                                              output_final_state=True)
+    assert rel_err(o_r, d["o"]) == 0.0
+    do = torch.randn_like(o_r)
+    dht = torch.randn_like(ht_r)
+    torch.autograd.backward([o_r, ht_r], [do, dht])
+    gl = [d[n].cuda().requires_grad_() for n in ("q", "k", "v", "g", "h0")]
+    o, ht = chunk_gla_scalar(*gl[:4], d["cu"].cuda(), initial_state=gl[4], output_final_state=True)
+    torch.autograd.backward([o, ht], [do.cuda(), dht.cuda()])
+    assert rel_err(o, d["o"]) < FP32_TOL and rel_err(ht, d["ht"]) < FP32_TOL
+    for a, b in zip(gl, leaves):
+        assert rel_err(a.grad, b.grad) < FP32_TOL
+
+
+def test_c2_full_size_bf16():
+    """BASELINE config 2 at full size (B=8, H=4, T=2048, K=V=64, bf16, h0) vs the float64
+    chunked oracle: outputs, final state and all gradients within 2e-2."""
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    B, H, T, K = 8, 4, 2048, 64
+    cu = (torch.arange(B + 1) * T).tolist()
+    args = make(B * T, H, K, K, cu, torch.bfloat16, seed=0)
+    o_r, ht_r, g_r = ref_fwd_bwd(*args)
+    o, ht, g = run_gpu(chunk_gla, *args)
+    assert rel_err(o, o_r) < BF16_TOL and rel_err(ht, ht_r) < BF16_TOL
+    for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g, g_r):
+        assert rel_err(a, b) < BF16_TOL, name

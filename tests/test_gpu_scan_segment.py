@@ -1,0 +1,111 @@
+"""GPU parity of the scan and segment kernels: bit-exact against the CPU oracle / CPU PyTorch."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import GOLDEN
+from oracle import gla as og
+from oracle import segment as oseg
+
+pytestmark = pytest.mark.gpu
+
+
+def test_scan_golden_bit_exact():
+    from ssla_b200.ops.common.scan import scan
+
+    d = torch.load(GOLDEN / "scan_interp.pt")
+    u = d["u"].cuda().requires_grad_()
+    g = d["g"].cuda().requires_grad_()
+    h = scan(u, g, d["cu"].cuda())
+    h.backward(d["dh"].cuda())
+    assert torch.equal(h.cpu(), d["h"])
+    assert torch.equal(u.grad.cpu(), d["du"]) and torch.equal(g.grad.cpu(), d["dg"])
+
+
+@pytest.mark.parametrize("C", [12, 24, 7, 256])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_scan_many_short_sequences(C, dtype):
+    from ssla_b200.ops.common.scan import scan
+
+    gen = torch.Generator().manual_seed(C)
+    lens = torch.randint(1, 12, (3000,), generator=gen)
+    lens[::97] = 0  # empty sequences
+    lens[5] = 300   # one long sequence
+    cu = torch.cat([torch.zeros(1, dtype=torch.int64), lens.cumsum(0)])
+    T = int(cu[-1])
+    u = torch.randn(T, C, generator=gen).to(dtype)
+    g = torch.sigmoid(torch.randn(T, C, generator=gen)).to(dtype)
+    h_r = og.scan_ref_vectorized(u, g, cu)
+    do = torch.randn(T, C, generator=gen).to(dtype)
+    du_r, dg_r = og.scan_ref_bwd_vectorized(do, g, h_r, cu)
+    uc, gc = u.cuda().requires_grad_(), g.cuda().requires_grad_()
+    h = scan(uc, gc, cu.cuda())
+    h.backward(do.cuda())
+    assert torch.equal(h.cpu(), h_r)
+    assert torch.equal(uc.grad.cpu(), du_r) and torch.equal(gc.grad.cpu(), dg_r)
+
+
+def _pool_case(seed=0, R=20000, S=5000, C=64, dtype=torch.float32, sorted_=True):
+    gen = torch.Generator().manual_seed(seed)
+    idx = torch.randint(0, S, (R,), generator=gen)
+    if sorted_:
+        idx = idx.sort().values
+    src = torch.randn(R, C, generator=gen)
+    src[::7] = src[3]  # ties for max
+    return src.to(dtype), idx, S
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_scatter_ops_bit_exact(dtype, sorted_):
+    from ssla_b200 import torch_scatter as ts
+    from ssla_b200.ops import segment as seg
+
+    src, idx, S = _pool_case(dtype=dtype, sorted_=sorted_)
+    exp_idx = idx[:, None].expand(-1, src.shape[1])
+    out, arg = ts.scatter_max(src.cuda(), exp_idx.cuda(), dim=0, dim_size=S)
+    o_r, a_r = oseg.scatter_max(src, idx, S)
+    assert torch.equal(out.cpu(), o_r) and torch.equal(arg.cpu(), a_r)
+    m = ts.scatter_mean(src.cuda(), exp_idx.cuda(), dim=0, dim_size=S)
+    assert torch.equal(m.cpu(), oseg.scatter_mean(src, idx, S))
+    s = ts.scatter_sum(src.cuda(), idx.cuda(), dim=0, dim_size=S)
+    assert torch.equal(s.cpu(), oseg.scatter_sum_fast(src, idx, S))
+    if sorted_:
+        off = seg.segment_offsets_sorted(idx.cuda(), S)
+        o2, a2 = seg.segment_reduce(src.cuda(), off, None, seg.MAX, want_arg=True)
+        assert torch.equal(o2.cpu(), o_r) and torch.equal(a2.cpu(), a_r)
+
+
+def test_scatter_fp32_matches_cpu_torch_index_add_order():
+    from ssla_b200 import torch_scatter as ts
+
+    src, idx, S = _pool_case(seed=3, sorted_=False)
+    ref = torch.zeros(S, src.shape[1]).index_add_(0, idx, src)
+    assert torch.equal(ts.scatter_sum(src.cuda(), idx.cuda(), dim=0, dim_size=S).cpu(), ref)
+
+
+def test_index_add_and_gather():
+    from ssla_b200.ops import segment as seg
+
+    gen = torch.Generator().manual_seed(1)
+    P, D, C = 50000, 9000, 24
+    idx = torch.randint(0, D, (P,), generator=gen)
+    idx[:40] = 17  # one big segment (> 32 rows: the long rank-sort path)
+    src = torch.randn(P, C, generator=gen)
+    out = seg.index_add_rows(src.cuda(), idx.cuda(), D)
+    ref = torch.zeros(D, C).index_add_(0, idx, src)
+    assert torch.equal(out.cpu(), ref)
+    gi = torch.randint(0, D, (777,), generator=gen)
+    assert torch.equal(seg.gather_rows(ref.cuda(), gi.cuda()).cpu(), ref[gi])
+
+
+def test_segment_edge_cases():
+    from ssla_b200.ops import segment as seg
+
+    idx = torch.zeros(0, dtype=torch.int64).cuda()
+    off = seg.segment_offsets_sorted(idx, 3)
+    assert off.tolist() == [0, 0, 0, 0]
+    out, arg = seg.segment_reduce(torch.zeros(0, 4).cuda(), off, None, seg.MAX, want_arg=True)
+    assert out.abs().sum() == 0 and (arg == 0).all()
+    off, rows = seg.segment_csr(torch.tensor([2, 2, 0]).cuda(), 4)
+    assert off.tolist() == [0, 1, 1, 3, 3] and rows[:3].tolist() == [2, 0, 1]
