@@ -106,16 +106,19 @@ def test_c1_anchor_both_operators():
 
 def test_chunk_gla_strong_decay_exact_path():
     """Decays large enough that the factorised exponent form would overflow: the kernels must
-    switch to exact per-element exponents (no inf/nan)."""
+    switch to exact per-element exponents (no inf/nan).  Reference: the fp32 token recurrence
+    (the float64 chunk oracle cannot represent these decays)."""
     from ssla_b200.ops.gla.chunk import chunk_gla
 
-    args = list(make(128, 2, 32, 32, [0, 128], torch.float32, seed=5, gscale=0.08))
-    o_r, ht_r, g_r = ref_fwd_bwd(*args)
-    o, ht, g = run_gpu(chunk_gla, *args)
-    assert torch.isfinite(o).all()
-    assert rel_err(o, o_r) < FP32_TOL and rel_err(ht, ht_r) < FP32_TOL
-    for a, b in zip(g, g_r):
-        assert rel_err(a, b) < 1e-4
+    q, k, v, g, h0, do, dht, cu = make(100, 2, 32, 32, [0, 100], torch.float32, seed=5, gscale=0.08)
+    leaves = [x.clone().requires_grad_() for x in (q, k, v, g, h0)]
+    o_r, ht_r = og.naive_gla_recurrent(*leaves[:4], cu, initial_state=leaves[4], output_final_state=True)
+    torch.autograd.backward([o_r, ht_r], [do, dht])
+    o, ht, g_ = run_gpu(chunk_gla, q, k, v, g, h0, do, dht, cu)
+    assert torch.isfinite(o).all() and all(torch.isfinite(x).all() for x in g_)
+    assert rel_err(o, o_r) < 1e-4 and rel_err(ht, ht_r) < 1e-4
+    for a, b in zip(g_, leaves):
+        assert rel_err(a, b.grad) < 1e-4
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, FP32_TOL), (torch.bfloat16, BF16_TOL)])
