@@ -106,6 +106,19 @@ int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* 
                        float* dg, float* dh0, void* workspace, size_t workspace_bytes,
                        ssla_stream_t stream);
 
+/* chunk_gla forward that allocates nothing: no counterpart in the reference.  For callers
+ * that cannot call cudaMalloc (a runtime that owns every allocation and hands the library
+ * only input/output buffers, a pool that has claimed all device memory).  Same arguments
+ * and results as ssla_chunk_gla_fwd minus `states` and `workspace`: the intermediates live
+ * in a fixed 64 MiB scratch array built into the library (held on every GPU that loads it
+ * until exit); shapes needing more return SSLA_ERR_WORKSPACE.  The first call on each device
+ * looks up the array's device address (make it before any stream capture).  All calls on a
+ * device share the array, so calls that overlap on the GPU race: serialise them. */
+int ssla_chunk_gla_fwd_noalloc(const void* q, const void* k, const void* v, const void* g,
+                               int dtype, int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs,
+                               int64_t T, int64_t H, int64_t K, int64_t V, float scale,
+                               const float* h0, void* o, float* ht, ssla_stream_t stream);
+
 /* ------------------------------------------------------------------ segments
  * Reductions of rows of src [R,C] into out [S,C] by a row->segment index [R] (int64).
  * Semantics of torch_scatter.scatter_max / scatter_mean / scatter_sum (dim=0) as called

@@ -39,6 +39,7 @@ SIGNATURES = {
         i32,
         [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p, p, p, p, p, p, sz, p],
     ),
+    "ssla_chunk_gla_fwd_noalloc": (i32, [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p]),
     "ssla_segment_offsets_sorted": (i32, [p, i64, i64, p, p]),
     "ssla_segment_csr_workspace_bytes": (sz, [i64, i64]),
     "ssla_segment_csr": (i32, [p, i64, i64, p, p, p, sz, p]),
