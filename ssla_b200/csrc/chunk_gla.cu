@@ -32,7 +32,9 @@ constexpr int NTHR = 256;
 
 // --------------------------------------------------------------------------- prep + scans
 __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __restrict__ cu,
-                                                             int64_t N, int64_t* __restrict__ off) {
+                                                             int64_t N, int64_t MC,
+                                                             int64_t* __restrict__ off,
+                                                             longlong2* __restrict__ tab) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -70,6 +72,17 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
     __syncthreads();
   }
   if (tid == 0) off[N] = carry;
+  __syncthreads();
+  // chunk table: {first token, valid rows | sequence << 32}, -1 sequence for unused ids
+  for (int64_t n = tid; n < N; n += 1024) {
+    const int64_t b = cu[n], e = cu[n + 1];
+    int64_t c = off[n];
+    for (int64_t t = b; t < e; t += BT, ++c) {
+      const int64_t len = (e - t) < BT ? (e - t) : BT;
+      tab[c] = make_longlong2(t, len | (n << 32));
+    }
+  }
+  for (int64_t c = carry + tid; c < MC; c += 1024) tab[c] = make_longlong2(0, (int64_t)-1 << 32);
 }
 
 __global__ void __launch_bounds__(256) state_scan_kernel(
@@ -87,19 +100,30 @@ __global__ void __launch_bounds__(256) state_scan_kernel(
   const int k = (int)(kv / V);
   const int64_t c0 = chunk_off[seq], c1 = chunk_off[seq + 1];
   float x = init ? init[idx] : 0.f;
-  if (!reverse) {
-#pragma unroll 4
-    for (int64_t c = c0; c < c1; ++c) {
-      const int64_t e = (c * H + head) * KV + kv;
-      per_chunk[e] = x;
-      x = fmaf(decay[(c * H + head) * K + k], x, dS[e]);
+  // Loads of dS / decay do not depend on the running state: fetch 8 chunks at a time so
+  // their latency overlaps, then run the 8 dependent FMAs.
+  constexpr int G = 8;
+  const int64_t n = c1 - c0;
+  for (int64_t b = 0; b < n; b += G) {
+    float d[G], a[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int64_t c = reverse ? c1 - 1 - (b + u) : c0 + b + u;
+      if (b + u < n) {
+        d[u] = decay[(c * H + head) * K + k];
+        a[u] = dS[(c * H + head) * KV + kv];
+      } else {
+        d[u] = 1.f;
+        a[u] = 0.f;
+      }
     }
-  } else {
-#pragma unroll 4
-    for (int64_t c = c1 - 1; c >= c0; --c) {
-      const int64_t e = (c * H + head) * KV + kv;
-      per_chunk[e] = x;
-      x = fmaf(decay[(c * H + head) * K + k], x, dS[e]);
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      if (b + u < n) {
+        const int64_t c = reverse ? c1 - 1 - (b + u) : c0 + b + u;
+        per_chunk[(c * H + head) * KV + kv] = x;
+        x = fmaf(d[u], x, a[u]);
+      }
     }
   }
   if (fin) fin[idx] = x;
@@ -219,7 +243,7 @@ __device__ __forceinline__ void sub_chunk_refs(const float* sg, float* ref, int*
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) local_state_kernel(
     int mode, const T* __restrict__ a_src, const T* __restrict__ b_src, const Tg* __restrict__ g,
-    const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off, int64_t N, int H,
+    const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab, int64_t N, int H,
     int K, int V, float scale, float* __restrict__ dS, float* __restrict__ decay) {
   constexpr int LD = L<P>::LD;
   extern __shared__ float sm[];
@@ -231,7 +255,7 @@ __global__ void __launch_bounds__(NTHR) local_state_kernel(
   const int head = blockIdx.y;
   int64_t seq, t0;
   int len;
-  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
   load_tile<Tg, P>(sg, g, t0, len, H, head, K);
   load_tile<T, P>(sa, a_src, t0, len, H, head, K);
   load_tile<T, P>(sb, b_src, t0, len, H, head, V);
@@ -259,9 +283,9 @@ __global__ void __launch_bounds__(NTHR) local_state_kernel(
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
-    T* __restrict__ o) {
+    T* __restrict__ o, const int* __restrict__ flags) {
   constexpr int LD = L<P>::LD;
   extern __shared__ float sm[];
   float* sq = sm;
@@ -277,9 +301,10 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
   __shared__ int exact_q[NC], exact_k[NC];
   const int64_t cid = blockIdx.x;
   const int head = blockIdx.y;
+  if (flags && !flags[cid * H + head]) return;
   int64_t seq, t0;
   int len;
-  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
   load_tile<T, P>(sq, q, t0, len, H, head, K);
   load_tile<T, P>(sk, k, t0, len, H, head, K);
   load_tile<Tg, P>(sg, g, t0, len, H, head, K);
@@ -338,10 +363,10 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) bwd_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const int64_t* __restrict__ chunk_off,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
     const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
-    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg) {
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ flags) {
   constexpr int LD = L<P>::LD;
   extern __shared__ float sm[];
   float* sq = sm;
@@ -361,9 +386,10 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
   __shared__ int exact_q[NC], exact_k[NC];
   const int64_t cid = blockIdx.x;
   const int head = blockIdx.y;
+  if (flags && !flags[cid * H + head]) return;
   int64_t seq, t0;
   int len;
-  if (!locate_chunk(cid, chunk_off, cu, N, seq, t0, len)) return;
+  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
   load_tile<T, P>(sq, q, t0, len, H, head, K);
   load_tile<T, P>(sk, k, t0, len, H, head, K);
   load_tile<Tg, P>(sg, g, t0, len, H, head, K);
@@ -545,7 +571,7 @@ template <int P> constexpr size_t smem_bwd() {
 
 template <typename T, typename Tg, int P>
 int run_local(int mode, const void* a_src, const void* b_src, const void* g, const int64_t* cu,
-              const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+              const longlong2* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
               float* dS, float* decay, cudaStream_t s) {
   auto kern = local_state_kernel<T, Tg, P>;
   const size_t smem = smem_local<P>();
@@ -558,29 +584,29 @@ int run_local(int mode, const void* a_src, const void* b_src, const void* g, con
 
 template <typename T, typename Tg, int P>
 int run_fwd_o(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
-              const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
-              const float* states, void* o, cudaStream_t s) {
+              const longlong2* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+              const float* states, void* o, const int* flags, cudaStream_t s) {
   auto kern = fwd_o_kernel<T, Tg, P>;
   const size_t smem = smem_fwd_o<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v,
                                                  (const Tg*)g, cu, off, N, H, K, V, scale, states,
-                                                 (T*)o);
+                                                 (T*)o, flags);
   SSLA_CHECK_LAUNCH("chunk_gla fwd_o");
   return SSLA_OK;
 }
 
 template <typename T, typename Tg, int P>
 int run_bwd(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
-            const int64_t* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
+            const longlong2* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
             const float* states, const float* dstates, const void* dout, void* dq, void* dk,
-            void* dv, float* dg, cudaStream_t s) {
+            void* dv, float* dg, const int* flags, cudaStream_t s) {
   auto kern = bwd_kernel<T, Tg, P>;
   const size_t smem = smem_bwd<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>(
       (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K, V, scale, states,
-      dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg);
+      dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, flags);
   SSLA_CHECK_LAUNCH("chunk_gla bwd");
   return SSLA_OK;
 }
@@ -609,8 +635,33 @@ inline int pad_of(int64_t K, int64_t V) {
 
 }  // namespace
 
-int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t* chunk_off, cudaStream_t s) {
-  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, chunk_off);
+int simt_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
+               const int64_t* cu, const longlong2* off, int64_t N, int64_t MC, int64_t H, int64_t K,
+               int64_t V, float scale, const float* states, void* o, const int* flags,
+               cudaStream_t s) {
+  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+      return run_fwd_o<T_, Tg, P>(q, k, v, g, cu, off, N, MC, (int)H, (int)K, (int)V, scale,
+                                  states, o, flags, s);
+    });
+  });
+}
+
+int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
+             const int64_t* cu, const longlong2* off, int64_t N, int64_t MC, int64_t H, int64_t K,
+             int64_t V, float scale, const float* states, const float* dstates, const void* dout,
+             void* dq, void* dk, void* dv, float* dg, const int* flags, cudaStream_t s) {
+  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+      return run_bwd<T_, Tg, P>(q, k, v, g, cu, off, N, MC, (int)H, (int)K, (int)V, scale, states,
+                                dstates, dout, dq, dk, dv, dg, flags, s);
+    });
+  });
+}
+
+int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chunk_off,
+                         longlong2* chunk_tab, cudaStream_t s) {
+  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, MC, chunk_off, chunk_tab);
   SSLA_CHECK_LAUNCH("chunk_gla chunk_offsets");
   return SSLA_OK;
 }
@@ -672,16 +723,16 @@ extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, c
   cudaStream_t s = (cudaStream_t)stream;
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, w.chunk_off, s))) return rc;
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
   const bool tc = tc_supported(dtype, dtype_g, K, V);
   if (MC > 0) {
     if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale,
+      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
                           w.dS, w.decay, s);
     } else {
       rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
         return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-          return run_local<T_, Tg, P>(0, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H,
+          return run_local<T_, Tg, P>(0, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, (int)H,
                                       (int)K, (int)V, scale, w.dS, w.decay, s);
         });
       });
@@ -691,15 +742,15 @@ extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, c
   if ((rc = launch_state_scan(w.dS, w.decay, w.chunk_off, n_seqs, H, K, V, h0, states, ht, false, s)))
     return rc;
   if (MC == 0) return SSLA_OK;
-  if (tc)
-    return tc_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale,
-                    states, o, s);
-  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
-    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-      return run_fwd_o<T_, Tg, P>(q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H, (int)K,
-                                  (int)V, scale, states, o, s);
-    });
-  });
+  if (tc) {
+    if ((rc = tc_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
+                       states, o, w.flags, s)))
+      return rc;
+    return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V,
+                      scale, states, o, w.flags, s);
+  }
+  return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V,
+                    scale, states, o, nullptr, s);
 }
 
 extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* g,
@@ -723,16 +774,16 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
   cudaStream_t s = (cudaStream_t)stream;
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, w.chunk_off, s))) return rc;
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
   const bool tc = tc_supported(dtype, dtype_g, K, V);
   if (MC > 0) {
     if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, cu_seqlens, w.chunk_off, n_seqs, MC, H,
+      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H,
                           scale, w.dS, w.decay, s);
     } else {
       rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
         return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-          return run_local<T_, Tg, P>(1, q, dout, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H,
+          return run_local<T_, Tg, P>(1, q, dout, g, cu_seqlens, w.chunk_tab, n_seqs, MC, (int)H,
                                       (int)K, (int)V, scale, w.dS, w.decay, s);
         });
       });
@@ -743,13 +794,13 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
                               s)))
     return rc;
   if (MC == 0) return SSLA_OK;
-  if (tc)
-    return tc_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, H, scale, states,
-                  w.dstates, dout, dq, dk, dv, dg, s);
-  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
-    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-      return run_bwd<T_, Tg, P>(q, k, v, g, cu_seqlens, w.chunk_off, n_seqs, MC, (int)H, (int)K,
-                                (int)V, scale, states, w.dstates, dout, dq, dk, dv, dg, s);
-    });
-  });
+  if (tc) {
+    if ((rc = tc_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
+                     states, w.dstates, dout, dq, dk, dv, dg, w.flags, s)))
+      return rc;
+    return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V, scale,
+                    states, w.dstates, dout, dq, dk, dv, dg, w.flags, s);
+  }
+  return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V, scale,
+                  states, w.dstates, dout, dq, dk, dv, dg, nullptr, s);
 }

@@ -1,0 +1,133 @@
+// Minimal tcgen05 (5th-generation tensor core) helpers for sm_100a, written as inline PTX.
+//
+// Conventions used by the chunked-GLA kernels:
+//  * operands are 16-bit tiles in shared memory stored "8x8 blocked": element (r, c) of an
+//    R x C tile lives at byte ((r/8)*(C/8) + c/8)*128 + (r%8)*16 + (c%8)*2, i.e. 128-byte core
+//    matrices of 8 rows x 16 bytes.  One such tile serves as a K-major operand (rows = M/N,
+//    columns = K) or, read the other way, as an MN-major operand (rows = K, columns = M/N),
+//    with no swizzle (SWIZZLE_NONE descriptors);
+//  * accumulators are fp32 in tensor memory (TMEM); an M=64 MMA with cta_group::1 writes row m
+//    to TMEM lane (m % 16) + 32 * (m / 16), column n, so warp w of a 4-warp group reads rows
+//    16w .. 16w+15 with its lanes 0..15;
+//  * one elected thread issues MMAs and commits them to an mbarrier; waits are bounded.
+#pragma once
+#include <stdint.h>
+
+namespace ssla {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_NONE, version 1 (Blackwell).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version
+  return d;                // base offset 0, lbo mode 0, layout type 0 (no swizzle)
+}
+
+// Descriptor of a 64-column blocked tile used K-major: K-adjacent core matrices 128 B apart,
+// M/N-adjacent ones (cols/8)*128 B apart.  k-step s (16 elements) starts 256*s bytes later.
+__device__ __forceinline__ uint64_t desc_kmajor(const void* tile, int cols, int kstep) {
+  return smem_desc(smem_u32(tile) + 256u * kstep, 128u, (uint32_t)(cols / 8) * 128u);
+}
+// The same storage read MN-major (tile rows = K): M/N-adjacent core matrices 128 B apart,
+// K-adjacent ones (cols/8)*128 B apart; k-step s starts 2*(cols/8)*128*s bytes later.
+__device__ __forceinline__ uint64_t desc_mnmajor(const void* tile, int cols, int kstep) {
+  const uint32_t kstride = (uint32_t)(cols / 8) * 128u;
+  return smem_desc(smem_u32(tile) + 2u * kstride * kstep, kstride, 128u);
+}
+
+// Instruction descriptor: kind::f16, fp32 accumulate.  in_fmt 0 = f16, 1 = bf16.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int in_fmt, int a_mn, int b_mn) {
+  return (1u << 4) | ((uint32_t)in_fmt << 7) | ((uint32_t)in_fmt << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(mbar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Make generic-proxy shared-memory writes visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mbar)), "r"(count)
+               : "memory");
+}
+
+// Bounded wait for the mbarrier phase with parity `parity`.  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_iter = 1u << 26) {
+  const uint32_t a = smem_u32(mbar);
+  for (uint32_t i = 0; i < max_iter; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Warp-collective TMEM allocation (ncols: power of two >= 32); address written to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of (row block of warp w, column c) for an M=64 accumulator at base column.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp, int col) {
+  return base + ((uint32_t)(32 * warp) << 16) + (uint32_t)col;
+}
+
+// Byte offset of element (r, c) in an 8x8-blocked tile with `cols` columns (16-bit elements).
+__host__ __device__ __forceinline__ int blk_off(int r, int c, int cols) {
+  return ((r >> 3) * (cols >> 3) + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2;
+}
+
+}  // namespace tc
+}  // namespace ssla

@@ -204,3 +204,22 @@ def test_c2_full_size_bf16():
     assert rel_err(o, o_r) < BF16_TOL and rel_err(ht, ht_r) < BF16_TOL
     for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g, g_r):
         assert rel_err(a, b) < BF16_TOL, name
+
+
+def test_chunk_gla_bf16_mixed_tensor_core_and_exact_chunks():
+    """bf16 inputs where some chunks have decay ranges beyond the tensor-core kernels'
+    single-reference bound: those chunks are flagged and recomputed by the exact kernels."""
+    from ssla_b200.ops.gla.chunk import chunk_gla
+
+    T, H, K = 256, 2, 64
+    q, k, v, g, h0, do, dht, cu = make(T, H, K, K, [0, 100, 256], torch.float32, seed=11)
+    g[128:192] = g[128:192] * 200.0  # strong decays in one chunk of the second sequence
+    q, k, v, g, do = (x.to(torch.bfloat16) for x in (q, k, v, g, do))
+    leaves = [x.float().clone().requires_grad_() for x in (q, k, v, g)] + [h0.clone().requires_grad_()]
+    o_r, ht_r = og.naive_gla_recurrent(*leaves[:4], cu, initial_state=leaves[4], output_final_state=True)
+    torch.autograd.backward([o_r, ht_r], [do.float(), dht])
+    o, ht, g_ = run_gpu(chunk_gla, q, k, v, g, h0, do, dht, cu)
+    assert rel_err(o, o_r) < BF16_TOL and rel_err(ht, ht_r) < BF16_TOL
+    for name, a, b in zip(("dq", "dk", "dv", "dg", "dh0"), g_, leaves):
+        assert torch.isfinite(a).all(), name
+        assert rel_err(a, b.grad) < BF16_TOL, name
