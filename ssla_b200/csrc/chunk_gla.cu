@@ -73,60 +73,117 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
   }
   if (tid == 0) off[N] = carry;
   __syncthreads();
-  // chunk table: {first token, valid rows | sequence << 32}, -1 sequence for unused ids
-  for (int64_t n = tid; n < N; n += 1024) {
-    const int64_t b = cu[n], e = cu[n + 1];
-    int64_t c = off[n];
-    for (int64_t t = b; t < e; t += BT, ++c) {
-      const int64_t len = (e - t) < BT ? (e - t) : BT;
-      tab[c] = make_longlong2(t, len | (n << 32));
+  // chunk table: {first token, valid rows | sequence << 32}, -1 sequence for unused ids.
+  // One thread per chunk id; its sequence is found by binary search over the offsets.
+  const int64_t total = carry;
+  for (int64_t c = tid; c < total; c += 1024) {
+    int64_t lo = 0, hi = N - 1;  // last n with off[n] <= c
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (off[mid] <= c) lo = mid; else hi = mid - 1;
     }
+    const int64_t t = cu[lo] + (c - off[lo]) * BT;
+    const int64_t e = cu[lo + 1];
+    const int64_t len = (e - t) < BT ? (e - t) : BT;
+    tab[c] = make_longlong2(t, len | (lo << 32));
   }
   for (int64_t c = carry + tid; c < MC; c += 1024) tab[c] = make_longlong2(0, (int64_t)-1 << 32);
 }
 
-__global__ void __launch_bounds__(256) state_scan_kernel(
+// h_{c+1} = decay_c * h_c + dS_c along the chunks of each sequence, element-wise in (k, v).
+// One thread per (state element, segment): the chunk axis is cut into `nseg` segments (chosen
+// on the host so the grid is about one resident wave); each segment first composes its affine
+// map (prod decay, local sum), segment start values are chained in shared memory, then every
+// segment re-walks its chunks from its start value writing the per-chunk states.  Loads are
+// issued 16 chunks at a time (they do not depend on the running state).
+constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 16;
+__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
     const float* __restrict__ init, float* __restrict__ per_chunk, float* __restrict__ fin,
-    bool reverse) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t KV = (int64_t)K * V;
-  if (idx >= N * H * KV) return;
-  const int64_t seq = idx / (H * KV);
-  const int64_t rem = idx - seq * H * KV;
-  const int head = (int)(rem / KV);
-  const int64_t kv = rem - head * KV;
-  const int k = (int)(kv / V);
-  const int64_t c0 = chunk_off[seq], c1 = chunk_off[seq + 1];
-  float x = init ? init[idx] : 0.f;
-  // Loads of dS / decay do not depend on the running state: fetch 8 chunks at a time so
-  // their latency overlaps, then run the 8 dependent FMAs.
-  constexpr int G = 8;
-  const int64_t n = c1 - c0;
-  for (int64_t b = 0; b < n; b += G) {
-    float d[G], a[G];
+    bool reverse, int nseg) {
+  __shared__ float sA[SCAN_MAXSEG][SCAN_EL], sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
+  const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
+  const int64_t KV = (int64_t)K * V, HKV = (int64_t)H * KV, HK = (int64_t)H * K;
+  const int64_t idx = (int64_t)blockIdx.x * SCAN_EL + el;
+  const bool valid = idx < N * HKV;
+  int64_t cs = 0, n = 0, ebase = 0, dbase = 0;
+  if (valid) {
+    const int64_t seq = idx / HKV;
+    const int64_t rem = idx - seq * HKV;
+    const int64_t head = rem / KV;
+    const int64_t kv = rem - head * KV;
+    const int64_t c0 = chunk_off[seq];
+    n = chunk_off[seq + 1] - c0;
+    cs = reverse ? c0 + n - 1 : c0;
+    ebase = head * KV + kv;
+    dbase = head * K + kv / V;
+  }
+  const int64_t dir = reverse ? -1 : 1;
+  const int64_t Ls = (n + nseg - 1) / nseg;
+  const int64_t i0 = sg * Ls, i1 = (i0 + Ls < n) ? i0 + Ls : n;
+  float A = 1.f, B = 0.f;
+  {
+    int64_t i = i0;
+    for (; i + SCAN_U <= i1; i += SCAN_U) {
+      float d[SCAN_U], a[SCAN_U];
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const int64_t c = reverse ? c1 - 1 - (b + u) : c0 + b + u;
-      if (b + u < n) {
-        d[u] = decay[(c * H + head) * K + k];
-        a[u] = dS[(c * H + head) * KV + kv];
-      } else {
-        d[u] = 1.f;
-        a[u] = 0.f;
+      for (int u = 0; u < SCAN_U; ++u) {
+        const int64_t c = cs + dir * (i + u);
+        d[u] = decay[c * HK + dbase];
+        a[u] = dS[c * HKV + ebase];
       }
+#pragma unroll
+      for (int u = 0; u < SCAN_U; ++u) { B = fmaf(d[u], B, a[u]); A *= d[u]; }
     }
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-      if (b + u < n) {
-        const int64_t c = reverse ? c1 - 1 - (b + u) : c0 + b + u;
-        per_chunk[(c * H + head) * KV + kv] = x;
-        x = fmaf(d[u], x, a[u]);
-      }
+    for (; i < i1; ++i) {
+      const int64_t c = cs + dir * i;
+      const float d = decay[c * HK + dbase];
+      B = fmaf(d, B, dS[c * HKV + ebase]);
+      A *= d;
     }
   }
-  if (fin) fin[idx] = x;
+  float x;
+  if (nseg > 1) {
+    sA[sg][el] = A;
+    sB[sg][el] = B;
+    __syncthreads();
+    if (sg == 0) {
+      float y = (valid && init) ? init[idx] : 0.f;
+      for (int s2 = 0; s2 < nseg; ++s2) {
+        sX[s2][el] = y;
+        y = fmaf(sA[s2][el], y, sB[s2][el]);
+      }
+      if (valid && fin) fin[idx] = y;
+    }
+    __syncthreads();
+    x = sX[sg][el];
+  } else {
+    x = (valid && init) ? init[idx] : 0.f;
+    if (valid && fin) fin[idx] = fmaf(A, x, B);
+  }
+  int64_t i = i0;
+  for (; i + SCAN_U <= i1; i += SCAN_U) {
+    float d[SCAN_U], a[SCAN_U];
+#pragma unroll
+    for (int u = 0; u < SCAN_U; ++u) {
+      const int64_t c = cs + dir * (i + u);
+      d[u] = decay[c * HK + dbase];
+      a[u] = dS[c * HKV + ebase];
+    }
+#pragma unroll
+    for (int u = 0; u < SCAN_U; ++u) {
+      per_chunk[(cs + dir * (i + u)) * HKV + ebase] = x;
+      x = fmaf(d[u], x, a[u]);
+    }
+  }
+  for (; i < i1; ++i) {
+    const int64_t c = cs + dir * i;
+    const float d = decay[c * HK + dbase];
+    const float a = dS[c * HKV + ebase];
+    per_chunk[c * HKV + ebase] = x;
+    x = fmaf(d, x, a);
+  }
 }
 
 // --------------------------------------------------------------------------- tile helpers
@@ -281,11 +338,11 @@ __global__ void __launch_bounds__(NTHR) local_state_kernel(
 
 // --------------------------------------------------------------------------- forward output
 template <typename T, typename Tg, int P>
-__global__ void __launch_bounds__(NTHR) fwd_o_kernel(
+__device__ __forceinline__ void fwd_o_body(int64_t cid, int head, 
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
-    T* __restrict__ o, const int* __restrict__ flags) {
+    T* __restrict__ o) {
   constexpr int LD = L<P>::LD;
   extern __shared__ float sm[];
   float* sq = sm;
@@ -299,9 +356,6 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
   float* sA = sO + BT * LD;
   __shared__ float ref[NC * P];
   __shared__ int exact_q[NC], exact_k[NC];
-  const int64_t cid = blockIdx.x;
-  const int head = blockIdx.y;
-  if (flags && !flags[cid * H + head]) return;
   int64_t seq, t0;
   int len;
   if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
@@ -359,14 +413,34 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
       });
 }
 
+// Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
+// kernels): a small grid strides over the (chunk, head) pairs and processes flagged ones only.
+template <typename T, typename Tg, int P>
+__global__ void __launch_bounds__(NTHR) fwd_o_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
+    int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
+    T* __restrict__ o, const int* __restrict__ flags, int64_t MC) {
+  if (!flags) {
+    fwd_o_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
+    return;
+  }
+  for (int64_t w = blockIdx.x; w < MC * H; w += gridDim.x) {
+    if (flags[w]) {
+      fwd_o_body<T, Tg, P>(w / H, (int)(w % H), q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
+      __syncthreads();
+    }
+  }
+}
+
 // --------------------------------------------------------------------------- backward
 template <typename T, typename Tg, int P>
-__global__ void __launch_bounds__(NTHR) bwd_kernel(
+__device__ __forceinline__ void bwd_body(int64_t cid, int head, 
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
     const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
-    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ flags) {
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg) {
   constexpr int LD = L<P>::LD;
   extern __shared__ float sm[];
   float* sq = sm;
@@ -384,9 +458,6 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
   __shared__ float ref[NC * P];
   __shared__ float sL[P], sLg[P];
   __shared__ int exact_q[NC], exact_k[NC];
-  const int64_t cid = blockIdx.x;
-  const int head = blockIdx.y;
-  if (flags && !flags[cid * H + head]) return;
   int64_t seq, t0;
   int len;
   if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
@@ -560,6 +631,27 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
   }
 }
 
+// Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
+// kernels): a small grid strides over the (chunk, head) pairs and processes flagged ones only.
+template <typename T, typename Tg, int P>
+__global__ void __launch_bounds__(NTHR) bwd_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
+    int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
+    const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ flags, int64_t MC) {
+  if (!flags) {
+    bwd_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
+    return;
+  }
+  for (int64_t w = blockIdx.x; w < MC * H; w += gridDim.x) {
+    if (flags[w]) {
+      bwd_body<T, Tg, P>(w / H, (int)(w % H), q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
+      __syncthreads();
+    }
+  }
+}
+
 // --------------------------------------------------------------------------- launchers
 template <int P> constexpr size_t smem_local() { return 3 * BT * L<P>::LD * 4; }
 template <int P> constexpr size_t smem_fwd_o() {
@@ -589,9 +681,10 @@ int run_fwd_o(const void* q, const void* k, const void* v, const void* g, const 
   auto kern = fwd_o_kernel<T, Tg, P>;
   const size_t smem = smem_fwd_o<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v,
-                                                 (const Tg*)g, cu, off, N, H, K, V, scale, states,
-                                                 (T*)o, flags);
+  const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
+                          : dim3((unsigned)MC, H);
+  kern<<<grid, NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H,
+                                K, V, scale, states, (T*)o, flags, MC);
   SSLA_CHECK_LAUNCH("chunk_gla fwd_o");
   return SSLA_OK;
 }
@@ -604,9 +697,11 @@ int run_bwd(const void* q, const void* k, const void* v, const void* g, const in
   auto kern = bwd_kernel<T, Tg, P>;
   const size_t smem = smem_bwd<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<dim3((unsigned)MC, H), NTHR, smem, s>>>(
-      (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K, V, scale, states,
-      dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, flags);
+  const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
+                          : dim3((unsigned)MC, H);
+  kern<<<grid, NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H,
+                                K, V, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk,
+                                (T*)dv, dg, flags, MC);
   SSLA_CHECK_LAUNCH("chunk_gla bwd");
   return SSLA_OK;
 }
@@ -671,9 +766,11 @@ int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_
                       float* final_state, bool reverse, cudaStream_t s) {
   const int64_t threads = N * H * K * V;
   if (threads == 0) return SSLA_OK;
-  state_scan_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(dS, decay, chunk_off, N, (int)H, (int)K,
-                                                           (int)V, init, per_chunk, final_state,
-                                                           reverse);
+  // segments per element: enough threads for about one resident wave (148 SMs x 2048)
+  int64_t nseg = (int64_t)kNumSMs * 2048 / threads;
+  nseg = nseg < 1 ? 1 : (nseg > SCAN_MAXSEG ? SCAN_MAXSEG : nseg);
+  state_scan_kernel<<<ceil_div(threads, SCAN_EL), SCAN_EL * (int)nseg, 0, s>>>(
+      dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk, final_state, reverse, (int)nseg);
   SSLA_CHECK_LAUNCH("chunk_gla state_scan");
   return SSLA_OK;
 }

@@ -131,42 +131,46 @@ __device__ __forceinline__ void stage_gate(unsigned char* raw, const Tg* __restr
   }
 }
 
-// From the staged raw gate tile: in-chunk cumulative sums gc (one warp per column, two rows per
-// lane, shuffle scan), ref, gL, exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk,
-// and E = exp(gc - ref) (STORE_GC: gc itself).
+// From the staged raw gate tile: in-chunk cumulative sums gc, ref (gc of row 31), gL (row 63),
+// exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk, and E = exp(gc - ref)
+// (STORE_GC: gc itself).  Thread (column c = tid % 64, quarter q = tid / 64) scans rows
+// 16q .. 16q+15 of its column serially in registers; the quarter totals are combined
+// through shared memory (two barriers, no shuffle chains).
 template <typename Tg, bool STORE_GC>
 __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw) {
-  const int tid = threadIdx.x;
+  static_assert(NT == 256, "gate_prep maps 4 threads to each of the 64 columns");
+  const int tid = threadIdx.x, c = tid & 63, qt = tid >> 6;
   const Tg* gr = reinterpret_cast<const Tg*>(raw);
   if (tid == 0) G.span_bits = 0u;
-  for (int e = tid; e < BT * D; e += NT) G.E[(e >> 6) * LDG + (e & 63)] = ldf(gr + e);
+  float x[16];
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    run += ldf(gr + (16 * qt + i) * D + c);
+    x[i] = run;
+  }
+  G.part[qt][c] = run;
   __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
-  for (int c = warp; c < D; c += NWARP) {
-    const float a = G.E[(2 * lane) * LDG + c], b = G.E[(2 * lane + 1) * LDG + c];
-    float x = a + b;
+  float off = 0.f;
+  for (int j = 0; j < qt; ++j) off += G.part[j][c];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    float excl = __shfl_up_sync(0xffffffffu, x, 1);
-    if (lane == 0) excl = 0.f;
-    const float g0 = excl + a, g1 = excl + a + b;
-    const float ref = __shfl_sync(0xffffffffu, g1, 15);  // row 31
-    const float gl = __shfl_sync(0xffffffffu, g1, 31);   // row 63
-    float m = fmaxf(fabsf(g0 - ref), fabsf(g1 - ref));
+  for (int i = 0; i < 16; ++i) x[i] += off;
+  if (qt == 1) G.ref[c] = x[15];  // row 31
+  if (qt == 3) G.gl[c] = x[15];   // row 63
+  __syncthreads();
+  const float ref = G.ref[c];
+  float m = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    G.E[(2 * lane) * LDG + c] = STORE_GC ? g0 : __expf(g0 - ref);
-    G.E[(2 * lane + 1) * LDG + c] = STORE_GC ? g1 : __expf(g1 - ref);
-    if (lane == 0) {
-      G.ref[c] = ref;
-      G.gl[c] = gl;
-      G.eref[c] = __expf(ref);
-      G.egl[c] = __expf(gl - ref);
-      atomicMax(&G.span_bits, __float_as_uint(m));
-    }
+  for (int i = 0; i < 16; ++i) {
+    m = fmaxf(m, fabsf(x[i] - ref));
+    G.E[(16 * qt + i) * LDG + c] = STORE_GC ? x[i] : __expf(x[i] - ref);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((tid & 31) == 0) atomicMax(&G.span_bits, __float_as_uint(m));
+  if (qt == 0) {
+    G.eref[c] = __expf(ref);
+    G.egl[c] = __expf(G.gl[c] - ref);
   }
   __syncthreads();
 }
@@ -216,6 +220,34 @@ __device__ __forceinline__ void mma64(uint32_t d, const void* a, int a_mn, const
     const uint64_t da = a_mn ? desc_mnmajor(a, D, s) : desc_kmajor(a, D, s);
     const uint64_t db = b_mn ? desc_mnmajor(b, D, s) : desc_kmajor(b, D, s);
     mma_f16(d, da, db, idesc, (accumulate || s > 0) ? 1u : 0u);
+  }
+}
+
+// Gate the staged q and k tiles in one pass: Q^ = scale q E, K^ = k / E (optionally keeping
+// the raw tiles).
+template <typename T>
+__device__ __forceinline__ void gate_qk(unsigned char* sQ, unsigned char* sK, const GateSmem& G, float scale,
+                                        unsigned char* rawQ, unsigned char* rawK) {
+  for (int e = threadIdx.x; e < BT * (D / 8); e += NT) {
+    const int r = e >> 3, c = (e & 7) * 8;
+    uint4* pq = reinterpret_cast<uint4*>(sQ + blk_off(r, c, D));
+    uint4* pk = reinterpret_cast<uint4*>(sK + blk_off(r, c, D));
+    const uint4 uq = *pq, uk = *pk;
+    if (rawQ) {
+      *reinterpret_cast<uint4*>(rawQ + blk_off(r, c, D)) = uq;
+      *reinterpret_cast<uint4*>(rawK + blk_off(r, c, D)) = uk;
+    }
+    const T* xq = reinterpret_cast<const T*>(&uq);
+    const T* xk = reinterpret_cast<const T*>(&uk);
+    float yq[8], yk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float e = G.E[r * LDG + c + i];
+      yq[i] = ldf(xq + i) * (scale * e);
+      yk[i] = __fdividef(ldf(xk + i), e);
+    }
+    *pq = pack8<T>(yq);
+    *pk = pack8<T>(yk);
   }
 }
 
@@ -315,6 +347,17 @@ __global__ void __launch_bounds__(NT) tc_fwd_o_kernel(
   stage_tile<T>(sQ, q, t0, len, H, head);
   stage_tile<T>(sK, k, t0, len, H, head);
   stage_tile<T>(sV, v, t0, len, H, head);
+  // chunk-start state: fetched into registers while the tiles land
+  constexpr int SV = D * (D / 8) / NT;  // 8-float vectors per thread
+  float hreg[SV][8];
+  {
+    const float* hs = states + (cid * H + head) * (int64_t)D * D;
+#pragma unroll
+    for (int j = 0; j < SV; ++j) {
+      const int e = tid + j * NT;
+      load8(hs + (e >> 3) * D + (e & 7) * 8, hreg[j]);
+    }
+  }
   cp_async_wait_all();
   __syncthreads();
   gate_prep<Tg, false>(G, graw);
@@ -325,18 +368,13 @@ __global__ void __launch_bounds__(NT) tc_fwd_o_kernel(
     if (warp == 0) tmem_dealloc(tb, 128);
     return;
   }
-  gate_tile<T>(sQ, [&](int r, int c) { return scale * G.E[r * LDG + c]; });
-  gate_tile<T>(sK, [&](int r, int c) { return __fdividef(1.f, G.E[r * LDG + c]); });
-  {
-    const float* hs = states + (cid * H + head) * (int64_t)D * D;
-    for (int e = tid; e < D * (D / 8); e += NT) {
-      const int r = e >> 3, c = (e & 7) * 8;
-      float x[8];
-      load8(hs + r * D + c, x);
+  gate_qk<T>(sQ, sK, G, scale, nullptr, nullptr);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] *= G.eref[r];
-      store8_tile<T>(sH, r, c, x);
-    }
+  for (int j = 0; j < SV; ++j) {
+    const int e = tid + j * NT, r = e >> 3;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hreg[j][i] *= G.eref[r];
+    store8_tile<T>(sH, r, (e & 7) * 8, hreg[j]);
   }
   operands_ready();
   constexpr uint32_t F = Fmt<T>::v;
@@ -414,6 +452,16 @@ __global__ void __launch_bounds__(NT) tc_bwd_kernel(
   stage_tile<T>(sK, k, t0, len, H, head);
   stage_tile<T>(sV, v, t0, len, H, head);
   stage_tile<T>(sDO, dout, t0, len, H, head);
+  // chunk-start state and its adjoint: fetched into registers while the tiles land
+  constexpr int SV = D * (D / 8) / NT;  // 8-float vectors per thread
+  const int64_t soff = (cid * H + head) * (int64_t)D * D;
+  float hreg[SV][8], dhreg[SV][8];
+#pragma unroll
+  for (int j = 0; j < SV; ++j) {
+    const int e = tid + j * NT;
+    load8(states + soff + (e >> 3) * D + (e & 7) * 8, hreg[j]);
+    load8(dstates + soff + (e >> 3) * D + (e & 7) * 8, dhreg[j]);
+  }
   cp_async_wait_all();
   __syncthreads();
   gate_prep<Tg, false>(G, graw);
@@ -427,25 +475,21 @@ __global__ void __launch_bounds__(NT) tc_bwd_kernel(
   // raw q and k stay (blocked layout) in the gate staging area for dg = q dq - k dk
   unsigned char* rawQ = graw;
   unsigned char* rawK = graw + TILE;
-  gate_tile<T>(sQ, [&](int r, int c) { return scale * G.E[r * LDG + c]; }, rawQ);
-  gate_tile<T>(sK, [&](int r, int c) { return __fdividef(1.f, G.E[r * LDG + c]); }, rawK);
-  const int64_t soff = (cid * H + head) * (int64_t)D * D;
-  for (int e = tid; e < D * (D / 8); e += NT) {
-    const int r = e >> 3, c = (e & 7) * 8;
-    float h[8], dh[8];
-    load8(states + soff + r * D + c, h);
-    load8(dstates + soff + r * D + c, dh);
+  gate_qk<T>(sQ, sK, G, scale, rawQ, rawK);
+#pragma unroll
+  for (int j = 0; j < SV; ++j) {
+    const int e = tid + j * NT, r = e >> 3, c = (e & 7) * 8;
     float hd = 0.f;
     const float er = G.eref[r], egl = G.egl[r];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      hd = fmaf(h[i], dh[i], hd);
-      h[i] *= er;
-      dh[i] *= egl;
+      hd = fmaf(hreg[j][i], dhreg[j][i], hd);
+      hreg[j][i] *= er;
+      dhreg[j][i] *= egl;
     }
     atomicAdd(&s_hdh[r], hd);
-    store8_tile<T>(sH, r, c, h);
-    store8_tile<T>(sDH, r, c, dh);
+    store8_tile<T>(sH, r, c, hreg[j]);
+    store8_tile<T>(sDH, r, c, dhreg[j]);
   }
   operands_ready();
   constexpr uint32_t F = Fmt<T>::v;
