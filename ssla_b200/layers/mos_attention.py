@@ -1,0 +1,114 @@
+"""MoS attention (layers/mos_attention.py:12-199): pixel events are replicated into the kxk
+patches around them, projected per patch position, run through the gated scan along each
+patch's time-ordered event sequence, projected back per position and summed onto their pixel
+events, then residual + LayerNorm.  Parameter and buffer names match the reference so its
+state_dicts load unchanged.
+
+GPU work: routing (``scatter_group_events_to_patch``), the per-position projections, the scan
+(``ssla_scan_fwd/bwd``), and the deterministic gather-back (``ssla_index_add_rows``)."""
+from __future__ import annotations
+
+import math
+from typing import Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..ops.common.scan import scan
+from ..utils.async_utils import gather_patch_events_to_group, get_patch2pixel_lut, scatter_group_events_to_patch
+
+
+def _per_position_linear(x: torch.Tensor, pos_id: torch.Tensor, weights: torch.Tensor, out_features: int):
+    """y[r] = weights[pos_id[r]] @ x[r] (weights [P, out, in]); rows are grouped by position so
+    each position is one GEMM."""
+    P = weights.shape[0]
+    out = torch.empty((x.shape[0], out_features), device=x.device, dtype=torch.float32)
+    if P == 1:
+        return F.linear(x, weights[0])
+    order = torch.sort(pos_id, stable=True)[1]
+    counts = torch.bincount(pos_id, minlength=P).tolist()
+    start = 0
+    for i, n in enumerate(counts):
+        if n:
+            rows = order[start:start + n]
+            out[rows] = F.linear(x[rows], weights[i])
+        start += n
+    return out
+
+
+class MosAttention(nn.Module):
+    def __init__(self, input_size: int, hidden_size: int, frame_size: Tuple[int, int], kernel_size: Tuple[int, int],
+                 stride: Tuple[int, int] = (1, 1), scatter_proj: bool = True, gather_proj: bool = True):
+        super().__init__()
+        self.input_size = input_size
+        self.hidden_size = hidden_size
+        self.frame_size = frame_size
+        self.frame_output_size = frame_size
+        self.kernel_size = kernel_size
+        self.stride = stride
+        self.scatter_proj = scatter_proj
+        self.gather_proj = gather_proj
+        n_pos = kernel_size[0] * kernel_size[1]
+        self.register_parameter("scatter_conv_weights", nn.Parameter(
+            torch.zeros([n_pos if scatter_proj else 1, input_size * hidden_size], dtype=torch.float32)))
+        self.register_parameter("gather_conv_weights", nn.Parameter(
+            torch.zeros([n_pos if gather_proj else 1, hidden_size * hidden_size], dtype=torch.float32)))
+        self._initialize_weights()
+        self.q_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.v_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.g_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.o_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.norm = nn.LayerNorm(hidden_size)
+        lut = get_patch2pixel_lut(frame_size, kernel_size, stride)
+        self.register_buffer("patch2pixel_lut", lut)
+        self.register_buffer("patch_outcoord", torch.zeros([lut.shape[0], 2], dtype=torch.int))
+        self.input_proj = nn.Linear(input_size, hidden_size, bias=False) if input_size != hidden_size else None
+
+    @torch.no_grad()
+    def _initialize_weights(self):
+        std = math.sqrt(2.0 / (self.input_size + self.hidden_size))  # Xavier
+        self.scatter_conv_weights.normal_(0, std)
+        self.gather_conv_weights.normal_(0, std)
+
+    def forward(self, inputs):
+        residual = inputs["events"]
+        if residual.shape[0] != inputs["time"].shape[0]:
+            raise ValueError("events and time must have one row per event")
+        patch = scatter_group_events_to_patch(inputs, frame_size=self.frame_size, patch2pixel_lut=self.patch2pixel_lut,
+                                              kernel_size=tuple(self.kernel_size), stride=tuple(self.stride))
+        pos_id = patch["pos_id"]
+        x = self._apply_scatter_proj(patch["events"], pos_id)
+        q = self.q_proj(x)
+        v = self.v_proj(x)
+        g = torch.sigmoid(self.g_proj(x))
+        lengths = patch["lengths"]
+        cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
+        cu[1:] = lengths.cumsum(0)
+        h = scan(u=v, g=g, cu_seqlens=cu)
+        o = self.o_proj(q * h)
+        o = self._apply_gather_proj(o, pos_id)
+        out = gather_patch_events_to_group(o, patch["orig_event_idx"], num_pixel_events=residual.shape[0])
+        if self.input_proj is not None:
+            residual = self.input_proj(residual)
+        out = self.norm(out + residual)
+        return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
+                "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}
+
+    def _apply_scatter_proj(self, x, pos_id):
+        w = self.scatter_conv_weights.reshape(-1, self.hidden_size, self.input_size)
+        return _per_position_linear(x, pos_id, w, self.hidden_size)
+
+    def _apply_gather_proj(self, x, pos_id):
+        w = self.gather_conv_weights.reshape(-1, self.hidden_size, self.hidden_size)
+        return _per_position_linear(x, pos_id, w, self.hidden_size)
+
+    def compute_flops(self, inputs):
+        E = inputs["events"].shape[0]
+        P = E * self.kernel_size[0] * self.kernel_size[1]
+        C, I = self.hidden_size, self.input_size
+        flops = P * C * (2 * I - 1) + 3 * P * C * (2 * C - 1) + P * C * 4 + P * C * 2 + P * C
+        flops += P * C * (2 * C - 1) * 2 + P * C
+        flops += E * C * (2 * I - 1) if self.input_proj is not None else 0
+        flops += E * C + E * (8 * C + 1)
+        return flops

@@ -1,0 +1,32 @@
+"""Temporal dropout (layers/temporal_dropout.py:6-59): of each sequence of length L keep
+ceil(L / w) events, every w-th counted back from the last (the last event is always kept)."""
+from __future__ import annotations
+
+import torch
+
+from .async_sparse_module import AsyncSparseModule
+
+
+class TemporalDropout(AsyncSparseModule):
+    def __init__(self, window_size, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        if window_size <= 0:
+            raise ValueError("window_size must be greater than 0.")
+        self.window_size = window_size
+
+    def forward(self, inputs, grouped_events=True):
+        inputs = self.prepare_inputs(inputs, grouped_events)
+        lengths = inputs["lengths"]
+        w = self.window_size
+        dev = lengths.device
+        with torch.no_grad():
+            start = torch.cumsum(lengths, 0) - lengths
+            keep_n = torch.div(lengths + (w - 1), w, rounding_mode="floor")
+            seq = torch.repeat_interleave(torch.arange(lengths.numel(), device=dev), keep_n)
+            kstart = torch.cumsum(keep_n, 0) - keep_n
+            j = torch.arange(int(keep_n.sum()), device=dev) - kstart[seq]
+            first = torch.remainder(lengths - 1, w)  # offset of the first kept event
+            idx = start[seq] + first[seq] + j * w
+        return {"events": inputs["events"][idx], "time": inputs["time"][idx], "lengths": keep_n,
+                "batch_id": inputs["batch_id"], "h": inputs["h"], "w": inputs["w"],
+                "batch_size": inputs["batch_size"]}

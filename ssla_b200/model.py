@@ -1,0 +1,174 @@
+"""SSLA model runner on the ssla_b200 layers: event preprocessing, the layer stack built from a
+model config (the dict of configs/model/MOS_*.yaml), dense grids from the last event of every
+output cell, and the YOLOX detection head's inference decode.
+
+Mirrors model_mos.py:32-228 (get_module, get_modulelist, MosModel.forward / preprocess_inputs /
+async_event_to_grid) and the forward / decode of layers/yolox_head.py:96-258, with the same
+module and parameter names, so reference checkpoints load.  Training-only parts of the
+reference (SimOTA assignment and losses, Lightning hooks, COCO evaluation) are not part of this
+runner.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List
+
+import torch
+import torch.nn as nn
+
+from .layers import (LinearAttention, MosAttention, SparseAdaptiveAvgPool, SparseAdaptiveMaxPool, SparseAvgPool,
+                     SparseMaxPool, TemporalDropout)
+from .ops import segment as _seg
+from .utils.farsecnn_utils import group_events, truncate_packed_sequence
+
+FRAME_SIZES = {"Gen1": ((240, 304), 2), "NCaltech101": ((180, 240), 101)}
+
+
+def get_module(cfg: Dict, frame_size, channel_size: int) -> nn.Module:
+    """One layer from its config entry (model_mos.py:32-86)."""
+    name = cfg["name"]
+    if name == "SparseMaxPool":
+        return SparseMaxPool(frame_size, kernel_size=[cfg["kernel_size"]] * 2)
+    if name == "SparseAvgPool":
+        return SparseAvgPool(frame_size, kernel_size=[cfg["kernel_size"]] * 2)
+    if name == "SparseAdaptiveMaxPool":
+        return SparseAdaptiveMaxPool(frame_size, [cfg["output_size"]] * 2)
+    if name == "SparseAdaptiveAvgPool":
+        return SparseAdaptiveAvgPool(frame_size, [cfg["output_size"]] * 2)
+    if name == "TemporalDropout":
+        return TemporalDropout(cfg["window_size"], frame_size)
+    if name == "MosAttention":
+        k = cfg["kernel_size"]
+        return MosAttention(input_size=channel_size, hidden_size=cfg["hidden_size"], frame_size=frame_size,
+                            kernel_size=[min(k, frame_size[0]), min(k, frame_size[1])],
+                            scatter_proj=cfg.get("scatter_proj", True), gather_proj=cfg.get("gather_proj", True))
+    if name == "LinearAttention":
+        return LinearAttention(input_size=channel_size, hidden_size=cfg["hidden_size"], frame_size=frame_size)
+    raise ValueError("Module does not exist: ", name)
+
+
+def get_modulelist(config_layers, sensor_size, in_channels, expected_strides):
+    """Layer stack and its output taps (model_mos.py:89-122)."""
+    layers, strides, feature_sizes, grid_sizes, output_indices = [], [], [], [], []
+    grid_size, channel_size, stride = sensor_size, in_channels, 1
+    for i, cfg in enumerate(config_layers):
+        if cfg["name"] in ("SparseMaxPool", "SparseAvgPool"):
+            if stride in expected_strides:
+                strides.append(stride)
+                feature_sizes.append(channel_size)
+                grid_sizes.append(grid_size)
+                output_indices.append(i)
+            stride *= cfg["kernel_size"]
+        m = get_module(cfg, grid_size, channel_size)
+        layers.append(m)
+        grid_size = m.frame_output_size
+        channel_size = getattr(m, "hidden_size", channel_size)
+    if stride in expected_strides and stride not in strides:
+        strides.append(stride)
+        feature_sizes.append(channel_size)
+        grid_sizes.append(grid_size)
+        output_indices.append(len(layers) - 1)
+    return nn.ModuleList(layers), strides, feature_sizes, grid_sizes, output_indices
+
+
+def preprocess_inputs(events: torch.Tensor, lengths: torch.Tensor, frame_size, hot_pixel_thres: int = 50):
+    """<x, y, t, p> events -> pixel groups with per-event features <dt, p> (model_mos.py:173-209):
+    dt = time since the previous event of the pixel / 1e5, clamped to 1, 1 for the first event;
+    with hot_pixel_thres > 0 only the first `hot_pixel_thres` events of a pixel are kept."""
+    with torch.no_grad():
+        x = torch.cat([events[..., :3], events[..., 2:3], events[..., 3:]], dim=-1)
+        grouped = group_events((x, lengths), frame_size)
+        feats = grouped["events"].clone()
+        t = feats[:, 0]
+        dt = torch.empty_like(t)
+        dt[0:1] = t[0:1]
+        dt[1:] = t[1:] - t[:-1]
+        # tensor / tensor: IEEE division on every device (a scalar divisor may become a
+        # multiplication by its reciprocal)
+        dt = torch.clamp(dt / torch.full_like(dt, 1e5), max=1)
+        first = torch.cumsum(grouped["lengths"], 0) - grouped["lengths"]
+        dt[first] = 1
+        feats[:, 0] = dt
+        grouped["events"] = feats
+        if hot_pixel_thres > 0:
+            grouped["events"], grouped["lengths"], grouped["time"] = truncate_packed_sequence(
+                grouped["events"], grouped["lengths"], threshold=hot_pixel_thres, others=grouped["time"])
+    return grouped
+
+
+def async_event_to_grid(x, grid_size, channels: int) -> torch.Tensor:
+    """Dense (B, C, Hg, Wg) grid holding the last event of every occupied cell
+    (model_mos.py:212-228)."""
+    last = torch.cumsum(x["lengths"], 0) - 1
+    ev = x["events"][last]
+    Hg, Wg = grid_size
+    cell = x["batch_id"] * (Hg * Wg) + x["h"] * Wg + x["w"]
+    B = x["batch_size"]
+    grid = _seg.index_add_rows_ad(ev.float(), cell, B * Hg * Wg)
+    return grid.reshape(B, Hg, Wg, channels).permute(0, 3, 1, 2)
+
+
+class YOLOXHead(nn.Module):
+    """Inference part of the YOLOX head (layers/yolox_head.py:96-258): 1x1 conv stems and
+    predictors per level, decoded to (B, anchors, 4 + 1 + num_classes) boxes
+    (cx, cy, w, h in pixels; objectness and class logits)."""
+
+    def __init__(self, num_classes, strides, in_channels, width):
+        super().__init__()
+        self.num_classes = num_classes
+        self.strides = strides
+        self.cls_convs, self.reg_convs = nn.ModuleList(), nn.ModuleList()
+        self.cls_preds, self.reg_preds, self.obj_preds = nn.ModuleList(), nn.ModuleList(), nn.ModuleList()
+        stem = lambda c: nn.Sequential(nn.Conv2d(c, width, kernel_size=1), nn.BatchNorm2d(width), nn.SiLU())
+        for c in in_channels:
+            self.cls_convs.append(stem(c))
+            self.reg_convs.append(stem(c))
+            self.cls_preds.append(nn.Conv2d(width, num_classes, 1))
+            self.reg_preds.append(nn.Conv2d(width, 4, 1))
+            self.obj_preds.append(nn.Conv2d(width, 1, 1))
+        prior = -math.log((1 - 0.01) / 0.01)
+        with torch.no_grad():
+            for m in list(self.cls_preds) + list(self.obj_preds):
+                m.bias.fill_(prior)
+
+    def forward(self, xin: List[torch.Tensor]) -> torch.Tensor:
+        outs = []
+        for k, x in enumerate(xin):
+            cf = self.cls_convs[k](x)
+            rf = self.reg_convs[k](x)
+            o = torch.cat([self.reg_preds[k](rf), self.obj_preds[k](rf), self.cls_preds[k](cf)], 1)
+            B, C, Hh, Ww = o.shape
+            o = o.permute(0, 2, 3, 1).reshape(B, Hh * Ww, C).clone()
+            yv, xv = torch.meshgrid(torch.arange(Hh, device=o.device), torch.arange(Ww, device=o.device),
+                                    indexing="ij")
+            grid = torch.stack((xv, yv), 2).reshape(1, Hh * Ww, 2).to(o.dtype)
+            s = self.strides[k]
+            o[..., :2] = (o[..., :2] + grid) * s
+            o[..., 2:4] = torch.exp(o[..., 2:4]) * s
+            outs.append(o)
+        return torch.cat(outs, 1)
+
+
+class MosDetector(nn.Module):
+    """Preprocessing + layer stack + grids + head (MosModel.forward, model_mos.py:157-170)."""
+
+    def __init__(self, model_config: Dict, dataset: str = "Gen1", hot_pixel_thres: int = 50):
+        super().__init__()
+        self.frame_size, self.num_classes = FRAME_SIZES[dataset]
+        self.hot_pixel_thres = hot_pixel_thres
+        self.backbone, strides, feats, grids, outs = get_modulelist(
+            model_config["layers"], self.frame_size, 2, model_config.get("expected_strides", [8, 16]))
+        self.strides, self.in_features, self.grid_sizes, self.output_indices = strides, feats, grids, outs
+        self.head = YOLOXHead(self.num_classes, strides, feats, feats[-1])
+
+    def backbone_grids(self, events: torch.Tensor, lengths: torch.Tensor) -> List[torch.Tensor]:
+        x = preprocess_inputs(events, lengths, self.frame_size, self.hot_pixel_thres)
+        taps = []
+        for i, layer in enumerate(self.backbone):
+            x = layer(x)
+            if i in self.output_indices:
+                taps.append(x)
+        return [async_event_to_grid(t, self.grid_sizes[k], self.in_features[k]) for k, t in enumerate(taps)]
+
+    def forward(self, events: torch.Tensor, lengths: torch.Tensor) -> torch.Tensor:
+        return self.head(self.backbone_grids(events, lengths))

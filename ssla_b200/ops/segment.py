@@ -95,3 +95,72 @@ def index_add_rows(src: torch.Tensor, index: torch.Tensor, num_rows: int) -> tor
                                      C, out.data_ptr(), ws.data_ptr(), nb, _lib.stream_of(src)),
                "index_add_rows")
     return out
+
+
+# --------------------------------------------------------------------------- autograd wrappers
+class _GatherRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, src, index):
+        ctx.save_for_backward(index)
+        ctx.n = src.shape[0]
+        return gather_rows(src, index)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (index,) = ctx.saved_tensors
+        return index_add_rows(grad.contiguous(), index, ctx.n), None
+
+
+class _IndexAddRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, src, index, num_rows):
+        ctx.save_for_backward(index)
+        return index_add_rows(src, index, num_rows)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (index,) = ctx.saved_tensors
+        return gather_rows(grad.contiguous(), index), None, None
+
+
+class _SegmentReduce(torch.autograd.Function):
+    """Reduction with gradients: sum / mean broadcast the output gradient to the rows of each
+    segment (divided by the count for mean); max routes it to the arg-max row."""
+
+    @staticmethod
+    def forward(ctx, src, seg_of_row, offsets, rows, op):
+        out, arg = segment_reduce(src, offsets, rows, op, want_arg=(op == MAX))
+        ctx.op = op
+        ctx.shape = src.shape
+        ctx.save_for_backward(seg_of_row, offsets, arg if arg is not None else offsets)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        seg, offsets, arg = ctx.saved_tensors
+        R, C = ctx.shape
+        grad = grad.contiguous()
+        if ctx.op == MAX:
+            gin = torch.zeros((R + 1, C), device=grad.device, dtype=grad.dtype)  # row R: empty segments
+            gin.scatter_(0, arg, grad)
+            return gin[:R], None, None, None, None
+        g = gather_rows(grad, seg)
+        if ctx.op == MEAN:
+            cnt = (offsets[1:] - offsets[:-1]).clamp(min=1).to(grad.dtype)
+            g = g / gather_rows(cnt.view(-1, 1).contiguous(), seg)
+        return g, None, None, None, None
+
+
+def gather_rows_ad(src: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """Differentiable ``src[index]``."""
+    return _GatherRows.apply(src.contiguous(), _i64(index))
+
+
+def index_add_rows_ad(src: torch.Tensor, index: torch.Tensor, num_rows: int) -> torch.Tensor:
+    """Differentiable deterministic ``zeros(num_rows, C).index_add_(0, index, src)``."""
+    return _IndexAddRows.apply(src.contiguous(), _i64(index), int(num_rows))
+
+
+def segment_reduce_ad(src: torch.Tensor, seg_of_row: torch.Tensor, offsets: torch.Tensor, rows, op: int):
+    """Differentiable segment reduction; ``seg_of_row`` is the segment id of every row."""
+    return _SegmentReduce.apply(src.contiguous(), _i64(seg_of_row), offsets, rows, op)

@@ -29,7 +29,7 @@ def _prep(src, index, dim, dim_size):
 def scatter_sum(src, index, dim=-1, out=None, dim_size: Optional[int] = None):
     index, S = _prep(src, index, dim, dim_size)
     off, rows = _seg.segment_csr(index, S)
-    return _seg.segment_reduce(src, off, rows, _seg.SUM)[0]
+    return _seg.segment_reduce_ad(src, index, off, rows, _seg.SUM)
 
 
 scatter_add = scatter_sum
@@ -38,13 +38,14 @@ scatter_add = scatter_sum
 def scatter_mean(src, index, dim=-1, out=None, dim_size: Optional[int] = None):
     index, S = _prep(src, index, dim, dim_size)
     off, rows = _seg.segment_csr(index, S)
-    return _seg.segment_reduce(src, off, rows, _seg.MEAN)[0]
+    return _seg.segment_reduce_ad(src, index, off, rows, _seg.MEAN)
 
 
 def scatter_max(src, index, dim=-1, out=None, dim_size: Optional[int] = None):
     index, S = _prep(src, index, dim, dim_size)
     off, rows = _seg.segment_csr(index, S)
-    return _seg.segment_reduce(src, off, rows, _seg.MAX, want_arg=True)
+    arg = _seg.segment_reduce(src.detach(), off, rows, _seg.MAX, want_arg=True)[1]
+    return _seg.segment_reduce_ad(src, index, off, rows, _seg.MAX), arg
 
 
 def scatter(src, index, dim=-1, out=None, dim_size=None, reduce: str = "sum"):

@@ -1,0 +1,178 @@
+"""Sparse event routing on the GPU: pixel grouping, receptive-field / patch look-up tables and
+the pixel -> patch (or receptive field) event replication used by MoS attention and sparse
+pooling.
+
+Semantics follow the reference (utils/async_utils.py:10-264, utils/farsecnn_utils.py:8-265):
+the same dictionaries in and out, the same orderings and dtypes.  Where the reference uses an
+unstable ``torch.sort`` to order the events of a patch by time (utils/async_utils.py:221-222,
+utils/farsecnn_utils.py:246), ties are broken deterministically here by (look-up-table
+position, event order), i.e. the order the reference builds before sorting.
+
+Replication is done from the active pixel groups outwards: every group is expanded to the
+(patch, position) pairs whose receptive field contains it (at most kh*kw), those pairs are
+ordered by (patch, position), and events follow.  This touches O(groups * kh * kw) entries
+instead of the reference's dense [B * num_patches, kh * kw] masks.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Tuple
+
+import torch
+
+
+def compute_padding_1d(in_size: int, kernel_size: int, stride: int, mode: str = "same") -> int:
+    """Total padding so that out = ceil(in / stride) ('same') or so that every input is covered
+    at least once ('minimal') (utils/farsecnn_utils.py:67-73)."""
+    if mode == "same":
+        return math.ceil((math.ceil(in_size / stride) - 1) * stride + kernel_size - in_size)
+    if mode == "minimal":
+        return math.ceil((in_size - kernel_size) / stride) * stride - in_size + kernel_size
+    raise ValueError(f"unknown padding mode {mode!r}")
+
+
+def _geometry(frame_size, kernel_size, stride):
+    H, W = int(frame_size[0]), int(frame_size[1])
+    kh, kw = int(kernel_size[0]), int(kernel_size[1])
+    sh, sw = int(stride[0]), int(stride[1])
+    ph, pw = compute_padding_1d(H, kh, sh), compute_padding_1d(W, kw, sw)
+    oh = (H + ph - kh) // sh + 1
+    ow = (W + pw - kw) // sw + 1
+    return H, W, kh, kw, sh, sw, ph // 2, pw // 2, oh, ow
+
+
+def receptive_field_lut(frame_size, kernel_size, stride) -> Tuple[torch.Tensor, torch.Tensor]:
+    """([oh*ow, kh*kw] pixel ids (y*W + x, -1 outside the frame), [oh*ow, 2] output coords <x, y>)
+    with 'same' padding split floor/ceil before/after (utils/farsecnn_utils.py:95-128,
+    utils/async_utils.py:96-122)."""
+    H, W, kh, kw, sh, sw, pt, pl, oh, ow = _geometry(frame_size, kernel_size, stride)
+    oy = torch.arange(oh).view(oh, 1, 1, 1)
+    ox = torch.arange(ow).view(1, ow, 1, 1)
+    dy = torch.arange(kh).view(1, 1, kh, 1)
+    dx = torch.arange(kw).view(1, 1, 1, kw)
+    y = oy * sh - pt + dy
+    x = ox * sw - pl + dx
+    inside = (y >= 0) & (y < H) & (x >= 0) & (x < W)
+    lut = torch.where(inside, y * W + x, torch.full_like(y * W + x, -1)).reshape(oh * ow, kh * kw)
+    outcoord = torch.stack(torch.meshgrid(torch.arange(ow), torch.arange(oh), indexing="xy"), -1)
+    return lut.to(torch.int64), outcoord.reshape(oh * ow, 2).to(torch.int64)
+
+
+def group_events(inputs, frame_size, max_events_per_px: int = 512) -> Dict[str, torch.Tensor]:
+    """Group events [B, N, C] (rows <x, y, t, features...>, per-sample lengths) by pixel
+    (utils/farsecnn_utils.py:130-174, utils/async_utils.py:10-84): stable order by
+    (sample, pixel), at most the last `max_events_per_px` events of a pixel kept."""
+    events, lengths = inputs
+    events = events.float()
+    B, Nmax = events.shape[0], events.shape[1]
+    H, W = int(frame_size[0]), int(frame_size[1])
+    dev = events.device
+    lengths = lengths.to(dev)
+    mask = torch.arange(Nmax, device=dev).unsqueeze(0) < lengths.unsqueeze(1)
+    ev = events[mask]
+    batch_id = torch.arange(B, device=dev).repeat_interleave(lengths.to(torch.int64))
+    pid = batch_id * (H * W) + ev[:, 1].to(torch.int64) * W + ev[:, 0].to(torch.int64)
+    order = torch.sort(pid, stable=True)[1]
+    spid = pid[order]
+    _, gid, counts = torch.unique_consecutive(spid, return_inverse=True, return_counts=True)
+    ev = ev[order]
+    G = counts.numel()
+    first = torch.zeros(G, dtype=torch.int64, device=dev)
+    if G:
+        first[1:] = counts.cumsum(0)[:-1]
+    gr_lengths = counts.clamp(max=max_events_per_px)
+    skip = counts - gr_lengths
+    keep = torch.arange(int(gr_lengths.sum()), device=dev)
+    start_new = torch.zeros(G, dtype=torch.int64, device=dev)
+    if G:
+        start_new[1:] = gr_lengths.cumsum(0)[:-1]
+    grp = torch.repeat_interleave(torch.arange(G, device=dev), gr_lengths)
+    src = keep - start_new[grp] + first[grp] + skip[grp]
+    rep = first  # one representative event per group
+    kept = ev[src]
+    return {
+        "events": kept[:, 3:],
+        "time": kept[:, 2].to(torch.int64),
+        "batch_id": batch_id[order][rep],
+        "h": ev[rep, 1].to(torch.int64),
+        "w": ev[rep, 0].to(torch.int64),
+        "lengths": gr_lengths,
+        "batch_size": B,
+    }
+
+
+def truncate_packed_sequence(data: torch.Tensor, seqlens: torch.Tensor, threshold: int, others=None):
+    """Keep the first `threshold` rows of every packed sequence (utils/farsecnn_utils.py:8-33)."""
+    dev = data.device
+    starts = torch.cumsum(seqlens, 0) - seqlens
+    pos = torch.arange(data.shape[0], device=dev) - torch.repeat_interleave(starts, seqlens)
+    keep = pos < threshold
+    new_lengths = seqlens.clamp(max=threshold)
+    if others is not None:
+        return data[keep], new_lengths, others[keep]
+    return data[keep], new_lengths
+
+
+def replicate_to_fields(
+    gr_batch_id: torch.Tensor,
+    gr_h: torch.Tensor,
+    gr_w: torch.Tensor,
+    gr_lengths: torch.Tensor,
+    gr_time: torch.Tensor,
+    frame_size,
+    kernel_size,
+    stride,
+):
+    """Replicate the events of pixel groups into every receptive field (patch) containing the
+    pixel, and order each field's events by time.
+
+    Returns a dict with
+      field_id   [F]  global field index b * num_fields + f of each non-empty field (ascending)
+      lengths    [F]  events per non-empty field
+      src        [P]  index into the group-ordered event array of each replicated event
+      pos_id     [P]  look-up-table position (0 .. kh*kw-1) the event was taken from
+      time       [P]  its timestamp
+    with events sorted by (field, time, position, source order)."""
+    H, W, kh, kw, sh, sw, pt, pl, oh, ow = _geometry(frame_size, kernel_size, stride)
+    dev = gr_lengths.device
+    nf = oh * ow
+    G = gr_lengths.numel()
+    area = kh * kw
+    # candidate (group, position) pairs: field coordinate that sees pixel (y, x) at (dy, dx)
+    dy = torch.arange(kh, device=dev).repeat_interleave(kw)
+    dx = torch.arange(kw, device=dev).repeat(kh)
+    ny = gr_h.view(G, 1) + pt - dy.view(1, area)
+    nx = gr_w.view(G, 1) + pl - dx.view(1, area)
+    ok = (ny >= 0) & (nx >= 0) & (ny % sh == 0) & (nx % sw == 0)
+    oy, ox = ny // sh, nx // sw
+    ok &= (oy < oh) & (ox < ow)
+    gidx = torch.arange(G, device=dev).view(G, 1).expand(G, area)[ok]
+    pos = torch.arange(area, device=dev).view(1, area).expand(G, area)[ok]
+    fid = (gr_batch_id.view(G, 1) * nf + oy * ow + ox)[ok]
+    # order pairs by (field, position); pairs of one group with distinct positions are distinct
+    key = fid * area + pos
+    order = torch.sort(key, stable=True)[1]
+    gidx, pos, fid = gidx[order], pos[order], fid[order]
+    field_ids, per_pair_field = torch.unique_consecutive(fid, return_inverse=True)
+    reps = gr_lengths[gidx]
+    lengths = torch.zeros(field_ids.numel(), dtype=gr_lengths.dtype, device=dev)
+    lengths.scatter_add_(0, per_pair_field, reps)
+    # expand pairs to events (group order within a pair)
+    gstart = torch.cumsum(gr_lengths, 0) - gr_lengths
+    n_ev = int(reps.sum())
+    pair_of_ev = torch.repeat_interleave(torch.arange(gidx.numel(), device=dev), reps)
+    pair_start = torch.cumsum(reps, 0) - reps
+    within = torch.arange(n_ev, device=dev) - pair_start[pair_of_ev]
+    src = gstart[gidx][pair_of_ev] + within
+    t = gr_time[src]
+    fld = per_pair_field[pair_of_ev]
+    # stable time sort inside each field (pre-order: field, position, event)
+    stride_t = (t.max() + 1) if n_ev else torch.tensor(1, device=dev)
+    order = torch.sort(fld.to(torch.int64) * stride_t + t, stable=True)[1]
+    return {
+        "field_id": field_ids,
+        "lengths": lengths,
+        "src": src[order],
+        "pos_id": pos[pair_of_ev][order],
+        "time": t[order],
+    }

@@ -109,3 +109,38 @@ def test_segment_edge_cases():
     assert out.abs().sum() == 0 and (arg == 0).all()
     off, rows = seg.segment_csr(torch.tensor([2, 2, 0]).cuda(), 4)
     assert off.tolist() == [0, 1, 1, 3, 3] and rows[:3].tolist() == [2, 0, 1]
+
+
+def test_segment_op_gradients_match_torch():
+    """Backward of the differentiable gather / index_add / segment reductions against torch
+    autograd of the equivalent CPU operations."""
+    from ssla_b200 import torch_scatter as ts
+    from ssla_b200.ops import segment as seg
+
+    gen = torch.Generator().manual_seed(5)
+    R, S, C = 3000, 700, 8
+    idx = torch.randint(0, S, (R,), generator=gen)
+    src = torch.randn(R, C, generator=gen, dtype=torch.float64).float()
+    gout = torch.randn(S, C, generator=gen)
+    for name, ours, ref in (
+        ("sum", lambda x: ts.scatter_sum(x, idx.cuda(), dim=0, dim_size=S),
+         lambda x: torch.zeros(S, C).index_add(0, idx, x)),
+        ("mean", lambda x: ts.scatter_mean(x, idx.cuda(), dim=0, dim_size=S),
+         lambda x: torch.zeros(S, C).index_add(0, idx, x) / torch.bincount(idx, minlength=S).clamp(min=1)[:, None]),
+        ("max", lambda x: ts.scatter_max(x, idx.cuda(), dim=0, dim_size=S)[0],
+         lambda x: torch.zeros(S, C).scatter_reduce(0, idx[:, None].expand(R, C), x, "amax", include_self=False)),
+        ("index_add", lambda x: seg.index_add_rows_ad(x, idx.cuda(), S),
+         lambda x: torch.zeros(S, C).index_add(0, idx, x)),
+    ):
+        a = src.cuda().requires_grad_()
+        b = src.clone().requires_grad_()
+        ours(a).backward(gout.cuda())
+        ref(b).backward(gout)
+        assert torch.allclose(a.grad.cpu(), b.grad, atol=1e-6), name
+    gi = torch.randint(0, R, (900,), generator=gen)
+    a = src.cuda().requires_grad_()
+    b = src.clone().requires_grad_()
+    g2 = torch.randn(900, C, generator=gen)
+    seg.gather_rows_ad(a, gi.cuda()).backward(g2.cuda())
+    b[gi].backward(g2)
+    assert torch.allclose(a.grad.cpu(), b.grad, atol=1e-6)
