@@ -25,8 +25,8 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -67,44 +67,62 @@ def make_inputs(seed: int, device="cpu"):
 
 
 class Clocks:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event reasons sampled through NVML every 2 ms while the timed region
+    runs (a background thread), for the `clocks` field of the result line."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"ssla_clocks_{os.getpid()}.csv"
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, cuda_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(cuda_index)
+            try:
+                bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self._nv = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)))
+                r = int(get_reasons(self._h))
+                self.reasons |= {n for bit, n in self.REASONS.items() if r & bit}
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+        if self._h is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            self.proc.wait()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
 
     def summary(self):
-        try:
-            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()]
-        except OSError:
+        if not self.samples:
             return None
-        rows = [[c.strip() for c in r] for r in rows if len(r) >= 6]
-        if not rows:
-            return None
-        sm = sorted(float(r[0]) for r in rows)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, x in zip(names, r[2:6]) if x.lower() == "active"})
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][1]), "reasons": reasons,
-                "samples": len(rows)}
+        sm = sorted(self.samples)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(sm)}
 
 
 def peaks():
@@ -160,6 +178,218 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+    return world, rank, local, dev, dist
+
+
+def _max_over_ranks(x, dist, dev):
+    if dist is None:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def _event_time(fn, n, stream, flush=None):
+    """Sum of per-step CUDA-event times of `n` calls (optional L2 flush before each)."""
+    tot = 0.0
+    for _ in range(n):
+        if flush is not None:
+            flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / 1e3
+
+
+MODEL_B = 64  # BASELINE config 5: batch 64 split across ranks
+
+
+def bench_model(dev, world, rank, dist, steps=3, warmup=2, variant="S"):
+    """SSLA forward (preprocessing, layer stack, grids, YOLOX decode) on this rank's share of a
+    64-sample batch of synthetic 100 ms / 240x304 event streams, then one NCCL all_gather of the
+    detections.  Returns frames/s for the whole batch (strong scaling) on rank 0."""
+    import yaml  # noqa: F401  (configs are spelled out below)
+
+    from ssla_b200.distributed import gather_outputs, shard_range
+    from ssla_b200.model import MosDetector
+    from ssla_b200.synthetic import event_batch, seeded_parameters
+
+    hidden = {"S": (12, 24, 48, 96), "L": (32, 64, 128, 256)}[variant]
+    layers = []
+    for lvl, c in enumerate(hidden):
+        layers += [{"name": "MosAttention", "kernel_size": 1 if lvl == 0 else 3, "hidden_size": c},
+                   {"name": "MosAttention", "kernel_size": 3, "hidden_size": c}]
+        if lvl < 3:
+            layers += [{"name": "SparseMaxPool", "kernel_size": 2}, {"name": "TemporalDropout", "window_size": 4}]
+    cfg = {"name": f"MOS_{variant}", "expected_strides": [8], "layers": layers}
+    torch.manual_seed(0)
+    m = MosDetector(cfg).to(dev).eval()
+    seeded_parameters(m, 2025)
+    a, b = shard_range(MODEL_B, rank, world)
+    ev, ln = event_batch(MODEL_B, seed=11)
+    ev_h, ln_h = ev[a:b].pin_memory(), ln[a:b]
+    n_events = int(ln.sum())
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        with torch.no_grad():
+            out = m(ev_h.to(dev, non_blocking=True), ln_h.to(dev))
+            return gather_outputs(out)
+
+    for _ in range(warmup):
+        step()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    secs = _max_over_ranks(_event_time(step, steps, stream), dist, dev)
+    return {"metric": f"SSLA-{variant} forward frames/s", "value": MODEL_B * steps / secs, "unit": "frames/s",
+            "events_per_s": n_events * steps / secs, "ms_per_batch": 1e3 * secs / steps, "batch": MODEL_B,
+            "per_rank_batch": b - a, "scaling": "strong", "steps": steps, "warmup": warmup,
+            "includes": "host->device event copy, preprocessing, 14 layers, grids, head decode, NCCL gather",
+            "data": "synthetic 20 bins x 5 ms, 2% occupancy, uniform + 20 Gaussian blobs"}
+
+
+def run_other(args):
+    world, rank, local, dev, dist = _dist_env()
+    stream = torch.cuda.current_stream(dev)
+    hbm, which = peaks()
+    if args.workload == "model":
+        line = bench_model(dev, world, rank, dist, steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            line.update({"n_gpus": world, "higher_is_better": True, "vs_baseline": None, "dtype": "f32",
+                         "config": {"workload": "SSLA-S forward, batch 64 split across ranks (BASELINE config 5)"}})
+            print(json.dumps(line), flush=True)
+    elif args.workload == "recurrent":
+        from ssla_b200 import _lib
+
+        L = _lib.load()
+        N, Hh, Kk, Vv, Tt = 65536, 4, 32, 32, 20
+        gen = torch.Generator().manual_seed(3 + rank)
+        mk = lambda d: torch.randn(Tt, N, Hh, d, generator=gen).to(torch.bfloat16).to(dev)
+        q, k, v = mk(Kk), mk(Kk), mk(Vv)
+        g = (F.logsigmoid(torch.randn(Tt, N, Hh, Kk, generator=gen)) / 16).to(torch.bfloat16).to(dev)
+        o = torch.empty(Tt, N, Hh, Vv, device=dev, dtype=torch.bfloat16)
+        st = [torch.zeros(N, Hh, Kk, Vv, device=dev), torch.empty(N, Hh, Kk, Vv, device=dev)]
+        cu = torch.arange(N + 1, device=dev)
+        sp = stream.cuda_stream
+        it = [0]
+
+        def step():
+            t = it[0] % Tt
+            src, dst = st[it[0] % 2], st[(it[0] + 1) % 2]
+            _lib.check(L.ssla_recurrent_gla_fwd(q[t].data_ptr(), k[t].data_ptr(), v[t].data_ptr(), g[t].data_ptr(),
+                                                _lib.BF16, _lib.BF16, cu.data_ptr(), N, N, Hh, Kk, Vv, Kk ** -0.5,
+                                                src.data_ptr(), o[t].data_ptr(), dst.data_ptr(), sp), "recurrent")
+            it[0] += 1
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        with Clocks(local) as clk:
+            secs = _max_over_ranks(_event_time(step, args.steps, stream), dist, dev)
+        bytes_step = 2 * N * Hh * Kk * Vv * 4 + N * Hh * (3 * Kk + 2 * Vv) * 2
+        if rank == 0:
+            gbs = bytes_step * args.steps / secs / 1e9
+            cpu = None
+            if not args.no_cpu_baseline and world == 1:
+                from oracle.gla import naive_gla_recurrent
+
+                torch.set_num_threads(os.cpu_count() or 1)
+                n_s = 4096
+                qs, ks, vs, gs = (x[0, :n_s].float().cpu() for x in (q, k, v, g))
+                t0 = time.perf_counter()
+                naive_gla_recurrent(qs, ks, vs, gs, torch.arange(n_s + 1), initial_state=torch.zeros(n_s, Hh, Kk, Vv),
+                                    output_final_state=True)
+                cpu = {"value": n_s / (time.perf_counter() - t0), "unit": "tokens/s", "cores": os.cpu_count(),
+                       "kind": "port", "sample": f"one streaming step of {n_s} sequences"}
+            print(json.dumps({
+                "metric": "fused_recurrent_gla streaming tokens/s", "value": world * N * args.steps / secs,
+                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "BASELINE config 3: 65536 sequences x H=4, K=V=32, one token per call, "
+                                       "fp32 state carried (ping-pong buffers), T=20 steps cycled",
+                           "l2": "state 1 GiB per buffer > L2"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                             "peak_source": which, "alg_bytes_per_step": bytes_step, "traffic": None},
+                "gpu_launches": args.steps, "cpu_baseline": cpu, "clocks": clk.summary()}), flush=True)
+    elif args.workload == "pool":
+        from ssla_b200.ops import segment as seg
+        from ssla_b200.synthetic import pooling_rows
+
+        feats, idx, cells = pooling_rows(seed=rank)
+        feats = feats.to(dev)
+        R, C = feats.shape
+        lines = {}
+        flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+        for kk in (2, 4):
+            inv, S = cells[kk]
+            inv = inv.to(dev)
+            holder = {}
+
+            def step():
+                off = seg.segment_offsets_sorted(inv, S)
+                mx, _ = seg.segment_reduce(feats, off, None, seg.MAX)
+                mn, _ = seg.segment_reduce(feats, off, None, seg.MEAN)
+                holder["back"] = seg.gather_rows(mx, inv)
+                holder["mean"] = mn
+
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize(dev)
+            secs = _max_over_ranks(_event_time(step, args.steps, stream, flush), dist, dev)
+            b_scatter = R * C * 2 + R * 8 + S * C * 2
+            b_gather = S * C * 2 + R * 8 + R * C * 2
+            alg = 2 * b_scatter + b_gather
+            gbs = alg * args.steps / secs / 1e9
+            lines[f"k{kk}"] = {"rows": R, "cells": S, "ms_per_step": 1e3 * secs / args.steps,
+                               "rows_per_s": world * R * args.steps / secs, "achieved_gbs": gbs, "frac": gbs / hbm,
+                               "alg_bytes_per_step": alg}
+        if rank == 0:
+            cpu = None
+            if not args.no_cpu_baseline and world == 1:
+                from oracle.segment import scatter_max, scatter_mean
+
+                torch.set_num_threads(os.cpu_count() or 1)
+                inv, S = cells[2]
+                f = feats.float().cpu()
+                t0 = time.perf_counter()
+                mx, _ = scatter_max(f, inv, S)
+                scatter_mean(f, inv, S)
+                mx[inv]
+                cpu = {"value": R / (time.perf_counter() - t0), "unit": "rows/s", "cores": os.cpu_count(),
+                       "kind": "port", "sample": "k=2 max + mean + gather back, all rows"}
+            k2 = lines["k2"]
+            print(json.dumps({
+                "metric": "sparse pooling rows/s (scatter max + mean + gather back, k=2)",
+                "value": k2["rows_per_s"], "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": k2["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "BASELINE config 4: 16 batches x 2 polarity planes at 240x304, ~5% active "
+                                       "pixels, Poisson(3) events, C=64 bf16", "l2": "flushed before every step",
+                           "per_k": lines},
+                "roofline": {"bound": "hbm", "achieved": k2["achieved_gbs"], "peak": hbm, "unit": "GB/s",
+                             "frac": k2["frac"], "peak_source": which, "alg_bytes_per_step": k2["alg_bytes_per_step"],
+                             "traffic": None},
+                "gpu_launches": 4 * args.steps, "cpu_baseline": cpu}), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -167,9 +397,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="chunk", choices=["chunk", "recurrent", "pool", "model"],
+                    help="chunk: headline (BASELINE config 2); recurrent: config 3; pool: config 4; "
+                         "model: config 5 frames/s")
+    ap.add_argument("--no-model", action="store_true", help="skip the SSLA-S frames/s field of the headline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "chunk":
+        return run_other(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -285,6 +521,7 @@ def main():
     e2e_secs = max_over_ranks(timed(e2e_step, args.steps))
     e2e_value = world * TOKENS * args.steps / e2e_secs
 
+    model_line = None if args.no_model else bench_model(dev, world, rank, dist, steps=3, warmup=2)
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -313,6 +550,7 @@ def main():
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
+        "ssla_s": model_line,
     }
     print(json.dumps(line), flush=True)
     if dist is not None:
