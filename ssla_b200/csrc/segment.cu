@@ -137,18 +137,20 @@ template <> __device__ __forceinline__ float lowest_of<float>() { return -FLT_MA
 template <> __device__ __forceinline__ float lowest_of<__nv_bfloat16>() { return -3.38953139e38f; }
 template <> __device__ __forceinline__ float lowest_of<__half>() { return -65504.f; }
 
-// Thread per (segment, VEC channels).  op: 0 sum, 1 mean, 2 max.
+// Block = (CV channel vectors) x (segments): threadIdx.x picks VEC channels, threadIdx.y the
+// segment, so a warp reads whole rows of consecutive segments and no index division is needed.
+// Rows are visited in ascending order; loads are issued 8 rows at a time (predicated), then
+// combined in row order.  op: 0 sum, 1 mean, 2 max.
 template <typename T, int VEC, int OP>
 __global__ void __launch_bounds__(256) reduce_kernel(const T* __restrict__ src,
                                                      const int64_t* __restrict__ off,
                                                      const int64_t* __restrict__ rows, int64_t R,
                                                      int64_t S, int64_t C, T* __restrict__ out,
                                                      int64_t* __restrict__ arg) {
-  const int64_t CV = C / VEC;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= S * CV) return;
-  const int64_t s = idx / CV;
-  const int64_t c = (idx - s * CV) * VEC;
+  constexpr int U = 4;
+  const int64_t s = (int64_t)blockIdx.x * blockDim.y + threadIdx.y;
+  if (s >= S) return;
+  const int64_t c = (int64_t)threadIdx.x * VEC;
   const int64_t b = off[s], e = off[s + 1];
   float acc[VEC];
   int64_t am[VEC];
@@ -158,19 +160,103 @@ __global__ void __launch_bounds__(256) reduce_kernel(const T* __restrict__ src,
     acc[i] = OP == 2 ? lo : 0.f;
     am[i] = R;
   }
-  for (int64_t p = b; p < e; ++p) {
-    const int64_t r = rows ? rows[p] : p;
-    float x[VEC];
-    Vec<T, VEC>::load(src + r * C + c, x);
+  for (int64_t p = b; p < e; p += U) {
+    float x[U][VEC];
+    int64_t rr[U];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      if (OP == 2) {
-        if (x[i] > acc[i]) { acc[i] = x[i]; am[i] = r; }
-      } else {
-        acc[i] = __fadd_rn(acc[i], x[i]);
+    for (int u = 0; u < U; ++u) {
+      if (p + u < e) {
+        rr[u] = rows ? rows[p + u] : p + u;
+        Vec<T, VEC>::load(src + rr[u] * C + c, x[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (p + u < e) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          if (OP == 2) {
+            if (x[u][i] > acc[i]) { acc[i] = x[u][i]; am[i] = rr[u]; }
+          } else {
+            acc[i] = __fadd_rn(acc[i], x[u][i]);
+          }
+        }
       }
     }
   }
+  if (OP == 1) {
+    const float cnt = (float)(e - b > 0 ? e - b : 1);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = __fdiv_rn(acc[i], cnt);
+  }
+  if (OP == 2) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i)
+      if (acc[i] == lo) acc[i] = 0.f;
+    if (arg) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) arg[s * C + c + i] = am[i];
+    }
+  }
+  Vec<T, VEC>::store(out + s * C + c, acc);
+}
+
+// Sorted segments (rows == nullptr): a block owns 256 / CV consecutive segments, whose rows
+// are one contiguous byte range.  The range is staged into shared memory with coalesced 16-byte
+// loads (all issued before any is consumed), in windows of at most `win_rows` rows; each thread
+// then reduces its (segment, channel vector) from shared memory in ascending row order.
+template <typename T, int VEC, int OP>
+__global__ void __launch_bounds__(256) reduce_sorted_tiled_kernel(const T* __restrict__ src,
+                                                                  const int64_t* __restrict__ off,
+                                                                  int64_t R, int64_t S, int64_t C,
+                                                                  int win_rows, T* __restrict__ out,
+                                                                  int64_t* __restrict__ arg) {
+  extern __shared__ uint4 stage4[];
+  const T* stage = reinterpret_cast<const T*>(stage4);
+  const int CV = (int)(C / VEC);
+  const int segs = 256 / CV;
+  const int64_t s0 = (int64_t)blockIdx.x * segs;
+  const int tid = threadIdx.x;
+  const int js = tid / CV, jv = tid - js * CV;
+  const int64_t s = s0 + js;
+  const bool mine = js < segs && s < S;
+  const int64_t sl = (s0 + segs < S) ? s0 + segs : S;
+  const int64_t r0 = off[s0], r1 = off[sl];
+  int64_t b = 0, e = 0;
+  if (mine) { b = off[s]; e = off[s + 1]; }
+  const int64_t c = (int64_t)jv * VEC;
+  float acc[VEC];
+  int64_t am[VEC];
+  const float lo = lowest_of<T>();
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    acc[i] = OP == 2 ? lo : 0.f;
+    am[i] = R;
+  }
+  const int64_t row16 = C * (int64_t)sizeof(T) / 16;  // 16-byte words per row
+  for (int64_t w0 = r0; w0 < r1; w0 += win_rows) {
+    const int64_t w1 = (w0 + win_rows < r1) ? w0 + win_rows : r1;
+    const int64_t n16 = (w1 - w0) * row16;
+    const uint4* g4 = reinterpret_cast<const uint4*>(src + w0 * C);
+    __syncthreads();
+    for (int64_t i = tid; i < n16; i += 256) stage4[i] = __ldg(g4 + i);
+    __syncthreads();
+    const int64_t pb = b > w0 ? b : w0, pe = e < w1 ? e : w1;
+    for (int64_t p = pb; p < pe; ++p) {
+      float x[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = ldf(stage + (p - w0) * C + c + i);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        if (OP == 2) {
+          if (x[i] > acc[i]) { acc[i] = x[i]; am[i] = p; }
+        } else {
+          acc[i] = __fadd_rn(acc[i], x[i]);
+        }
+      }
+    }
+  }
+  if (!mine) return;
   if (OP == 1) {
     const float cnt = (float)(e - b > 0 ? e - b : 1);
 #pragma unroll
@@ -205,18 +291,44 @@ __global__ void __launch_bounds__(256) gather_kernel(const T* __restrict__ src,
 template <typename T>
 int run_reduce(const void* src, const int64_t* off, const int64_t* rows, int64_t R, int64_t S,
                int64_t C, int op, void* out, int64_t* arg, cudaStream_t s) {
+  if (S == 0 || C == 0) return SSLA_OK;
   const bool v4 = C % 4 == 0 && aligned_to(src, 4 * sizeof(T)) && aligned_to(out, 4 * sizeof(T));
-  const int64_t threads = S * (v4 ? C / 4 : C);
-  if (threads == 0) return SSLA_OK;
-  const int grid = ceil_div(threads, 256);
-#define SSLA_RED(VEC, OP) \
-  reduce_kernel<T, VEC, OP><<<grid, 256, 0, s>>>((const T*)src, off, rows, R, S, C, (T*)out, arg)
-  if (v4) {
-    if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
-  } else {
-    if (op == 0) SSLA_RED(1, 0); else if (op == 1) SSLA_RED(1, 1); else SSLA_RED(1, 2);
+  const int64_t CV = v4 ? C / 4 : C;
+  if (CV > 256) {
+    set_error("ssla_segment_reduce: C=%lld too wide (at most %d)", (long long)C, v4 ? 1024 : 256);
+    return SSLA_ERR_UNSUPPORTED;
   }
+  const int segs = (int)(256 / CV);
+  const unsigned grid = (unsigned)ceil_div(S, segs);
+  const bool tiled = rows == nullptr && (C * (int64_t)sizeof(T)) % 16 == 0 && aligned_to(src, 16);
+  if (tiled) {
+    constexpr int kStageBytes = 48 * 1024;
+    const int win = (int)(kStageBytes / (C * (int64_t)sizeof(T)));
+    if (win < 1) {
+      set_error("ssla_segment_reduce: row of %lld bytes exceeds the staging buffer", (long long)(C * sizeof(T)));
+      return SSLA_ERR_UNSUPPORTED;
+    }
+    const size_t smem = (size_t)win * C * sizeof(T);
+#define SSLA_RED(VEC, OP)                                                                   \
+  reduce_sorted_tiled_kernel<T, VEC, OP><<<grid, 256, smem, s>>>((const T*)src, off, R, S, C, win, \
+                                                                 (T*)out, arg)
+    if (v4) {
+      if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
+    } else {
+      if (op == 0) SSLA_RED(1, 0); else if (op == 1) SSLA_RED(1, 1); else SSLA_RED(1, 2);
+    }
 #undef SSLA_RED
+  } else {
+    const dim3 block((unsigned)CV, (unsigned)segs);
+#define SSLA_RED(VEC, OP) \
+  reduce_kernel<T, VEC, OP><<<grid, block, 0, s>>>((const T*)src, off, rows, R, S, C, (T*)out, arg)
+    if (v4) {
+      if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
+    } else {
+      if (op == 0) SSLA_RED(1, 0); else if (op == 1) SSLA_RED(1, 1); else SSLA_RED(1, 2);
+    }
+#undef SSLA_RED
+  }
   SSLA_CHECK_LAUNCH("ssla_segment_reduce");
   return SSLA_OK;
 }

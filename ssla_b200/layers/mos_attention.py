@@ -4,8 +4,17 @@ patch's time-ordered event sequence, projected back per position and summed onto
 events, then residual + LayerNorm.  Parameter and buffer names match the reference so its
 state_dicts load unchanged.
 
-GPU work: routing (``scatter_group_events_to_patch``), the per-position projections, the scan
-(``ssla_scan_fwd/bwd``), and the deterministic gather-back (``ssla_index_add_rows``)."""
+Per-position projections without masks: a pixel event sits at a given position of exactly one
+patch, so
+  * scatter projection: Y_j = x W_j^T for all positions j is one batched GEMM over the pixel
+    events, and the patch rows are the gather Y[pos, src] (the routing gather itself);
+  * gather projection + gather-back: out[e] = sum_j W_j o[row(e, j)] is one GEMM of the
+    [E, positions * C] buffer of patch outputs (deterministic scatter, zeros where a position
+    has no patch) with the concatenated weights.
+The reference does 9 boolean-masked F.linear calls per projection and an atomics-based
+index_add_ (layers/mos_attention.py:148-167, utils/async_utils.py:262-263).  GPU work:
+routing (ssla_b200.utils.routing), GEMMs (cuBLAS), the scan (``ssla_scan_fwd/bwd``) and row
+gathers (``ssla_gather_rows``)."""
 from __future__ import annotations
 
 import math
@@ -16,7 +25,9 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..ops.common.scan import scan
-from ..utils.async_utils import gather_patch_events_to_group, get_patch2pixel_lut, scatter_group_events_to_patch
+from ..ops.segment import gather_rows_ad, index_add_rows_ad
+from ..utils.async_utils import get_patch2pixel_lut
+from ..utils.routing import replicate_to_fields
 
 
 def _per_position_linear(x: torch.Tensor, pos_id: torch.Tensor, weights: torch.Tensor, out_features: int):
@@ -75,20 +86,34 @@ class MosAttention(nn.Module):
         residual = inputs["events"]
         if residual.shape[0] != inputs["time"].shape[0]:
             raise ValueError("events and time must have one row per event")
-        patch = scatter_group_events_to_patch(inputs, frame_size=self.frame_size, patch2pixel_lut=self.patch2pixel_lut,
-                                              kernel_size=tuple(self.kernel_size), stride=tuple(self.stride))
-        pos_id = patch["pos_id"]
-        x = self._apply_scatter_proj(patch["events"], pos_id)
+        r = replicate_to_fields(inputs["batch_id"], inputs["h"], inputs["w"], inputs["lengths"], inputs["time"],
+                                self.frame_size, tuple(self.kernel_size), tuple(self.stride))
+        src, pos_id = r["src"], r["pos_id"]
+        E = residual.shape[0]
+        C = self.hidden_size
+        # scatter projection: all positions at once on the pixel events, then the routing gather
+        ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
+        P = ws.shape[0]
+        y = torch.matmul(residual.unsqueeze(0), ws.transpose(1, 2))  # [P, E, C]
+        key = src if P == 1 else pos_id * E + src
+        x = gather_rows_ad(y.reshape(P * E, C), key)
         q = self.q_proj(x)
         v = self.v_proj(x)
         g = torch.sigmoid(self.g_proj(x))
-        lengths = patch["lengths"]
+        lengths = r["lengths"]
         cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
         cu[1:] = lengths.cumsum(0)
         h = scan(u=v, g=g, cu_seqlens=cu)
         o = self.o_proj(q * h)
-        o = self._apply_gather_proj(o, pos_id)
-        out = gather_patch_events_to_group(o, patch["orig_event_idx"], num_pixel_events=residual.shape[0])
+        # gather projection + gather-back: [E, P, C] buffer of patch outputs, one GEMM
+        wg = self.gather_conv_weights.reshape(-1, C, C)
+        Pg = wg.shape[0]
+        if Pg == 1:
+            out = index_add_rows_ad(o, src, E) @ wg[0].t()
+        else:
+            z = torch.zeros((E * Pg, C), device=o.device, dtype=o.dtype)
+            z = z.index_put((src * Pg + pos_id,), o)  # unique (event, position) pairs
+            out = z.view(E, Pg * C) @ wg.permute(0, 2, 1).reshape(Pg * C, C)
         if self.input_proj is not None:
             residual = self.input_proj(residual)
         out = self.norm(out + residual)
