@@ -1,12 +1,14 @@
 // Tensor-core (tcgen05 / TMEM) kernels of the chunked GLA path for 16-bit inputs, K = V = 64.
 //
-// One CTA of 256 threads (8 warps) owns one (64-token chunk, head).  TMEM is allocated first
-// (allocating after outstanding loads was measured to serialise the CTAs of an SM); input
-// tiles are then copied with cp.async straight into 16-bit operand tiles in shared memory
-// ("8x8 blocked", see tc_util.cuh) and gated in place; one thread issues 64x64x16
-// tcgen05.mma instructions into fp32 TMEM accumulators; the epilogue reads TMEM with
-// tcgen05.ld.  An M=64 accumulator occupies lanes 0-15 of each of the four TMEM
-// subpartitions; warps w and w+4 share subpartition w and split the accumulator's columns.
+// Work item = (64-token chunk, head).  Every kernel is persistent: a CTA of 512 threads
+// (16 warps) walks items blockIdx.x, blockIdx.x + gridDim.x, ... and, while it computes one
+// item, the next item's tiles are already in flight (cp.async) into the other of two
+// shared-memory stages.  Inputs land straight in 16-bit operand tiles stored "8x8 blocked"
+// (see tc_util.cuh); 16-byte chunks are walked in storage order so shared-memory accesses are
+// conflict-free.  One thread issues 64x64x16 tcgen05.mma instructions into fp32 TMEM
+// accumulators; the epilogues read TMEM with the 16x256b shape, so all 32 lanes of a warp
+// carry data (an M=64 accumulator fills lanes 0-15 of each TMEM subpartition).  Warps w, w+4,
+// w+8, w+12 share subpartition w % 4 and take 16 accumulator columns each.
 //
 // Gating: with gc the in-chunk cumulative log decay, ref = gc of the chunk's 32nd row and
 // E = exp(gc - ref) (the only exponentials evaluated by the output / backward kernels),
@@ -29,13 +31,19 @@ namespace {
 
 using namespace ssla::tc;
 
-constexpr int NT = 256;
+constexpr int NT = 512;
+constexpr int D = 64;                      // K = V = 64
 constexpr int NWARP = NT / 32;
-constexpr int D = 64;         // K = V = 64
-constexpr int LDG = D + 1;    // fp32 gate tile stride
+constexpr int NG = NT / 64;                // gate-scan groups: thread (column, group) owns RG rows
+constexpr int RG = BT / NG;
+constexpr int EPI_COLS = D / (NWARP / 4);  // accumulator columns per warp in the epilogues
+constexpr int LDG = D + 1;                 // fp32 gate tile stride
 constexpr float kTcSpan = 40.f;
-constexpr int TILE = BT * D * 2;  // bytes of one 64x64 16-bit tile
-constexpr int GRAW = BT * D * 4;  // staging bytes of the raw gate tile (fp32 worst case)
+constexpr int TILE = BT * D * 2;           // bytes of one 64x64 16-bit tile
+constexpr int SP = D + 4;                  // padded row stride (floats) of a staged fp32 state
+constexpr int STATE = D * SP * 4;          // bytes of one staged fp32 state
+static_assert(EPI_COLS == 16, "epilogues read 16 columns per warp (16x256b.x2)");
+static_assert(NT == BT * D / 8, "staging assumes one 16-byte chunk of a 16-bit tile per thread");
 
 template <typename T> struct Fmt;
 template <> struct Fmt<__nv_bfloat16> { static constexpr int v = 1; };
@@ -50,19 +58,11 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   __half2 x = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&x);
 }
-
-template <typename T> __device__ __forceinline__ void load8(const T* p, float* x) {
-  const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
-  const T* e = reinterpret_cast<const T*>(&r);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = ldf(e + i);
+template <typename T> __device__ __forceinline__ void unpack2(uint32_t u, float& a, float& b) {
+  const T* e = reinterpret_cast<const T*>(&u);
+  a = ldf(e);
+  b = ldf(e + 1);
 }
-template <> __device__ __forceinline__ void load8<float>(const float* p, float* x) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-}
-
 template <typename T> __device__ __forceinline__ uint4 pack8(const float* x) {
   uint4 u;
   u.x = pack2<T>(x[0], x[1]);
@@ -71,82 +71,109 @@ template <typename T> __device__ __forceinline__ uint4 pack8(const float* x) {
   u.w = pack2<T>(x[6], x[7]);
   return u;
 }
-template <typename T> __device__ __forceinline__ void store8_tile(unsigned char* tile, int r, int c, const float* x) {
-  *reinterpret_cast<uint4*>(tile + blk_off(r, c, D)) = pack8<T>(x);
+
+// Two adjacent elements (r, c), (r, c+1) of an 8x8-blocked 16-bit tile (c even).
+template <typename T> __device__ __forceinline__ void st2_tile(unsigned char* tile, int r, int c, float a, float b) {
+  *reinterpret_cast<uint32_t*>(tile + blk_off(r, c, D)) = pack2<T>(a, b);
 }
-template <typename T> __device__ __forceinline__ void store8_global(T* p, const float* x) {
-  *reinterpret_cast<uint4*>(p) = pack8<T>(x);
+template <typename T> __device__ __forceinline__ void ld2_tile(const unsigned char* tile, int r, int c, float& a, float& b) {
+  unpack2<T>(*reinterpret_cast<const uint32_t*>(tile + blk_off(r, c, D)), a, b);
 }
-// 16 values of row r, columns c..c+15, of an 8x8-blocked 16-bit tile.
-template <typename T>
-__device__ __forceinline__ void tile_row16(const unsigned char* tile, int r, int c, float* x) {
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint4 u = *reinterpret_cast<const uint4*>(tile + blk_off(r, c + 8 * h, D));
-    const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[8 * h + i] = ldf(e + i);
-  }
+template <typename T> __device__ __forceinline__ void st2_global(T* p, float a, float b) {
+  *reinterpret_cast<uint32_t*>(p) = pack2<T>(a, b);
+}
+
+// 16-byte chunk e of a 64-column blocked tile, in storage order (byte 16 e): its row and first
+// column.  Consecutive lanes then touch consecutive 16-byte words of shared memory; on the
+// global side 8 lanes read the same 16 bytes of 8 consecutive rows.
+__device__ __forceinline__ void chunk_rc(int e, int& r, int& c) {
+  const int m = e >> 3;
+  r = ((m >> 3) << 3) | (e & 7);
+  c = (m & 7) << 3;
 }
 
 struct GateSmem {
-  float E[BT * LDG];  // exp(gc - ref) (or gc itself for local_state); dg scratch at the end
+  float E[BT * LDG];  // exp(gc - ref) (or gc itself for local_state); dgc scratch in the backward
   float ref[D];       // gc of row 31
   float eref[D];      // exp(ref)
   float egl[D];       // exp(gL - ref), gL = gc of row 63
   float gl[D];        // gL
-  float part[4][D];   // per-quarter partial sums (dg reverse cumsum, dgL)
+  float part[NG][D];  // per-group partial sums (gate scan, dg reverse cumsum, dgL)
   unsigned int span_bits;
 };
+constexpr size_t kGateBytes = sizeof(GateSmem);
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
                "r"(valid ? 16 : 0)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Per-thread staging geometry, fixed for the kernel's lifetime: this thread's chunk of every
+// 16-bit tile (row tr, column tc) and its offset within an item's [64, H, 64] token block.
+struct Stager {
+  int tr, tc, toff;
+  __device__ __forceinline__ Stager(int H) {
+    chunk_rc(threadIdx.x, tr, tc);
+    toff = tr * H * D + tc;
+  }
+  // One 64x64 16-bit tile of the item whose first element is `base` (rows >= len zero-filled).
+  template <typename T>
+  __device__ __forceinline__ void tile(unsigned char* dst, const T* __restrict__ base, int len) const {
+    const bool ok = tr < len;
+    cp_async16(dst + 16 * threadIdx.x, ok ? base + toff : base, ok);
+  }
+};
+
+// The raw gate tile of the item, row-major (element type Tg).
+template <typename Tg>
+__device__ __forceinline__ void stage_gate(unsigned char* raw, const Tg* __restrict__ base, int len, int H) {
+  constexpr int PER_ROW = D * (int)sizeof(Tg) / 16;
+#pragma unroll
+  for (int j = 0; j < BT * PER_ROW / NT; ++j) {
+    const int e = threadIdx.x + j * NT;
+    const int r = e / PER_ROW, c = (e % PER_ROW) * (16 / (int)sizeof(Tg));
+    const bool ok = r < len;
+    cp_async16(raw + 16 * e, ok ? base + r * H * D + c : base, ok);
+  }
 }
 
-// Copy a [64 tokens, 64] 16-bit tile of one head into an 8x8-blocked operand tile (rows >= len
-// are zero-filled).
-template <typename T>
-__device__ __forceinline__ void stage_tile(unsigned char* tile, const T* __restrict__ src, int64_t t0,
-                                           int len, int H, int head) {
-  for (int e = threadIdx.x; e < BT * (D / 8); e += NT) {
-    const int r = e >> 3, c = (e & 7) * 8;
-    const T* p = src + ((t0 + (r < len ? r : 0)) * H + head) * (int64_t)D + c;
-    cp_async16(tile + blk_off(r, c, D), p, r < len);
+// A contiguous fp32 [64, 64] state into shared memory (row stride SP floats).
+__device__ __forceinline__ void stage_state(float* dst, const float* __restrict__ src) {
+#pragma unroll
+  for (int j = 0; j < D * D / 4 / NT; ++j) {
+    const int e = threadIdx.x + j * NT;
+    cp_async16(dst + (e >> 4) * SP + (e & 15) * 4, src + 4 * e, true);
   }
 }
-// The gate tile, row-major in `raw` (element type Tg).
-template <typename Tg>
-__device__ __forceinline__ void stage_gate(unsigned char* raw, const Tg* __restrict__ g, int64_t t0,
-                                           int len, int H, int head) {
-  constexpr int PER_ROW = D * (int)sizeof(Tg) / 16;
-  for (int e = threadIdx.x; e < BT * PER_ROW; e += NT) {
-    const int r = e / PER_ROW, c = (e % PER_ROW) * (16 / (int)sizeof(Tg));
-    const Tg* p = g + ((t0 + (r < len ? r : 0)) * H + head) * (int64_t)D + c;
-    cp_async16(raw + (r * D + c) * sizeof(Tg), p, r < len);
-  }
+
+// This thread's 8 values of a staged fp32 state: row tr, columns tc .. tc+7 (its chunk of the
+// 16-bit tile it will write).
+__device__ __forceinline__ void state_regs(const float* src, const Stager& sg, float* v) {
+  const float4* p = reinterpret_cast<const float4*>(src + sg.tr * SP + sg.tc);
+  const float4 a = p[0], b = p[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 // From the staged raw gate tile: in-chunk cumulative sums gc, ref (gc of row 31), gL (row 63),
 // exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk, and E = exp(gc - ref)
-// (STORE_GC: gc itself).  Thread (column c = tid % 64, quarter q = tid / 64) scans rows
-// 16q .. 16q+15 of its column serially in registers; the quarter totals are combined
-// through shared memory (two barriers, no shuffle chains).
+// (STORE_GC: gc itself).  Thread (column c = tid % 64, group q = tid / 64) scans rows
+// RG*q .. RG*q+RG-1 of its column serially in registers; the group totals are combined
+// through shared memory.
 template <typename Tg, bool STORE_GC>
 __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw) {
-  static_assert(NT == 256, "gate_prep maps 4 threads to each of the 64 columns");
+  static_assert(NT % 64 == 0 && 31 % RG == RG - 1, "row 31 must end a group");
   const int tid = threadIdx.x, c = tid & 63, qt = tid >> 6;
   const Tg* gr = reinterpret_cast<const Tg*>(raw);
   if (tid == 0) G.span_bits = 0u;
-  float x[16];
+  float x[RG];
   float run = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    run += ldf(gr + (16 * qt + i) * D + c);
+  for (int i = 0; i < RG; ++i) {
+    run += ldf(gr + (RG * qt + i) * D + c);
     x[i] = run;
   }
   G.part[qt][c] = run;
@@ -154,16 +181,16 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   float off = 0.f;
   for (int j = 0; j < qt; ++j) off += G.part[j][c];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) x[i] += off;
-  if (qt == 1) G.ref[c] = x[15];  // row 31
-  if (qt == 3) G.gl[c] = x[15];   // row 63
+  for (int i = 0; i < RG; ++i) x[i] += off;
+  if (qt == 31 / RG) G.ref[c] = x[RG - 1];  // row 31
+  if (qt == NG - 1) G.gl[c] = x[RG - 1];    // row 63
   __syncthreads();
   const float ref = G.ref[c];
   float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < RG; ++i) {
     m = fmaxf(m, fabsf(x[i] - ref));
-    G.E[(16 * qt + i) * LDG + c] = STORE_GC ? x[i] : __expf(x[i] - ref);
+    G.E[(RG * qt + i) * LDG + c] = STORE_GC ? x[i] : __expf(x[i] - ref);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -175,26 +202,9 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   __syncthreads();
 }
 
-// In-place gating of an 8x8-blocked 16-bit tile: x[r][c] *= f(r, c); optionally keeps the raw
-// tile in `raw_copy`.
-template <typename T, class F>
-__device__ __forceinline__ void gate_tile(unsigned char* tile, F f, unsigned char* raw_copy = nullptr) {
-  for (int e = threadIdx.x; e < BT * (D / 8); e += NT) {
-    const int r = e >> 3, c = (e & 7) * 8;
-    uint4* p = reinterpret_cast<uint4*>(tile + blk_off(r, c, D));
-    const uint4 u = *p;
-    if (raw_copy) *reinterpret_cast<uint4*>(raw_copy + blk_off(r, c, D)) = u;
-    const T* x = reinterpret_cast<const T*>(&u);
-    float y[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = ldf(x + i) * f(r, c + i);
-    *p = pack8<T>(y);
-  }
-}
-
-__device__ __forceinline__ void mbar_setup(uint64_t* mbar) {
+__device__ __forceinline__ void mbar_setup(uint64_t* mbar, int n) {
   if (threadIdx.x == 0) {
-    mbar_init(mbar, 1);
+    for (int i = 0; i < n; ++i) mbar_init(mbar + i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
 }
@@ -207,391 +217,516 @@ __device__ __forceinline__ void operands_ready() {
   fence_after();
 }
 
-__device__ __forceinline__ void wait_mma(uint64_t* mbar, uint32_t parity) {
-  mbar_wait(mbar, parity);
+__device__ __forceinline__ void wait_mma(uint64_t* mbar, uint32_t& phase) {
+  mbar_wait(mbar, phase);
+  phase ^= 1u;
   fence_after();
 }
 
-// Four k-steps (K = 64) of D (+)= A * B^T.
+// Four k-steps (K = 64) of D (+)= A * B^T; operands are 64-column blocked tiles read K-major
+// or MN-major.
 __device__ __forceinline__ void mma64(uint32_t d, const void* a, int a_mn, const void* b, int b_mn,
                                       uint32_t idesc, bool accumulate) {
+  const uint64_t da = a_mn ? desc_mn64(a) : desc_k64(a);
+  const uint64_t db = b_mn ? desc_mn64(b) : desc_k64(b);
+  const uint64_t sa = a_mn ? 128u : 16u, sb = b_mn ? 128u : 16u;
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const uint64_t da = a_mn ? desc_mnmajor(a, D, s) : desc_kmajor(a, D, s);
-    const uint64_t db = b_mn ? desc_mnmajor(b, D, s) : desc_kmajor(b, D, s);
-    mma_f16(d, da, db, idesc, (accumulate || s > 0) ? 1u : 0u);
-  }
+  for (int s = 0; s < 4; ++s) mma_f16(d, da + s * sa, db + s * sb, idesc, (accumulate || s > 0) ? 1u : 0u);
 }
 
-// Gate the staged q and k tiles in one pass: Q^ = scale q E, K^ = k / E (optionally keeping
-// the raw tiles).
+// Gate the staged q and k chunks of this thread: Q^ = scale q E, K^ = k / E, written to dQ /
+// dK (which may be the source tiles themselves).
 template <typename T>
-__device__ __forceinline__ void gate_qk(unsigned char* sQ, unsigned char* sK, const GateSmem& G, float scale,
-                                        unsigned char* rawQ, unsigned char* rawK) {
-  for (int e = threadIdx.x; e < BT * (D / 8); e += NT) {
-    const int r = e >> 3, c = (e & 7) * 8;
-    uint4* pq = reinterpret_cast<uint4*>(sQ + blk_off(r, c, D));
-    uint4* pk = reinterpret_cast<uint4*>(sK + blk_off(r, c, D));
-    const uint4 uq = *pq, uk = *pk;
-    if (rawQ) {
-      *reinterpret_cast<uint4*>(rawQ + blk_off(r, c, D)) = uq;
-      *reinterpret_cast<uint4*>(rawK + blk_off(r, c, D)) = uk;
-    }
-    const T* xq = reinterpret_cast<const T*>(&uq);
-    const T* xk = reinterpret_cast<const T*>(&uk);
-    float yq[8], yk[8];
+__device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned char* sK, unsigned char* dQ,
+                                        unsigned char* dK, const GateSmem& G, const Stager& sg, float scale) {
+  const int off = 16 * threadIdx.x;
+  const uint4 uq = *reinterpret_cast<const uint4*>(sQ + off);
+  const uint4 uk = *reinterpret_cast<const uint4*>(sK + off);
+  const T* xq = reinterpret_cast<const T*>(&uq);
+  const T* xk = reinterpret_cast<const T*>(&uk);
+  const float* e = G.E + sg.tr * LDG + sg.tc;
+  float yq[8], yk[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float e = G.E[r * LDG + c + i];
-      yq[i] = ldf(xq + i) * (scale * e);
-      yk[i] = __fdividef(ldf(xk + i), e);
-    }
-    *pq = pack8<T>(yq);
-    *pk = pack8<T>(yk);
+  for (int i = 0; i < 8; ++i) {
+    yq[i] = ldf(xq + i) * (scale * e[i]);
+    yk[i] = __fdividef(ldf(xk + i), e[i]);
   }
+  *reinterpret_cast<uint4*>(dQ + off) = pack8<T>(yq);
+  *reinterpret_cast<uint4*>(dK + off) = pack8<T>(yk);
 }
 
-// Epilogue mapping: TMEM subpartition (row block) and column half of this warp.
+// Epilogue geometry (16x256b.x2): this warp reads TMEM subpartition sp, columns c0 .. c0+15;
+// pair p of the 8 values holds row r0 + 8*(p&1), columns c0 + cc + 8*(p>>1) + {0, 1}.
 struct Epi {
-  int sp, c0, row;
+  int sp, c0, r0, cc;
   __device__ __forceinline__ Epi() {
-    const int warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     sp = warp & 3;
-    c0 = (warp >> 2) * 32;
-    row = 16 * sp + (threadIdx.x & 31);
+    c0 = (warp >> 2) * EPI_COLS;
+    r0 = 16 * sp + (lane >> 2);
+    cc = c0 + 2 * (lane & 3);
   }
-  __device__ __forceinline__ bool owns() const { return (threadIdx.x & 31) < 16; }
+  __device__ __forceinline__ int row(int p) const { return r0 + 8 * (p & 1); }
+  __device__ __forceinline__ int col(int p) const { return cc + 8 * (p >> 1); }
+  __device__ __forceinline__ void load(uint32_t tbase, float* v) const {
+    tmem_ld16x256b_x2(tmem_addr(tbase, sp, c0), v);
+  }
 };
 
+// --------------------------------------------------------------------------- persistent loop
+struct Item {
+  int64_t t0;  // first token of the chunk
+  int cid, head, len;
+};
+
+// Item cursor: it = cid * H + head, advanced by gridDim.x without divisions.
+struct Cursor {
+  int cid, head;
+  __device__ __forceinline__ void advance(int gq, int gr, int H) {
+    head += gr;
+    cid += gq;
+    if (head >= H) {
+      head -= H;
+      ++cid;
+    }
+  }
+};
+
+__device__ __forceinline__ longlong2 item_entry(const Cursor& c, int MC, const longlong2* __restrict__ tab) {
+  return c.cid < MC ? tab[c.cid] : make_longlong2(0, -1ll << 32);
+}
+__device__ __forceinline__ bool decode_item(const Cursor& c, longlong2 e, Item& x) {
+  if ((e.y >> 32) < 0) return false;
+  x.cid = c.cid;
+  x.head = c.head;
+  x.t0 = e.x;
+  x.len = (int)(e.y & 0xffffffff);
+  return true;
+}
+
+// Valid chunks form a prefix of the chunk table, so a CTA stops at its first invalid item.
+// The table entry of the item after next is loaded one iteration before it is decoded.
+template <class Load, class Proc>
+__device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* __restrict__ tab, Load load,
+                                                Proc proc) {
+  const int G = gridDim.x, gq = G / H, gr = G % H;
+  Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
+  Cursor c1 = c, c2;
+  c1.advance(gq, gr, H);
+  c2 = c1;
+  c2.advance(gq, gr, H);
+  Item cur;
+  bool have = decode_item(c, item_entry(c, MC, tab), cur);
+  longlong2 e_next = item_entry(c1, MC, tab);
+  if (have) load(cur, 0);
+  cp_async_commit();
+  for (int i = 0; have; ++i) {
+    const longlong2 e_after = item_entry(c2, MC, tab);
+    Item nxt;
+    const bool nhave = decode_item(c1, e_next, nxt);
+    if (nhave) load(nxt, (i + 1) & 1);
+    cp_async_commit();
+    cp_async_wait_prev();
+    __syncthreads();
+    proc(cur, i & 1);
+    __syncthreads();
+    cur = nxt;
+    have = nhave;
+    e_next = e_after;
+    c1 = c2;
+    c2.advance(gq, gr, H);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // --------------------------------------------------------------------------- local state
+// stage: a tile | b tile | raw gate
+template <typename Tg> __host__ __device__ constexpr int ls_stage_bytes() { return 2 * TILE + BT * D * (int)sizeof(Tg); }
+
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT) tc_local_state_kernel(
+__global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
     int mode, const T* __restrict__ a_src, const T* __restrict__ b_src, const Tg* __restrict__ g,
-    const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab, int64_t N, int H,
-    float scale, float* __restrict__ dS, float* __restrict__ decay) {
+    const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, float* __restrict__ dS,
+    float* __restrict__ decay) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* sA = smem;
-  unsigned char* sB = sA + TILE;
-  unsigned char* graw = sB + TILE;
-  GateSmem& G = *reinterpret_cast<GateSmem*>(graw + GRAW);
+  constexpr int STAGE = ls_stage_bytes<Tg>();
+  GateSmem& G = *reinterpret_cast<GateSmem*>(smem + 2 * STAGE);
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t cid = blockIdx.x;
-  const int head = blockIdx.y;
-  int64_t seq, t0;
-  int len;
-  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
   if (warp == 0) tmem_alloc(&tbase_s, 64);
-  mbar_setup(&mbar);
-  stage_gate<Tg>(graw, g, t0, len, H, head);
-  stage_tile<T>(sA, a_src, t0, len, H, head);
-  stage_tile<T>(sB, b_src, t0, len, H, head);
-  cp_async_wait_all();
+  mbar_setup(&mbar, 1);
   __syncthreads();
-  gate_prep<Tg, true>(G, graw);
-  if (mode == 0)
-    gate_tile<T>(sA, [&](int r, int c) { return __expf(G.gl[c] - G.E[r * LDG + c]); });
-  else
-    gate_tile<T>(sA, [&](int r, int c) { return scale * __expf(G.E[r * LDG + c]); });
-  operands_ready();
+  fence_after();
   const uint32_t tb = tbase_s;
-  if (tid == 0) {
-    mma64(tb, sA, 1, sB, 1, idesc_f16(64, 64, Fmt<T>::v, 1, 1), false);
-    commit(&mbar);
-  }
-  wait_mma(&mbar, 0);
+  uint32_t phase = 0;
   const Epi ep;
-  float* out = dS + (cid * H + head) * (int64_t)D * D;
-  for (int cb = ep.c0; cb < ep.c0 + 32; cb += 16) {
-    float v[16];
-    tmem_ld16(tmem_addr(tb, ep.sp, cb), v);
-    if (ep.owns()) {
-      float4* o4 = reinterpret_cast<float4*>(out + ep.row * D + cb);
+  const Stager sg(H);
+  persistent_loop(
+      MC, H, chunk_tab,
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        const int64_t base = (x.t0 * H + x.head) * D;
+        sg.tile<T>(b, a_src + base, x.len);
+        sg.tile<T>(b + TILE, b_src + base, x.len);
+        stage_gate<Tg>(b + 2 * TILE, g + base, x.len, H);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* sA = smem + st * STAGE;
+        unsigned char* sB = sA + TILE;
+        gate_prep<Tg, true>(G, sB + TILE);
+        {
+          uint4* p = reinterpret_cast<uint4*>(sA + 16 * tid);
+          const uint4 u = *p;
+          const T* xs = reinterpret_cast<const T*>(&u);
+          const float* gc = G.E + sg.tr * LDG + sg.tc;
+          float y[8];
+          if (mode == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    }
-  }
-  if (tid < D) decay[(cid * H + head) * D + tid] = __expf(G.gl[tid]);
-  fence_before();
+            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * __expf(G.gl[sg.tc + i] - gc[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * (scale * __expf(gc[i]));
+          }
+          *p = pack8<T>(y);
+        }
+        operands_ready();
+        if (tid == 0) {
+          mma64(tb, sA, 1, sB, 1, idesc_f16(64, 64, Fmt<T>::v, 1, 1), false);
+          commit(&mbar);
+        }
+        wait_mma(&mbar, phase);
+        float v[8];
+        ep.load(tb, v);
+        float* out = dS + ((int64_t)x.cid * H + x.head) * D * D;
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          *reinterpret_cast<float2*>(out + ep.row(p) * D + ep.col(p)) = make_float2(v[2 * p], v[2 * p + 1]);
+        if (tid < D) decay[((int64_t)x.cid * H + x.head) * D + tid] = __expf(G.gl[tid]);
+        fence_before();
+      });
   __syncthreads();
+  fence_after();
   if (warp == 0) tmem_dealloc(tb, 64);
 }
 
 // --------------------------------------------------------------------------- forward output
+// stage: q | k | v tiles | fp32 chunk-start state (its first 8 KB become the 16-bit H' tile) |
+// raw gate.  Q^ and K^ are gated in place.
+template <typename Tg> __host__ __device__ constexpr int fo_stage_bytes() { return 3 * TILE + STATE + BT * D * (int)sizeof(Tg); }
+
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT) tc_fwd_o_kernel(
+__global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
-    int64_t N, int H, float scale, const float* __restrict__ states, T* __restrict__ o,
-    int* __restrict__ flags) {
+    const Tg* __restrict__ g, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
+    const float* __restrict__ states, T* __restrict__ o, int* __restrict__ flags) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* sQ = smem;
-  unsigned char* sK = sQ + TILE;
-  unsigned char* sV = sK + TILE;
-  unsigned char* sH = sV + TILE;
-  unsigned char* sA = sH + TILE;
-  unsigned char* graw = sA + TILE;
-  GateSmem& G = *reinterpret_cast<GateSmem*>(graw + GRAW);
+  constexpr int STAGE = fo_stage_bytes<Tg>();
+  unsigned char* sA = smem + 2 * STAGE;
+  GateSmem& G = *reinterpret_cast<GateSmem*>(sA + TILE);
   __shared__ uint64_t mbar;
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t cid = blockIdx.x;
-  const int head = blockIdx.y;
-  int64_t seq, t0;
-  int len;
-  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
   if (warp == 0) tmem_alloc(&tbase_s, 128);
-  mbar_setup(&mbar);
-  stage_gate<Tg>(graw, g, t0, len, H, head);
-  stage_tile<T>(sQ, q, t0, len, H, head);
-  stage_tile<T>(sK, k, t0, len, H, head);
-  stage_tile<T>(sV, v, t0, len, H, head);
-  // chunk-start state: fetched into registers while the tiles land
-  constexpr int SV = D * (D / 8) / NT;  // 8-float vectors per thread
-  float hreg[SV][8];
-  {
-    const float* hs = states + (cid * H + head) * (int64_t)D * D;
-#pragma unroll
-    for (int j = 0; j < SV; ++j) {
-      const int e = tid + j * NT;
-      load8(hs + (e >> 3) * D + (e & 7) * 8, hreg[j]);
-    }
-  }
-  cp_async_wait_all();
+  mbar_setup(&mbar, 1);
   __syncthreads();
-  gate_prep<Tg, false>(G, graw);
-  const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
-  if (tid == 0) flags[cid * H + head] = exact ? 1 : 0;
+  fence_after();
   const uint32_t tb = tbase_s;
-  if (exact) {
-    if (warp == 0) tmem_dealloc(tb, 128);
-    return;
-  }
-  gate_qk<T>(sQ, sK, G, scale, nullptr, nullptr);
-#pragma unroll
-  for (int j = 0; j < SV; ++j) {
-    const int e = tid + j * NT, r = e >> 3;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) hreg[j][i] *= G.eref[r];
-    store8_tile<T>(sH, r, (e & 7) * 8, hreg[j]);
-  }
-  operands_ready();
-  constexpr uint32_t F = Fmt<T>::v;
-  if (tid == 0) {
-    mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);        // A = Q^ K^^T
-    mma64(tb + 64, sQ, 0, sH, 1, idesc_f16(64, 64, F, 0, 1), false);   // O = Q^ H'
-    commit(&mbar);
-  }
-  wait_mma(&mbar, 0);
+  uint32_t phase = 0;
   const Epi ep;
-  for (int cb = ep.c0; cb < ep.c0 + 32; cb += 16) {
-    float x[16];
-    tmem_ld16(tmem_addr(tb, ep.sp, cb), x);
-    if (ep.owns()) {
+  const Stager sg(H);
+  constexpr uint32_t F = Fmt<T>::v;
+  persistent_loop(
+      MC, H, chunk_tab,
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        const int64_t base = (x.t0 * H + x.head) * D;
+        sg.tile<T>(b, q + base, x.len);
+        sg.tile<T>(b + TILE, k + base, x.len);
+        sg.tile<T>(b + 2 * TILE, v + base, x.len);
+        stage_state(reinterpret_cast<float*>(b + 3 * TILE), states + ((int64_t)x.cid * H + x.head) * D * D);
+        stage_gate<Tg>(b + 3 * TILE + STATE, g + base, x.len, H);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* sQ = smem + st * STAGE;
+        unsigned char* sK = sQ + TILE;
+        unsigned char* sV = sK + TILE;
+        unsigned char* sH = sV + TILE;
+        float hreg[8];
+        state_regs(reinterpret_cast<const float*>(sH), sg, hreg);
+        gate_prep<Tg, false>(G, sH + STATE);  // its barriers order the state reads before sH writes
+        const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
+        if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
+        if (exact) return;
+        gate_qk<T>(sQ, sK, sQ, sK, G, sg, scale);
+        operands_ready();
+        if (tid == 0) mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);  // A = Q^ K^^T
+        {
+          const float er = G.eref[sg.tr];
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (cb + i > ep.row) x[i] = 0.f;
-      store8_tile<T>(sA, ep.row, cb, x);
-      store8_tile<T>(sA, ep.row, cb + 8, x + 8);
-    }
-  }
-  operands_ready();
-  if (tid == 0) {
-    mma64(tb + 64, sA, 0, sV, 1, idesc_f16(64, 64, F, 0, 1), true);    // O += A V
-    commit(&mbar);
-  }
-  wait_mma(&mbar, 1);
-  for (int cb = ep.c0; cb < ep.c0 + 32; cb += 16) {
-    float x[16];
-    tmem_ld16(tmem_addr(tb + 64, ep.sp, cb), x);
-    if (ep.owns() && ep.row < len) {
-      T* dst = o + ((t0 + ep.row) * H + head) * (int64_t)D + cb;
-      store8_global<T>(dst, x);
-      store8_global<T>(dst + 8, x + 8);
-    }
-  }
-  fence_before();
+          for (int i = 0; i < 8; ++i) hreg[i] *= er;
+          *reinterpret_cast<uint4*>(sH + 16 * tid) = pack8<T>(hreg);
+        }
+        operands_ready();
+        if (tid == 0) {
+          mma64(tb + 64, sQ, 0, sH, 1, idesc_f16(64, 64, F, 0, 1), false);  // O = Q^ H'
+          commit(&mbar);
+        }
+        wait_mma(&mbar, phase);
+        {
+          float a[8];
+          ep.load(tb, a);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int r = ep.row(p), c = ep.col(p);
+            st2_tile<T>(sA, r, c, c > r ? 0.f : a[2 * p], c + 1 > r ? 0.f : a[2 * p + 1]);
+          }
+        }
+        operands_ready();
+        if (tid == 0) {
+          mma64(tb + 64, sA, 0, sV, 1, idesc_f16(64, 64, F, 0, 1), true);  // O += A V
+          commit(&mbar);
+        }
+        wait_mma(&mbar, phase);
+        {
+          float y[8];
+          ep.load(tb + 64, y);
+          T* ob = o + (x.t0 * H + x.head) * D;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int r = ep.row(p);
+            if (r < x.len) st2_global<T>(ob + (int64_t)r * H * D + ep.col(p), y[2 * p], y[2 * p + 1]);
+          }
+        }
+        fence_before();
+      });
   __syncthreads();
+  fence_after();
   if (warp == 0) tmem_dealloc(tb, 128);
 }
 
 // --------------------------------------------------------------------------- backward
+// stage: q | k | v | do tiles | fp32 state h | fp32 adjoint dh (the first 8 KB of each become
+// the 16-bit H' / dH' tiles) | raw gate.  Gated Q^, K^ and the score tiles A, dA are working
+// tiles outside the stages; the raw q and k stay in the stage for dg.
+template <typename Tg> __host__ __device__ constexpr int bw_stage_bytes() { return 4 * TILE + 2 * STATE + BT * D * (int)sizeof(Tg); }
+
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT) tc_bwd_kernel(
+__global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
-    int64_t N, int H, float scale, const float* __restrict__ states,
-    const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
-    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, int* __restrict__ flags) {
+    const Tg* __restrict__ g, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
+    const float* __restrict__ states, const float* __restrict__ dstates, const T* __restrict__ dout,
+    T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg,
+    int* __restrict__ flags) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* sQ = smem;
-  unsigned char* sK = sQ + TILE;
-  unsigned char* sV = sK + TILE;
-  unsigned char* sDO = sV + TILE;
-  unsigned char* sH = sDO + TILE;
-  unsigned char* sDH = sH + TILE;
-  unsigned char* sA = sDH + TILE;
+  constexpr int STAGE = bw_stage_bytes<Tg>();
+  unsigned char* sQg = smem + 2 * STAGE;
+  unsigned char* sKg = sQg + TILE;
+  unsigned char* sA = sKg + TILE;
   unsigned char* sdA = sA + TILE;
-  unsigned char* graw = sdA + TILE;
-  GateSmem& G = *reinterpret_cast<GateSmem*>(graw + GRAW);
-  __shared__ uint64_t mbar;
+  GateSmem& G = *reinterpret_cast<GateSmem*>(sdA + TILE);
+  __shared__ uint64_t mbar[2];  // [0]: score batch, then dq / dk;  [1]: dv
   __shared__ uint32_t tbase_s;
-  __shared__ float s_hdh[D], s_dgl[D];
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t cid = blockIdx.x;
-  const int head = blockIdx.y;
-  int64_t seq, t0;
-  int len;
-  if (!locate_chunk(cid, chunk_tab, seq, t0, len)) return;
+  __shared__ float s_hdh[2 * D], s_dgl[D];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (warp == 0) tmem_alloc(&tbase_s, 256);
-  mbar_setup(&mbar);
-  if (tid < D) s_hdh[tid] = 0.f;
-  stage_gate<Tg>(graw, g, t0, len, H, head);
-  stage_tile<T>(sQ, q, t0, len, H, head);
-  stage_tile<T>(sK, k, t0, len, H, head);
-  stage_tile<T>(sV, v, t0, len, H, head);
-  stage_tile<T>(sDO, dout, t0, len, H, head);
-  // chunk-start state and its adjoint: fetched into registers while the tiles land
-  constexpr int SV = D * (D / 8) / NT;  // 8-float vectors per thread
-  const int64_t soff = (cid * H + head) * (int64_t)D * D;
-  float hreg[SV][8], dhreg[SV][8];
-#pragma unroll
-  for (int j = 0; j < SV; ++j) {
-    const int e = tid + j * NT;
-    load8(states + soff + (e >> 3) * D + (e & 7) * 8, hreg[j]);
-    load8(dstates + soff + (e >> 3) * D + (e & 7) * 8, dhreg[j]);
-  }
-  cp_async_wait_all();
+  mbar_setup(mbar, 2);
   __syncthreads();
-  gate_prep<Tg, false>(G, graw);
-  const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
-  if (tid == 0) flags[cid * H + head] = exact ? 1 : 0;
+  fence_after();
   const uint32_t tb = tbase_s;
-  if (exact) {
-    if (warp == 0) tmem_dealloc(tb, 256);
-    return;
-  }
-  // raw q and k stay (blocked layout) in the gate staging area for dg = q dq - k dk
-  unsigned char* rawQ = graw;
-  unsigned char* rawK = graw + TILE;
-  gate_qk<T>(sQ, sK, G, scale, rawQ, rawK);
-#pragma unroll
-  for (int j = 0; j < SV; ++j) {
-    const int e = tid + j * NT, r = e >> 3, c = (e & 7) * 8;
-    float hd = 0.f;
-    const float er = G.eref[r], egl = G.egl[r];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      hd = fmaf(hreg[j][i], dhreg[j][i], hd);
-      hreg[j][i] *= er;
-      dhreg[j][i] *= egl;
-    }
-    atomicAdd(&s_hdh[r], hd);
-    store8_tile<T>(sH, r, c, hreg[j]);
-    store8_tile<T>(sDH, r, c, dhreg[j]);
-  }
-  operands_ready();
-  constexpr uint32_t F = Fmt<T>::v;
-  if (tid == 0) {
-    mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);         // A  = Q^ K^^T
-    mma64(tb + 64, sDO, 0, sV, 0, idesc_f16(64, 64, F, 0, 0), false);   // dA = do v^T
-    mma64(tb + 128, sK, 1, sV, 1, idesc_f16(64, 64, F, 1, 1), false);   // S  = K^^T v
-    commit(&mbar);
-  }
-  wait_mma(&mbar, 0);
+  uint32_t phase = 0, phase_dv = 0;
   const Epi ep;
-  float dgl_part = 0.f;
-  for (int cb = ep.c0; cb < ep.c0 + 32; cb += 16) {
-    float x[16], y[16], z[16];
-    tmem_ld16(tmem_addr(tb, ep.sp, cb), x);
-    tmem_ld16(tmem_addr(tb + 64, ep.sp, cb), y);
-    tmem_ld16(tmem_addr(tb + 128, ep.sp, cb), z);
-    if (ep.owns()) {
+  const Stager sg(H);
+  constexpr uint32_t F = Fmt<T>::v;
+  persistent_loop(
+      MC, H, chunk_tab,
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        const int64_t base = (x.t0 * H + x.head) * D;
+        const int64_t soff = ((int64_t)x.cid * H + x.head) * D * D;
+        sg.tile<T>(b, q + base, x.len);
+        sg.tile<T>(b + TILE, k + base, x.len);
+        sg.tile<T>(b + 2 * TILE, v + base, x.len);
+        sg.tile<T>(b + 3 * TILE, dout + base, x.len);
+        stage_state(reinterpret_cast<float*>(b + 4 * TILE), states + soff);
+        stage_state(reinterpret_cast<float*>(b + 4 * TILE + STATE), dstates + soff);
+        stage_gate<Tg>(b + 4 * TILE + 2 * STATE, g + base, x.len, H);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* rQ = smem + st * STAGE;
+        unsigned char* rK = rQ + TILE;
+        unsigned char* sV = rK + TILE;
+        unsigned char* sDO = sV + TILE;
+        unsigned char* sH = sDO + TILE;
+        unsigned char* sDH = sH + STATE;
+        float hreg[8], dhreg[8];
+        state_regs(reinterpret_cast<const float*>(sH), sg, hreg);
+        state_regs(reinterpret_cast<const float*>(sDH), sg, dhreg);
+        gate_prep<Tg, false>(G, sDH + STATE);  // its barriers order the state reads before sH/sDH writes
+        const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
+        if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
+        if (exact) return;
+        gate_qk<T>(rQ, rK, sQg, sKg, G, sg, scale);
+        operands_ready();
+        if (tid == 0) {
+          mma64(tb, sQg, 0, sKg, 0, idesc_f16(64, 64, F, 0, 0), false);       // A  = Q^ K^^T
+          mma64(tb + 64, sDO, 0, sV, 0, idesc_f16(64, 64, F, 0, 0), false);   // dA = do v^T
+          mma64(tb + 128, sKg, 1, sV, 1, idesc_f16(64, 64, F, 1, 1), false);  // S  = K^^T v
+          commit(&mbar[0]);
+        }
+        // H', dH' tiles and h.dh per row while the score batch runs
+        {
+          const float er = G.eref[sg.tr], egl = G.egl[sg.tr];
+          float hd = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (cb + i > ep.row) { x[i] = 0.f; y[i] = 0.f; }
-      store8_tile<T>(sA, ep.row, cb, x);
-      store8_tile<T>(sA, ep.row, cb + 8, x + 8);
-      store8_tile<T>(sdA, ep.row, cb, y);
-      store8_tile<T>(sdA, ep.row, cb + 8, y + 8);
-      // row `row` of S is key index `row`: dh'[row, :] . S[row, :]
-      float dh16[16];
-      tile_row16<T>(sDH, ep.row, cb, dh16);
+          for (int i = 0; i < 8; ++i) {
+            hd = fmaf(hreg[i], dhreg[i], hd);
+            hreg[i] *= er;
+            dhreg[i] *= egl;
+          }
+          // lanes l, l^8, l^16, l^24 hold row tr, column blocks 4h .. 4h+3 (h = warp parity)
+          hd += __shfl_xor_sync(0xffffffffu, hd, 8);
+          hd += __shfl_xor_sync(0xffffffffu, hd, 16);
+          if (lane < 8) s_hdh[(sg.tc >> 5) * D + sg.tr] = hd;
+          *reinterpret_cast<uint4*>(sH + 16 * tid) = pack8<T>(hreg);
+          *reinterpret_cast<uint4*>(sDH + 16 * tid) = pack8<T>(dhreg);
+        }
+        fence_proxy_async();
+        __syncthreads();
+        wait_mma(&mbar[0], phase);
+        {
+          float a[8], b[8], z[8];
+          ep.load(tb, a);
+          ep.load(tb + 64, b);
+          ep.load(tb + 128, z);
+          float dgl0 = 0.f, dgl1 = 0.f;  // rows r0, r0 + 8
 #pragma unroll
-      for (int i = 0; i < 16; ++i) dgl_part = fmaf(dh16[i], z[i], dgl_part);
-    }
-  }
-  if (ep.owns()) G.part[warp >> 2][ep.row] = dgl_part;
-  operands_ready();
-  if (tid == 0) {
-    mma64(tb + 192, sA, 1, sDO, 1, idesc_f16(64, 64, F, 1, 1), false);  // dv  = A^T do
-    mma64(tb + 192, sK, 0, sDH, 1, idesc_f16(64, 64, F, 0, 1), true);   //     + K^ dh'
-    mma64(tb, sDO, 0, sH, 0, idesc_f16(64, 64, F, 0, 0), false);        // dq~ = do H'^T
-    mma64(tb, sdA, 0, sK, 1, idesc_f16(64, 64, F, 0, 1), true);         //     + dA K^
-    mma64(tb + 64, sV, 0, sDH, 0, idesc_f16(64, 64, F, 0, 0), false);   // dk~ = v dh'^T
-    mma64(tb + 64, sdA, 1, sQ, 1, idesc_f16(64, 64, F, 1, 1), true);    //     + dA^T Q^
-    commit(&mbar);
-  }
-  // dgL per key index: exp(gL) h.dh + dh'.(K^^T v)
-  if (tid < D) s_dgl[tid] = G.eref[tid] * G.egl[tid] * s_hdh[tid] + G.part[0][tid] + G.part[1][tid];
-  wait_mma(&mbar, 1);
-  const int64_t roff = ((t0 + ep.row) * H + head) * (int64_t)D;
-  const bool live = ep.owns() && ep.row < len;
-  for (int cb = ep.c0; cb < ep.c0 + 32; cb += 16) {
-    float x[16], y[16], z[16];
-    tmem_ld16(tmem_addr(tb + 192, ep.sp, cb), z);
-    tmem_ld16(tmem_addr(tb, ep.sp, cb), x);
-    tmem_ld16(tmem_addr(tb + 64, ep.sp, cb), y);
-    if (ep.owns()) {
-      float qr[16], kr[16];
-      tile_row16<T>(rawQ, ep.row, cb, qr);
-      tile_row16<T>(rawK, ep.row, cb, kr);
+          for (int p = 0; p < 4; ++p) {
+            const int r = ep.row(p), c = ep.col(p);
+            const bool m0 = c > r, m1 = c + 1 > r;
+            st2_tile<T>(sA, r, c, m0 ? 0.f : a[2 * p], m1 ? 0.f : a[2 * p + 1]);
+            st2_tile<T>(sdA, r, c, m0 ? 0.f : b[2 * p], m1 ? 0.f : b[2 * p + 1]);
+            // row r of S is key index r: dh'[r, :] . S[r, :]
+            float d0, d1;
+            ld2_tile<T>(sDH, r, c, d0, d1);
+            const float t = fmaf(d0, z[2 * p], d1 * z[2 * p + 1]);
+            if (p & 1) dgl1 += t; else dgl0 += t;
+          }
+          dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 1);
+          dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 2);
+          dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 1);
+          dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 2);
+          if ((lane & 3) == 0) {
+            G.part[warp >> 2][ep.r0] = dgl0;
+            G.part[warp >> 2][ep.r0 + 8] = dgl1;
+          }
+        }
+        operands_ready();
+        if (tid == 0) {
+          mma64(tb + 192, sA, 1, sDO, 1, idesc_f16(64, 64, F, 1, 1), false);  // dv  = A^T do
+          mma64(tb + 192, sKg, 0, sDH, 1, idesc_f16(64, 64, F, 0, 1), true);  //     + K^ dh'
+          commit(&mbar[1]);
+          mma64(tb, sDO, 0, sH, 0, idesc_f16(64, 64, F, 0, 0), false);        // dq~ = do H'^T
+          mma64(tb, sdA, 0, sKg, 1, idesc_f16(64, 64, F, 0, 1), true);        //     + dA K^
+          mma64(tb + 64, sV, 0, sDH, 0, idesc_f16(64, 64, F, 0, 0), false);   // dk~ = v dh'^T
+          mma64(tb + 64, sdA, 1, sQg, 1, idesc_f16(64, 64, F, 1, 1), true);   //     + dA^T Q^
+          commit(&mbar[0]);
+        }
+        // dgL per key index: exp(gL) h.dh + dh'.(K^^T v)
+        if (tid < D) {
+          float sp = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float e = G.E[ep.row * LDG + cb + i];
-        x[i] *= scale * e;
-        y[i] = __fdividef(y[i], e);
-      }
+          for (int j = 0; j < NWARP / 4; ++j) sp += G.part[j][tid];
+          s_dgl[tid] = G.eref[tid] * G.egl[tid] * (s_hdh[tid] + s_hdh[D + tid]) + sp;
+        }
+        const int64_t base = (x.t0 * H + x.head) * D;
+        wait_mma(&mbar[1], phase_dv);
+        {
+          float z[8];
+          ep.load(tb + 192, z);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) G.E[ep.row * LDG + cb + i] = qr[i] * x[i] - kr[i] * y[i];  // dgc
-      if (live) {
-        store8_global<T>(dv + roff + cb, z);
-        store8_global<T>(dv + roff + cb + 8, z + 8);
-        store8_global<T>(dq + roff + cb, x);
-        store8_global<T>(dq + roff + cb + 8, x + 8);
-        store8_global<T>(dk + roff + cb, y);
-        store8_global<T>(dk + roff + cb + 8, y + 8);
-      }
-    }
-  }
-  fence_before();
+          for (int p = 0; p < 4; ++p) {
+            const int r = ep.row(p);
+            if (r < x.len) st2_global<T>(dv + base + (int64_t)r * H * D + ep.col(p), z[2 * p], z[2 * p + 1]);
+          }
+        }
+        wait_mma(&mbar[0], phase);
+        {
+          float a[8], b[8];
+          ep.load(tb, a);
+          ep.load(tb + 64, b);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int r = ep.row(p), c = ep.col(p);
+            float* e = G.E + r * LDG + c;
+            const float e0 = e[0], e1 = e[1];
+            const float q0 = a[2 * p] * (scale * e0), q1 = a[2 * p + 1] * (scale * e1);
+            const float k0 = __fdividef(b[2 * p], e0), k1 = __fdividef(b[2 * p + 1], e1);
+            float rq0, rq1, rk0, rk1;
+            ld2_tile<T>(rQ, r, c, rq0, rq1);
+            ld2_tile<T>(rK, r, c, rk0, rk1);
+            e[0] = rq0 * q0 - rk0 * k0;  // dgc
+            e[1] = rq1 * q1 - rk1 * k1;
+            if (r < x.len) {
+              const int64_t off = base + (int64_t)r * H * D + c;
+              st2_global<T>(dq + off, q0, q1);
+              st2_global<T>(dk + off, k0, k1);
+            }
+          }
+        }
+        fence_before();
+        __syncthreads();
+        // dg = reverse cumulative sum over rows of dgc (+ dgL at every row): NG groups of RG rows
+        {
+          const int c = tid & 63, qt = tid >> 6;
+          float y[RG];
+          float run = 0.f;
+#pragma unroll
+          for (int i = RG - 1; i >= 0; --i) {
+            run += G.E[(RG * qt + i) * LDG + c];
+            y[i] = run;
+          }
+          G.part[qt][c] = run;
+          __syncthreads();
+          float after = s_dgl[c];
+          for (int j = qt + 1; j < NG; ++j) after += G.part[j][c];
+          float* dst = dg + base + (int64_t)RG * qt * H * D + c;
+#pragma unroll
+          for (int i = 0; i < RG; ++i)
+            if (RG * qt + i < x.len) dst[(int64_t)i * H * D] = y[i] + after;
+        }
+      });
   __syncthreads();
+  fence_after();
   if (warp == 0) tmem_dealloc(tb, 256);
-  // dg = reverse cumulative sum over rows of dgc (+ dgL at every row): 4 quarters of 16 rows
-  {
-    const int c = tid & 63, qt = tid >> 6;
-    float s = 0.f;
-    for (int r = 16 * qt + 15; r >= 16 * qt; --r) { s += G.E[r * LDG + c]; G.E[r * LDG + c] = s; }
-    G.part[qt][c] = s;
-    __syncthreads();
-    float after = s_dgl[c];
-    for (int j = qt + 1; j < 4; ++j) after += G.part[j][c];
-    for (int r = 16 * qt; r < 16 * qt + 16; ++r) G.E[r * LDG + c] += after;
-    __syncthreads();
-    for (int e = tid; e < len * D; e += NT) {
-      const int r = e >> 6, cc = e & 63;
-      dg[((t0 + r) * H + head) * (int64_t)D + cc] = G.E[r * LDG + cc];
-    }
-  }
 }
 
 template <typename K_>
 int prepare(K_ kern, size_t smem) {
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess) {
     set_error("chunk_gla tensor-core kernel: cannot reserve %zu bytes of shared memory", smem);
     return SSLA_ERR_CUDA;
   }
+  return SSLA_OK;
+}
+
+// Persistent grid: as many CTAs as fit on the device at once (shared memory and TMEM columns
+// permitting), capped by the number of items.
+template <typename K_>
+int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned& grid) {
+  int rc = prepare(kern, smem);
+  if (rc) return rc;
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem) != cudaSuccess || per_sm < 1) {
+    set_error("chunk_gla tensor-core kernel: occupancy query failed");
+    return SSLA_ERR_CUDA;
+  }
+  if (per_sm * tmem_cols > 512) per_sm = 512 / tmem_cols;
+  const int64_t cap = (int64_t)per_sm * sms;
+  grid = (unsigned)(items < cap ? items : cap);
   return SSLA_OK;
 }
 
@@ -609,7 +744,14 @@ int prepare(K_ kern, size_t smem) {
     return __VA_ARGS__();                                                               \
   }()
 
-constexpr size_t kGateBytes = sizeof(GateSmem);
+// Item indices are 32-bit.
+int check_items(int64_t MC, int64_t H) {
+  if (MC * H >= (int64_t)1 << 31) {
+    set_error("chunk_gla tensor-core kernels: %lld chunk-heads exceed the 2^31 item limit", (long long)(MC * H));
+    return SSLA_ERR_UNSUPPORTED;
+  }
+  return SSLA_OK;
+}
 
 }  // namespace
 
@@ -621,14 +763,16 @@ int tc_supported(int dtype, int dtype_g, int64_t K, int64_t V) {
 int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src,
                    const void* g, const int64_t* cu, const longlong2* chunk_tab, int64_t N,
                    int64_t MC, int64_t H, float scale, float* dS, float* decay, cudaStream_t s) {
+  if (MC * H == 0) return SSLA_OK;
+  if (int rc = check_items(MC, H)) return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
     auto kern = tc_local_state_kernel<T, Tg>;
-    const size_t smem = 2 * TILE + GRAW + kGateBytes;
-    int rc = prepare(kern, smem);
+    const size_t smem = 2 * ls_stage_bytes<Tg>() + kGateBytes;
+    unsigned grid = 0;
+    int rc = persistent_grid(kern, smem, 64, MC * H, grid);
     if (rc) return rc;
-    kern<<<dim3((unsigned)MC, (unsigned)H), NT, smem, s>>>(mode, (const T*)a_src, (const T*)b_src,
-                                                         (const Tg*)g, cu, chunk_tab, N, (int)H,
-                                                         scale, dS, decay);
+    kern<<<grid, NT, smem, s>>>(mode, (const T*)a_src, (const T*)b_src, (const Tg*)g, chunk_tab, (int)MC,
+                                (int)H, scale, dS, decay);
     SSLA_CHECK_LAUNCH("chunk_gla tc_local_state");
     return SSLA_OK;
   });
@@ -637,14 +781,16 @@ int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const vo
 int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
              const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
              float scale, const float* states, void* o, int* flags, cudaStream_t s) {
+  if (MC * H == 0) return SSLA_OK;
+  if (int rc = check_items(MC, H)) return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
     auto kern = tc_fwd_o_kernel<T, Tg>;
-    const size_t smem = 5 * TILE + GRAW + kGateBytes;
-    int rc = prepare(kern, smem);
+    const size_t smem = 2 * fo_stage_bytes<Tg>() + TILE + kGateBytes;
+    unsigned grid = 0;
+    int rc = persistent_grid(kern, smem, 128, MC * H, grid);
     if (rc) return rc;
-    kern<<<dim3((unsigned)MC, (unsigned)H), NT, smem, s>>>((const T*)q, (const T*)k, (const T*)v,
-                                                         (const Tg*)g, cu, chunk_tab, N, (int)H,
-                                                         scale, states, (T*)o, flags);
+    kern<<<grid, NT, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, chunk_tab, (int)MC,
+                                (int)H, scale, states, (T*)o, flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_fwd_o");
     return SSLA_OK;
   });
@@ -654,14 +800,17 @@ int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, 
            const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
            float scale, const float* states, const float* dstates, const void* dout, void* dq,
            void* dk, void* dv, float* dg, int* flags, cudaStream_t s) {
+  if (MC * H == 0) return SSLA_OK;
+  if (int rc = check_items(MC, H)) return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
     auto kern = tc_bwd_kernel<T, Tg>;
-    const size_t smem = 8 * TILE + GRAW + kGateBytes;
-    int rc = prepare(kern, smem);
+    const size_t smem = 2 * bw_stage_bytes<Tg>() + 4 * TILE + kGateBytes;
+    unsigned grid = 0;
+    int rc = persistent_grid(kern, smem, 256, MC * H, grid);
     if (rc) return rc;
-    kern<<<dim3((unsigned)MC, (unsigned)H), NT, smem, s>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, chunk_tab, N, (int)H, scale, states,
-        dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, flags);
+    kern<<<grid, NT, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, chunk_tab, (int)MC,
+                                (int)H, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv,
+                                dg, flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_bwd");
     return SSLA_OK;
   });

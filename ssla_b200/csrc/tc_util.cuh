@@ -119,6 +119,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16x256b.x2 load (warp-collective): 16 TMEM lanes x 16 columns spread over the 32 threads.
+// Thread t receives pairs p = 0..3: v[2p], v[2p+1] = lane (t/4) + 8*(p&1), columns
+// 2*(t%4) + 8*(p>>1) + {0, 1} (relative to the address's lane and column).
+__device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Base descriptors of a 64-column blocked tile (k-step s adds 16*s / 128*s to the K-major /
+// MN-major descriptor: the start-address field counts 16-byte units).
+__device__ __forceinline__ uint64_t desc_k64(const void* tile) { return smem_desc(smem_u32(tile), 128u, 1024u); }
+__device__ __forceinline__ uint64_t desc_mn64(const void* tile) { return smem_desc(smem_u32(tile), 1024u, 128u); }
+
 // TMEM address of (row block of warp w, column c) for an M=64 accumulator at base column.
 __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp, int col) {
   return base + ((uint32_t)(32 * warp) << 16) + (uint32_t)col;
