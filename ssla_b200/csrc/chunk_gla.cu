@@ -821,11 +821,11 @@ extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, c
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
   if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
-  const bool tc = tc_supported(dtype, dtype_g, K, V);
+  const void* in[4] = {q, k, v, g};
+  const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 4);
   if (MC > 0) {
     if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
-                          w.dS, w.decay, s);
+      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, w.chunk_tab, T, MC, H, scale, w.dS, w.decay, s);
     } else {
       rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
         return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
@@ -840,8 +840,7 @@ extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, c
     return rc;
   if (MC == 0) return SSLA_OK;
   if (tc) {
-    if ((rc = tc_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
-                       states, o, w.flags, s)))
+    if ((rc = tc_fwd_o(dtype, dtype_g, q, k, v, g, w.chunk_tab, T, MC, H, scale, states, o, w.flags, s)))
       return rc;
     return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V,
                       scale, states, o, w.flags, s);
@@ -872,11 +871,11 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
   if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
-  const bool tc = tc_supported(dtype, dtype_g, K, V);
+  const void* in[5] = {q, k, v, g, dout};
+  const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 5);
   if (MC > 0) {
     if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H,
-                          scale, w.dS, w.decay, s);
+      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, w.chunk_tab, T, MC, H, scale, w.dS, w.decay, s);
     } else {
       rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
         return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
@@ -892,8 +891,8 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
     return rc;
   if (MC == 0) return SSLA_OK;
   if (tc) {
-    if ((rc = tc_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, scale,
-                     states, w.dstates, dout, dq, dk, dv, dg, w.flags, s)))
+    if ((rc = tc_bwd(dtype, dtype_g, q, k, v, g, w.chunk_tab, T, MC, H, scale, states, w.dstates, dout, dq, dk,
+                     dv, dg, w.flags, s)))
       return rc;
     return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V, scale,
                     states, w.dstates, dout, dq, dk, dv, dg, w.flags, s);

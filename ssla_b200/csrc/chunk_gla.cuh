@@ -90,16 +90,18 @@ int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v
 // Tensor-core (tcgen05) implementation for 16-bit inputs with K = V = 64 (chunk_gla_tc.cu).
 // tc_fwd_o / tc_bwd write flags[cid*H+head] = 1 for chunks they leave to the exact kernels.
 int tc_supported(int dtype, int dtype_g, int64_t K, int64_t V);
-int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src,
-                   const void* g, const int64_t* cu, const longlong2* chunk_tab, int64_t N,
-                   int64_t MC, int64_t H, float scale, float* dS, float* decay, cudaStream_t s);
+// 1 when every pointer is 16-byte aligned (TMA base addresses).
+int tc_aligned(const void* const* ptrs, int n);
+int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src, const void* g,
+                   const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, float* dS,
+                   float* decay, cudaStream_t s);
 int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
-             const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
-             float scale, const float* states, void* o, int* flags, cudaStream_t s);
+             const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, const float* states,
+             void* o, int* flags, cudaStream_t s);
 int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
-           const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
-           float scale, const float* states, const float* dstates, const void* dout, void* dq,
-           void* dk, void* dv, float* dg, int* flags, cudaStream_t s);
+           const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, const float* states,
+           const float* dstates, const void* dout, void* dq, void* dk, void* dv, float* dg, int* flags,
+           cudaStream_t s);
 
 }  // namespace chunk
 }  // namespace ssla

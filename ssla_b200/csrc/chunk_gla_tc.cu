@@ -2,10 +2,14 @@
 //
 // Work item = (64-token chunk, head).  Every kernel is persistent: a CTA of 512 threads
 // (16 warps) walks items blockIdx.x, blockIdx.x + gridDim.x, ... and, while it computes one
-// item, the next item's tiles are already in flight (cp.async) into the other of two
-// shared-memory stages.  Inputs land straight in 16-bit operand tiles stored "8x8 blocked"
-// (see tc_util.cuh); 16-byte chunks are walked in storage order so shared-memory accesses are
-// conflict-free.  One thread issues 64x64x16 tcgen05.mma instructions into fp32 TMEM
+// item, the next item's tiles are already in flight into the other of two shared-memory
+// stages.  Loads are TMA: warp 0 issues one tensor copy per 64x64 tile (q/k/v/do, the gate)
+// and two per fp32 chunk state, completing on the stage's mbarrier, so no thread waits on a
+// copy it issued.  Tiles use the 128-byte swizzle: row r occupies bytes r*128 .. r*128+127
+// with its 16-byte piece j stored at piece position j ^ (r % 8).  A 16-bit tile then serves
+// as a K-major operand (rows = M/N) or an MN-major operand (rows = K) of tcgen05.mma through
+// SWIZZLE_128B descriptors, and threads that touch piece j of 8 consecutive rows hit 8
+// different bank groups.  One thread issues 64x64x16 tcgen05.mma instructions into fp32 TMEM
 // accumulators; the epilogues read TMEM with the 16x256b shape, so all 32 lanes of a warp
 // carry data (an M=64 accumulator fills lanes 0-15 of each TMEM subpartition).  Warps w, w+4,
 // w+8, w+12 share subpartition w % 4 and take 16 accumulator columns each.
@@ -22,6 +26,8 @@
 // mode 1 dS = (scale q exp(gc))^T do, with per-element exponents.  Every factor of the output
 // and backward kernels is bounded by exp(span/2), span = the chunk's decay range; a chunk with
 // span > kTcSpan is flagged and recomputed by the exact CUDA-core kernels (chunk_gla.cu).
+#include <cuda.h>
+
 #include "chunk_gla.cuh"
 #include "tc_util.cuh"
 
@@ -40,8 +46,7 @@ constexpr int EPI_COLS = D / (NWARP / 4);  // accumulator columns per warp in th
 constexpr int LDG = D + 1;                 // fp32 gate tile stride
 constexpr float kTcSpan = 40.f;
 constexpr int TILE = BT * D * 2;           // bytes of one 64x64 16-bit tile
-constexpr int SP = D + 4;                  // padded row stride (floats) of a staged fp32 state
-constexpr int STATE = D * SP * 4;          // bytes of one staged fp32 state
+constexpr int STATE = D * D * 4;           // bytes of one staged fp32 state (two 32-column halves)
 static_assert(EPI_COLS == 16, "epilogues read 16 columns per warp (16x256b.x2)");
 static_assert(NT == BT * D / 8, "staging assumes one 16-byte chunk of a 16-bit tile per thread");
 
@@ -72,25 +77,30 @@ template <typename T> __device__ __forceinline__ uint4 pack8(const float* x) {
   return u;
 }
 
-// Two adjacent elements (r, c), (r, c+1) of an 8x8-blocked 16-bit tile (c even).
+// Byte offset of element (r, c) of a 128-byte-swizzled 64x64 16-bit tile.
+__device__ __forceinline__ int toff(int r, int c) { return (r << 7) + ((((c >> 3) ^ r) & 7) << 4) + ((c & 7) << 1); }
+
+// SWIZZLE_128B descriptors of such a tile (1024-byte aligned).  Within one 64x64x16 MMA the
+// only stride the tensor core needs is between groups of 8 rows along the tile (1024 bytes;
+// given as both LBO and SBO).  A k-step of 16 elements advances the start address by 32 bytes
+// (K-major: within the swizzled row) or 2048 bytes (MN-major: 16 rows).
+__device__ __forceinline__ uint64_t desc_sw128(const void* tile) {
+  return smem_desc(smem_u32(tile), 1024u, 1024u) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ uint64_t desc_k(const void* tile) { return desc_sw128(tile); }
+__device__ __forceinline__ uint64_t desc_mn(const void* tile) { return desc_sw128(tile); }
+
+// Two adjacent elements (r, c), (r, c+1) of a 16-bit tile (c even).
 template <typename T> __device__ __forceinline__ void st2_tile(unsigned char* tile, int r, int c, float a, float b) {
-  *reinterpret_cast<uint32_t*>(tile + blk_off(r, c, D)) = pack2<T>(a, b);
+  *reinterpret_cast<uint32_t*>(tile + toff(r, c)) = pack2<T>(a, b);
 }
 template <typename T> __device__ __forceinline__ void ld2_tile(const unsigned char* tile, int r, int c, float& a, float& b) {
-  unpack2<T>(*reinterpret_cast<const uint32_t*>(tile + blk_off(r, c, D)), a, b);
+  unpack2<T>(*reinterpret_cast<const uint32_t*>(tile + toff(r, c)), a, b);
 }
 template <typename T> __device__ __forceinline__ void st2_global(T* p, float a, float b) {
   *reinterpret_cast<uint32_t*>(p) = pack2<T>(a, b);
 }
 
-// 16-byte chunk e of a 64-column blocked tile, in storage order (byte 16 e): its row and first
-// column.  Consecutive lanes then touch consecutive 16-byte words of shared memory; on the
-// global side 8 lanes read the same 16 bytes of 8 consecutive rows.
-__device__ __forceinline__ void chunk_rc(int e, int& r, int& c) {
-  const int m = e >> 3;
-  r = ((m >> 3) << 3) | (e & 7);
-  c = (m & 7) << 3;
-}
 
 struct GateSmem {
   float E[BT * LDG];  // exp(gc - ref) (or gc itself for local_state); dgc scratch in the backward
@@ -103,57 +113,55 @@ struct GateSmem {
 };
 constexpr size_t kGateBytes = sizeof(GateSmem);
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
-// Per-thread staging geometry, fixed for the kernel's lifetime: this thread's chunk of every
-// 16-bit tile (row tr, column tc) and its offset within an item's [64, H, 64] token block.
-struct Stager {
-  int tr, tc, toff;
-  __device__ __forceinline__ Stager(int H) {
-    chunk_rc(threadIdx.x, tr, tc);
-    toff = tr * H * D + tc;
-  }
-  // One 64x64 16-bit tile of the item whose first element is `base` (rows >= len zero-filled).
-  template <typename T>
-  __device__ __forceinline__ void tile(unsigned char* dst, const T* __restrict__ base, int len) const {
-    const bool ok = tr < len;
-    cp_async16(dst + 16 * threadIdx.x, ok ? base + toff : base, ok);
-  }
+// Thread t owns the 16-byte piece of row tr = t % 64, columns tc .. tc+7 (tc = 8 * (t / 64))
+// of every 16-bit tile in the gating and state-conversion passes (byte toff(tr, tc)).
+struct Own {
+  int tr, tc;
+  int off;
+  __device__ __forceinline__ Own() : tr(threadIdx.x & 63), tc((threadIdx.x >> 6) << 3), off(toff(tr, tc)) {}
 };
 
-// The raw gate tile of the item, row-major (element type Tg).
+// Issued by warp 0: n16 16-bit tiles (tensor maps m16[i], 3-D views (D, H, T) of the token
+// arrays, box 64 x 1 x 64) into dst16 + i*TILE, the raw gate (map mg, unswizzled), and nstate
+// fp32 states (2-D map ms over [items * 64 rows, 64], two 32-column boxes each) into sdst[i],
+// all completing on `bar`.
+__device__ __forceinline__ void issue_loads(unsigned char* dst16, const CUtensorMap* const* m16, int n16,
+                                            unsigned char* graw, const CUtensorMap* mg, uint32_t gbytes,
+                                            unsigned char* const* sdst, const CUtensorMap* const* ms, int nstate,
+                                            int srow, int64_t t0, int head, uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) mbar_arrive_expect_tx(bar, n16 * TILE + gbytes + nstate * STATE);
+  __syncwarp();
+  if (lane < n16) tma_load_3d(dst16 + lane * TILE, m16[lane], 0, head, (int)t0, bar);
+  if (lane == 8) tma_load_3d(graw, mg, 0, head, (int)t0, bar);
+  if (lane >= 16 && lane < 16 + 2 * nstate) {
+    const int j = lane - 16;
+    tma_load_2d(sdst[j >> 1] + (j & 1) * (STATE / 2), ms[j >> 1], (j & 1) * 32, srow, bar);
+  }
+}
+
+// Rows >= len of a partial chunk (the TMA box reads past the chunk): zero them in the 16-bit
+// tiles and the raw gate.
 template <typename Tg>
-__device__ __forceinline__ void stage_gate(unsigned char* raw, const Tg* __restrict__ base, int len, int H) {
+__device__ __forceinline__ void zero_tail(unsigned char* dst16, int n16, unsigned char* graw, int len) {
+  const Own me;
+  if (me.tr >= len)
+    for (int i = 0; i < n16; ++i) *reinterpret_cast<uint4*>(dst16 + i * TILE + me.off) = make_uint4(0, 0, 0, 0);
   constexpr int PER_ROW = D * (int)sizeof(Tg) / 16;
 #pragma unroll
   for (int j = 0; j < BT * PER_ROW / NT; ++j) {
     const int e = threadIdx.x + j * NT;
-    const int r = e / PER_ROW, c = (e % PER_ROW) * (16 / (int)sizeof(Tg));
-    const bool ok = r < len;
-    cp_async16(raw + 16 * e, ok ? base + r * H * D + c : base, ok);
+    if (e / PER_ROW >= len) *reinterpret_cast<uint4*>(graw + 16 * e) = make_uint4(0, 0, 0, 0);
   }
 }
 
-// A contiguous fp32 [64, 64] state into shared memory (row stride SP floats).
-__device__ __forceinline__ void stage_state(float* dst, const float* __restrict__ src) {
-#pragma unroll
-  for (int j = 0; j < D * D / 4 / NT; ++j) {
-    const int e = threadIdx.x + j * NT;
-    cp_async16(dst + (e >> 4) * SP + (e & 15) * 4, src + 4 * e, true);
-  }
-}
-
-// This thread's 8 values of a staged fp32 state: row tr, columns tc .. tc+7 (its chunk of the
-// 16-bit tile it will write).
-__device__ __forceinline__ void state_regs(const float* src, const Stager& sg, float* v) {
-  const float4* p = reinterpret_cast<const float4*>(src + sg.tr * SP + sg.tc);
-  const float4 a = p[0], b = p[1];
+// This thread's 8 values of a staged fp32 state: row tr, columns tc .. tc+7 (two 16-byte
+// pieces of a 128-byte-swizzled 32-column half).
+__device__ __forceinline__ void state_regs(const unsigned char* src, const Own& me, float* v) {
+  const unsigned char* h = src + (me.tc >> 5) * (STATE / 2) + (me.tr << 7);
+  const int j = (me.tc & 31) >> 2;
+  const float4 a = *reinterpret_cast<const float4*>(h + (((j ^ me.tr) & 7) << 4));
+  const float4 b = *reinterpret_cast<const float4*>(h + ((((j + 1) ^ me.tr) & 7) << 4));
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
@@ -223,13 +231,12 @@ __device__ __forceinline__ void wait_mma(uint64_t* mbar, uint32_t& phase) {
   fence_after();
 }
 
-// Four k-steps (K = 64) of D (+)= A * B^T; operands are 64-column blocked tiles read K-major
-// or MN-major.
+// Four k-steps (K = 64) of D (+)= A * B^T; operands are 64x64 tiles read K-major or MN-major.
 __device__ __forceinline__ void mma64(uint32_t d, const void* a, int a_mn, const void* b, int b_mn,
                                       uint32_t idesc, bool accumulate) {
-  const uint64_t da = a_mn ? desc_mn64(a) : desc_k64(a);
-  const uint64_t db = b_mn ? desc_mn64(b) : desc_k64(b);
-  const uint64_t sa = a_mn ? 128u : 16u, sb = b_mn ? 128u : 16u;
+  const uint64_t da = a_mn ? desc_mn(a) : desc_k(a);
+  const uint64_t db = b_mn ? desc_mn(b) : desc_k(b);
+  const uint64_t sa = a_mn ? 128u : 2u, sb = b_mn ? 128u : 2u;
 #pragma unroll
   for (int s = 0; s < 4; ++s) mma_f16(d, da + s * sa, db + s * sb, idesc, (accumulate || s > 0) ? 1u : 0u);
 }
@@ -238,13 +245,13 @@ __device__ __forceinline__ void mma64(uint32_t d, const void* a, int a_mn, const
 // dK (which may be the source tiles themselves).
 template <typename T>
 __device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned char* sK, unsigned char* dQ,
-                                        unsigned char* dK, const GateSmem& G, const Stager& sg, float scale) {
-  const int off = 16 * threadIdx.x;
+                                        unsigned char* dK, const GateSmem& G, const Own& me, float scale) {
+  const int off = me.off;
   const uint4 uq = *reinterpret_cast<const uint4*>(sQ + off);
   const uint4 uk = *reinterpret_cast<const uint4*>(sK + off);
   const T* xq = reinterpret_cast<const T*>(&uq);
   const T* xk = reinterpret_cast<const T*>(&uk);
-  const float* e = G.E + sg.tr * LDG + sg.tc;
+  const float* e = G.E + me.tr * LDG + me.tc;
   float yq[8], yk[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -272,6 +279,13 @@ struct Epi {
     tmem_ld16x256b_x2(tmem_addr(tbase, sp, c0), v);
   }
 };
+
+// The 128-byte swizzle is anchored at 1024-byte boundaries: kernels align their dynamic
+// shared memory explicitly (launchers reserve kAlignSlack extra bytes).
+constexpr size_t kAlignSlack = 1024;
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
 
 // --------------------------------------------------------------------------- persistent loop
 struct Item {
@@ -305,11 +319,13 @@ __device__ __forceinline__ bool decode_item(const Cursor& c, longlong2 e, Item& 
 }
 
 // Valid chunks form a prefix of the chunk table, so a CTA stops at its first invalid item.
-// The table entry of the item after next is loaded one iteration before it is decoded.
-template <class Load, class Proc>
-__device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* __restrict__ tab, Load load,
-                                                Proc proc) {
+// `issue(item, stage)` runs on warp 0 and starts the item's copies on full[stage];
+// `zero(item, stage)` clears rows past a partial chunk; `proc(item, stage)` computes.
+template <class Issue, class Zero, class Proc>
+__device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* __restrict__ tab, uint64_t* full,
+                                                Issue issue, Zero zero, Proc proc) {
   const int G = gridDim.x, gq = G / H, gr = G % H;
+  const bool w0 = threadIdx.x < 32;
   Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
   Cursor c1 = c, c2;
   c1.advance(gq, gr, H);
@@ -318,17 +334,19 @@ __device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* 
   Item cur;
   bool have = decode_item(c, item_entry(c, MC, tab), cur);
   longlong2 e_next = item_entry(c1, MC, tab);
-  if (have) load(cur, 0);
-  cp_async_commit();
+  if (have && w0) issue(cur, 0);
   for (int i = 0; have; ++i) {
     const longlong2 e_after = item_entry(c2, MC, tab);
     Item nxt;
     const bool nhave = decode_item(c1, e_next, nxt);
-    if (nhave) load(nxt, (i + 1) & 1);
-    cp_async_commit();
-    cp_async_wait_prev();
-    __syncthreads();
+    if (nhave && w0) issue(nxt, (i + 1) & 1);
+    mbar_wait(&full[i & 1], (i >> 1) & 1);
+    if (cur.len < BT) {
+      zero(cur, i & 1);
+      __syncthreads();
+    }
     proc(cur, i & 1);
+    fence_proxy_async();  // generic writes to this stage before the TMA refills it
     __syncthreads();
     cur = nxt;
     have = nhave;
@@ -336,7 +354,6 @@ __device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* 
     c1 = c2;
     c2.advance(gq, gr, H);
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // --------------------------------------------------------------------------- local state
@@ -345,45 +362,54 @@ template <typename Tg> __host__ __device__ constexpr int ls_stage_bytes() { retu
 
 template <typename T, typename Tg>
 __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
-    int mode, const T* __restrict__ a_src, const T* __restrict__ b_src, const Tg* __restrict__ g,
-    const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, float* __restrict__ dS,
-    float* __restrict__ decay) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+    const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
+    const __grid_constant__ CUtensorMap mg, int mode, const longlong2* __restrict__ chunk_tab, int MC, int H,
+    float scale, float* __restrict__ dS, float* __restrict__ decay) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = ls_stage_bytes<Tg>();
   GateSmem& G = *reinterpret_cast<GateSmem*>(smem + 2 * STAGE);
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, full[2];
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) tmem_alloc(&tbase_s, 64);
-  mbar_setup(&mbar, 1);
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
   fence_after();
   const uint32_t tb = tbase_s;
   uint32_t phase = 0;
   const Epi ep;
-  const Stager sg(H);
+  const Own me;
+  const CUtensorMap* m16[2] = {&ma, &mb};
   persistent_loop(
-      MC, H, chunk_tab,
+      MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
         unsigned char* b = smem + st * STAGE;
-        const int64_t base = (x.t0 * H + x.head) * D;
-        sg.tile<T>(b, a_src + base, x.len);
-        sg.tile<T>(b + TILE, b_src + base, x.len);
-        stage_gate<Tg>(b + 2 * TILE, g + base, x.len, H);
+        issue_loads(b, m16, 2, b + 2 * TILE, &mg, BT * D * sizeof(Tg), nullptr, nullptr, 0, 0, x.t0, x.head,
+                    &full[st]);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        zero_tail<Tg>(b, 2, b + 2 * TILE, x.len);
       },
       [&](const Item& x, int st) {
         unsigned char* sA = smem + st * STAGE;
         unsigned char* sB = sA + TILE;
         gate_prep<Tg, true>(G, sB + TILE);
         {
-          uint4* p = reinterpret_cast<uint4*>(sA + 16 * tid);
+          uint4* p = reinterpret_cast<uint4*>(sA + me.off);
           const uint4 u = *p;
           const T* xs = reinterpret_cast<const T*>(&u);
-          const float* gc = G.E + sg.tr * LDG + sg.tc;
+          const float* gc = G.E + me.tr * LDG + me.tc;
           float y[8];
           if (mode == 0) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * __expf(G.gl[sg.tc + i] - gc[i]);
+            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * __expf(G.gl[me.tc + i] - gc[i]);
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * (scale * __expf(gc[i]));
@@ -417,35 +443,45 @@ template <typename Tg> __host__ __device__ constexpr int fo_stage_bytes() { retu
 
 template <typename T, typename Tg>
 __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
-    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
-    const float* __restrict__ states, T* __restrict__ o, int* __restrict__ flags) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mg,
+    const __grid_constant__ CUtensorMap mh, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
+    T* __restrict__ o, int* __restrict__ flags) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = fo_stage_bytes<Tg>();
   unsigned char* sA = smem + 2 * STAGE;
   GateSmem& G = *reinterpret_cast<GateSmem*>(sA + TILE);
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar, full[2];
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) tmem_alloc(&tbase_s, 128);
-  mbar_setup(&mbar, 1);
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
   fence_after();
   const uint32_t tb = tbase_s;
   uint32_t phase = 0;
   const Epi ep;
-  const Stager sg(H);
+  const Own me;
+  const CUtensorMap* m16[3] = {&mq, &mk, &mv};
   constexpr uint32_t F = Fmt<T>::v;
   persistent_loop(
-      MC, H, chunk_tab,
+      MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
         unsigned char* b = smem + st * STAGE;
-        const int64_t base = (x.t0 * H + x.head) * D;
-        sg.tile<T>(b, q + base, x.len);
-        sg.tile<T>(b + TILE, k + base, x.len);
-        sg.tile<T>(b + 2 * TILE, v + base, x.len);
-        stage_state(reinterpret_cast<float*>(b + 3 * TILE), states + ((int64_t)x.cid * H + x.head) * D * D);
-        stage_gate<Tg>(b + 3 * TILE + STATE, g + base, x.len, H);
+        unsigned char* sd[1] = {b + 3 * TILE};
+        const CUtensorMap* ms[1] = {&mh};
+        issue_loads(b, m16, 3, b + 3 * TILE + STATE, &mg, BT * D * sizeof(Tg), sd, ms, 1, (x.cid * H + x.head) * D,
+                    x.t0, x.head, &full[st]);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        zero_tail<Tg>(b, 3, b + 3 * TILE + STATE, x.len);
       },
       [&](const Item& x, int st) {
         unsigned char* sQ = smem + st * STAGE;
@@ -453,19 +489,19 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
         unsigned char* sV = sK + TILE;
         unsigned char* sH = sV + TILE;
         float hreg[8];
-        state_regs(reinterpret_cast<const float*>(sH), sg, hreg);
+        state_regs(sH, me, hreg);
         gate_prep<Tg, false>(G, sH + STATE);  // its barriers order the state reads before sH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
         if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
         if (exact) return;
-        gate_qk<T>(sQ, sK, sQ, sK, G, sg, scale);
+        gate_qk<T>(sQ, sK, sQ, sK, G, me, scale);
         operands_ready();
         if (tid == 0) mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);  // A = Q^ K^^T
         {
-          const float er = G.eref[sg.tr];
+          const float er = G.eref[me.tr];
 #pragma unroll
           for (int i = 0; i < 8; ++i) hreg[i] *= er;
-          *reinterpret_cast<uint4*>(sH + 16 * tid) = pack8<T>(hreg);
+          *reinterpret_cast<uint4*>(sH + me.off) = pack8<T>(hreg);
         }
         operands_ready();
         if (tid == 0) {
@@ -513,44 +549,52 @@ template <typename Tg> __host__ __device__ constexpr int bw_stage_bytes() { retu
 
 template <typename T, typename Tg>
 __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
-    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-    const Tg* __restrict__ g, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
-    const float* __restrict__ states, const float* __restrict__ dstates, const T* __restrict__ dout,
-    T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg,
-    int* __restrict__ flags) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+    const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mh,
+    const __grid_constant__ CUtensorMap mdh, const longlong2* __restrict__ chunk_tab, int MC, int H,
+    float scale, T* __restrict__ dq,
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, int* __restrict__ flags) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = bw_stage_bytes<Tg>();
   unsigned char* sQg = smem + 2 * STAGE;
   unsigned char* sKg = sQg + TILE;
   unsigned char* sA = sKg + TILE;
   unsigned char* sdA = sA + TILE;
   GateSmem& G = *reinterpret_cast<GateSmem*>(sdA + TILE);
-  __shared__ uint64_t mbar[2];  // [0]: score batch, then dq / dk;  [1]: dv
+  __shared__ uint64_t mbar[2], full[2];  // mbar[0]: score batch, then dq / dk;  mbar[1]: dv
   __shared__ uint32_t tbase_s;
-  __shared__ float s_hdh[2 * D], s_dgl[D];
+  __shared__ float s_hd8[8][D], s_dgl[D];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (warp == 0) tmem_alloc(&tbase_s, 256);
-  mbar_setup(mbar, 2);
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&mbar[i], 1);
+      mbar_init(&full[i], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
   fence_after();
   const uint32_t tb = tbase_s;
   uint32_t phase = 0, phase_dv = 0;
   const Epi ep;
-  const Stager sg(H);
+  const Own me;
+  const CUtensorMap* m16[4] = {&mq, &mk, &mv, &mdo};
   constexpr uint32_t F = Fmt<T>::v;
   persistent_loop(
-      MC, H, chunk_tab,
+      MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
         unsigned char* b = smem + st * STAGE;
-        const int64_t base = (x.t0 * H + x.head) * D;
-        const int64_t soff = ((int64_t)x.cid * H + x.head) * D * D;
-        sg.tile<T>(b, q + base, x.len);
-        sg.tile<T>(b + TILE, k + base, x.len);
-        sg.tile<T>(b + 2 * TILE, v + base, x.len);
-        sg.tile<T>(b + 3 * TILE, dout + base, x.len);
-        stage_state(reinterpret_cast<float*>(b + 4 * TILE), states + soff);
-        stage_state(reinterpret_cast<float*>(b + 4 * TILE + STATE), dstates + soff);
-        stage_gate<Tg>(b + 4 * TILE + 2 * STATE, g + base, x.len, H);
+        unsigned char* sd[2] = {b + 4 * TILE, b + 4 * TILE + STATE};
+        const CUtensorMap* ms[2] = {&mh, &mdh};
+        issue_loads(b, m16, 4, b + 4 * TILE + 2 * STATE, &mg, BT * D * sizeof(Tg), sd, ms, 2,
+                    (x.cid * H + x.head) * D, x.t0, x.head, &full[st]);
+      },
+      [&](const Item& x, int st) {
+        unsigned char* b = smem + st * STAGE;
+        zero_tail<Tg>(b, 4, b + 4 * TILE + 2 * STATE, x.len);
       },
       [&](const Item& x, int st) {
         unsigned char* rQ = smem + st * STAGE;
@@ -560,13 +604,13 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         unsigned char* sH = sDO + TILE;
         unsigned char* sDH = sH + STATE;
         float hreg[8], dhreg[8];
-        state_regs(reinterpret_cast<const float*>(sH), sg, hreg);
-        state_regs(reinterpret_cast<const float*>(sDH), sg, dhreg);
+        state_regs(sH, me, hreg);
+        state_regs(sDH, me, dhreg);
         gate_prep<Tg, false>(G, sDH + STATE);  // its barriers order the state reads before sH/sDH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
         if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
         if (exact) return;
-        gate_qk<T>(rQ, rK, sQg, sKg, G, sg, scale);
+        gate_qk<T>(rQ, rK, sQg, sKg, G, me, scale);
         operands_ready();
         if (tid == 0) {
           mma64(tb, sQg, 0, sKg, 0, idesc_f16(64, 64, F, 0, 0), false);       // A  = Q^ K^^T
@@ -576,7 +620,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         }
         // H', dH' tiles and h.dh per row while the score batch runs
         {
-          const float er = G.eref[sg.tr], egl = G.egl[sg.tr];
+          const float er = G.eref[me.tr], egl = G.egl[me.tr];
           float hd = 0.f;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -584,12 +628,9 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
             hreg[i] *= er;
             dhreg[i] *= egl;
           }
-          // lanes l, l^8, l^16, l^24 hold row tr, column blocks 4h .. 4h+3 (h = warp parity)
-          hd += __shfl_xor_sync(0xffffffffu, hd, 8);
-          hd += __shfl_xor_sync(0xffffffffu, hd, 16);
-          if (lane < 8) s_hdh[(sg.tc >> 5) * D + sg.tr] = hd;
-          *reinterpret_cast<uint4*>(sH + 16 * tid) = pack8<T>(hreg);
-          *reinterpret_cast<uint4*>(sDH + 16 * tid) = pack8<T>(dhreg);
+          s_hd8[me.tc >> 3][me.tr] = hd;
+          *reinterpret_cast<uint4*>(sH + me.off) = pack8<T>(hreg);
+          *reinterpret_cast<uint4*>(sDH + me.off) = pack8<T>(dhreg);
         }
         fence_proxy_async();
         __syncthreads();
@@ -634,10 +675,12 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         }
         // dgL per key index: exp(gL) h.dh + dh'.(K^^T v)
         if (tid < D) {
-          float sp = 0.f;
+          float sp = 0.f, hdh = 0.f;
 #pragma unroll
           for (int j = 0; j < NWARP / 4; ++j) sp += G.part[j][tid];
-          s_dgl[tid] = G.eref[tid] * G.egl[tid] * (s_hdh[tid] + s_hdh[D + tid]) + sp;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) hdh += s_hd8[j][tid];
+          s_dgl[tid] = G.eref[tid] * G.egl[tid] * hdh + sp;
         }
         const int64_t base = (x.t0 * H + x.head) * D;
         wait_mma(&mbar[1], phase_dv);
@@ -730,6 +773,62 @@ int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned
   return SSLA_OK;
 }
 
+// ---------------------------------------------------------------------------- tensor maps
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+           const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  const EncodeTiled enc = encode_fn();
+  if (!enc) {
+    set_error("chunk_gla: cuTensorMapEncodeTiled is unavailable");
+    return SSLA_ERR_CUDA;
+  }
+  const cuuint32_t es[3] = {1u, 1u, 1u};
+  const CUresult r = enc(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("chunk_gla: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSLA_ERR_CUDA;
+  }
+  return SSLA_OK;
+}
+
+// 3-D view (D = 64, H, T) of a [T, H, 64] token array, box 64 x 1 x 64: 16-bit operands with
+// the 128-byte swizzle, the gate (any dtype) unswizzled.
+int make_map(CUtensorMap* m, const void* base, int dtype, int64_t T, int64_t H, bool swizzle) {
+  const int eb = dtype == SSLA_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = dtype == SSLA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == SSLA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * eb, (cuuint64_t)H * D * eb};
+  const cuuint32_t box[3] = {(cuuint32_t)D, 1u, (cuuint32_t)BT};
+  return encode(m, dt, 3, base, dims, strides, box, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// 2-D view [rows, 64] of fp32 states (64 rows per (chunk, head)), box 32 columns x 64 rows,
+// 128-byte swizzle.
+int make_state_map(CUtensorMap* m, const float* base, int64_t rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)D};
+  return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 #define SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, ...)                                    \
   [&]() -> int {                                                                        \
     if (dtype == SSLA_BF16) {                                                           \
@@ -744,10 +843,11 @@ int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned
     return __VA_ARGS__();                                                               \
   }()
 
-// Item indices are 32-bit.
-int check_items(int64_t MC, int64_t H) {
-  if (MC * H >= (int64_t)1 << 31) {
-    set_error("chunk_gla tensor-core kernels: %lld chunk-heads exceed the 2^31 item limit", (long long)(MC * H));
+// Item indices and TMA row coordinates are 32-bit.
+int check_sizes(int64_t T, int64_t MC, int64_t H) {
+  if (MC * H * D >= (int64_t)1 << 31 || T >= (int64_t)1 << 31) {
+    set_error("chunk_gla tensor-core kernels: T=%lld or %lld chunk-heads x 64 exceed the 2^31 limit",
+              (long long)T, (long long)(MC * H));
     return SSLA_ERR_UNSUPPORTED;
   }
   return SSLA_OK;
@@ -760,57 +860,78 @@ int tc_supported(int dtype, int dtype_g, int64_t K, int64_t V) {
          K == D && V == D;
 }
 
-int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src,
-                   const void* g, const int64_t* cu, const longlong2* chunk_tab, int64_t N,
-                   int64_t MC, int64_t H, float scale, float* dS, float* decay, cudaStream_t s) {
+int tc_aligned(const void* const* ptrs, int n) {
+  for (int i = 0; i < n; ++i)
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16) return 0;
+  return 1;
+}
+
+int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src, const void* g,
+                   const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, float* dS,
+                   float* decay, cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
-  if (int rc = check_items(MC, H)) return rc;
-  return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
-    auto kern = tc_local_state_kernel<T, Tg>;
-    const size_t smem = 2 * ls_stage_bytes<Tg>() + kGateBytes;
+  if (int rc = check_sizes(T, MC, H)) return rc;
+  CUtensorMap ma, mb, mg;
+  int rc;
+  if ((rc = make_map(&ma, a_src, dtype, T, H, true)) || (rc = make_map(&mb, b_src, dtype, T, H, true)) ||
+      (rc = make_map(&mg, g, dtype_g, T, H, false)))
+    return rc;
+  return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
+    auto kern = tc_local_state_kernel<T_, Tg>;
+    const size_t smem = 2 * ls_stage_bytes<Tg>() + kGateBytes + kAlignSlack;
     unsigned grid = 0;
-    int rc = persistent_grid(kern, smem, 64, MC * H, grid);
-    if (rc) return rc;
-    kern<<<grid, NT, smem, s>>>(mode, (const T*)a_src, (const T*)b_src, (const Tg*)g, chunk_tab, (int)MC,
-                                (int)H, scale, dS, decay);
+    int rc2 = persistent_grid(kern, smem, 64, MC * H, grid);
+    if (rc2) return rc2;
+    kern<<<grid, NT, smem, s>>>(ma, mb, mg, mode, chunk_tab, (int)MC, (int)H, scale, dS, decay);
     SSLA_CHECK_LAUNCH("chunk_gla tc_local_state");
     return SSLA_OK;
   });
 }
 
 int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
-             const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
-             float scale, const float* states, void* o, int* flags, cudaStream_t s) {
+             const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, const float* states,
+             void* o, int* flags, cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
-  if (int rc = check_items(MC, H)) return rc;
-  return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
-    auto kern = tc_fwd_o_kernel<T, Tg>;
-    const size_t smem = 2 * fo_stage_bytes<Tg>() + TILE + kGateBytes;
+  if (int rc = check_sizes(T, MC, H)) return rc;
+  CUtensorMap mq, mk, mv, mg, mh;
+  int rc;
+  if ((rc = make_map(&mq, q, dtype, T, H, true)) || (rc = make_map(&mk, k, dtype, T, H, true)) ||
+      (rc = make_map(&mv, v, dtype, T, H, true)) || (rc = make_map(&mg, g, dtype_g, T, H, false)) ||
+      (rc = make_state_map(&mh, states, MC * H * D)))
+    return rc;
+  return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
+    auto kern = tc_fwd_o_kernel<T_, Tg>;
+    const size_t smem = 2 * fo_stage_bytes<Tg>() + TILE + kGateBytes + kAlignSlack;
     unsigned grid = 0;
-    int rc = persistent_grid(kern, smem, 128, MC * H, grid);
-    if (rc) return rc;
-    kern<<<grid, NT, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, chunk_tab, (int)MC,
-                                (int)H, scale, states, (T*)o, flags);
+    int rc2 = persistent_grid(kern, smem, 128, MC * H, grid);
+    if (rc2) return rc2;
+    kern<<<grid, NT, smem, s>>>(mq, mk, mv, mg, mh, chunk_tab, (int)MC, (int)H, scale, (T_*)o, flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_fwd_o");
     return SSLA_OK;
   });
 }
 
 int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
-           const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
-           float scale, const float* states, const float* dstates, const void* dout, void* dq,
-           void* dk, void* dv, float* dg, int* flags, cudaStream_t s) {
+           const longlong2* chunk_tab, int64_t T, int64_t MC, int64_t H, float scale, const float* states,
+           const float* dstates, const void* dout, void* dq, void* dk, void* dv, float* dg, int* flags,
+           cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
-  if (int rc = check_items(MC, H)) return rc;
-  return SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, [&] {
-    auto kern = tc_bwd_kernel<T, Tg>;
-    const size_t smem = 2 * bw_stage_bytes<Tg>() + 4 * TILE + kGateBytes;
+  if (int rc = check_sizes(T, MC, H)) return rc;
+  CUtensorMap mq, mk, mv, mdo, mg, mh, mdh;
+  int rc;
+  if ((rc = make_map(&mq, q, dtype, T, H, true)) || (rc = make_map(&mk, k, dtype, T, H, true)) ||
+      (rc = make_map(&mv, v, dtype, T, H, true)) || (rc = make_map(&mdo, dout, dtype, T, H, true)) ||
+      (rc = make_map(&mg, g, dtype_g, T, H, false)) || (rc = make_state_map(&mh, states, MC * H * D)) ||
+      (rc = make_state_map(&mdh, dstates, MC * H * D)))
+    return rc;
+  return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
+    auto kern = tc_bwd_kernel<T_, Tg>;
+    const size_t smem = 2 * bw_stage_bytes<Tg>() + 4 * TILE + kGateBytes + kAlignSlack;
     unsigned grid = 0;
-    int rc = persistent_grid(kern, smem, 256, MC * H, grid);
-    if (rc) return rc;
-    kern<<<grid, NT, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, chunk_tab, (int)MC,
-                                (int)H, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv,
-                                dg, flags);
+    int rc2 = persistent_grid(kern, smem, 256, MC * H, grid);
+    if (rc2) return rc2;
+    kern<<<grid, NT, smem, s>>>(mq, mk, mv, mdo, mg, mh, mdh, chunk_tab, (int)MC, (int)H, scale, (T_*)dq,
+                                (T_*)dk, (T_*)dv, dg, flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_bwd");
     return SSLA_OK;
   });

@@ -94,6 +94,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
   return false;
 }
 
+// mbarrier arrive (count 1) that also announces `bytes` of incoming async-copy transactions.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mbar)), "r"(bytes)
+               : "memory");
+}
+
+// TMA tiled load of a 3-D box (no multicast) into shared memory, completing on `mbar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(mbar))
+      : "memory");
+}
+
+// TMA tiled load of a 2-D box (no multicast) into shared memory, completing on `mbar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(mbar))
+      : "memory");
+}
+
+// Bulk (non-tensor) copy global -> shared of `bytes` (multiple of 16, both addresses 16-byte
+// aligned), completing on `mbar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+               : "memory");
+}
+
 // Warp-collective TMEM allocation (ncols: power of two >= 32); address written to *dst.
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
@@ -131,11 +164,6 @@ __device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-// Base descriptors of a 64-column blocked tile (k-step s adds 16*s / 128*s to the K-major /
-// MN-major descriptor: the start-address field counts 16-byte units).
-__device__ __forceinline__ uint64_t desc_k64(const void* tile) { return smem_desc(smem_u32(tile), 128u, 1024u); }
-__device__ __forceinline__ uint64_t desc_mn64(const void* tile) { return smem_desc(smem_u32(tile), 1024u, 128u); }
 
 // TMEM address of (row block of warp w, column c) for an M=64 accumulator at base column.
 __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp, int col) {
