@@ -34,11 +34,15 @@ constexpr int NTHR = 256;
 __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __restrict__ cu,
                                                              int64_t N, int64_t MC,
                                                              int64_t* __restrict__ off,
-                                                             longlong2* __restrict__ tab) {
+                                                             longlong2* __restrict__ tab,
+                                                             int* __restrict__ exact_count) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry = 0;
+  if (tid == 0) {
+    carry = 0;
+    if (exact_count) *exact_count = 0;
+  }
   __syncthreads();
   for (int64_t base = 0; base < N; base += 1024) {
     const int64_t n = base + tid;
@@ -414,7 +418,7 @@ __device__ __forceinline__ void fwd_o_body(int64_t cid, int head,
 }
 
 // Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
-// kernels): a small grid strides over the (chunk, head) pairs and processes flagged ones only.
+// kernels): a small grid strides over the listed (chunk, head) items only (none: it exits).
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
@@ -425,11 +429,11 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
     fwd_o_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
     return;
   }
-  for (int64_t w = blockIdx.x; w < MC * H; w += gridDim.x) {
-    if (flags[w]) {
-      fwd_o_body<T, Tg, P>(w / H, (int)(w % H), q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
-      __syncthreads();
-    }
+  const int n = flags[0];
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int w = flags[1 + i];
+    fwd_o_body<T, Tg, P>(w / H, w % H, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
+    __syncthreads();
   }
 }
 
@@ -632,7 +636,7 @@ __device__ __forceinline__ void bwd_body(int64_t cid, int head,
 }
 
 // Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
-// kernels): a small grid strides over the (chunk, head) pairs and processes flagged ones only.
+// kernels): a small grid strides over the listed (chunk, head) items only (none: it exits).
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) bwd_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
@@ -644,11 +648,11 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
     bwd_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
     return;
   }
-  for (int64_t w = blockIdx.x; w < MC * H; w += gridDim.x) {
-    if (flags[w]) {
-      bwd_body<T, Tg, P>(w / H, (int)(w % H), q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
-      __syncthreads();
-    }
+  const int n = flags[0];
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int w = flags[1 + i];
+    bwd_body<T, Tg, P>(w / H, w % H, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
+    __syncthreads();
   }
 }
 
@@ -755,8 +759,8 @@ int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v
 }
 
 int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chunk_off,
-                         longlong2* chunk_tab, cudaStream_t s) {
-  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, MC, chunk_off, chunk_tab);
+                         longlong2* chunk_tab, int* flags, cudaStream_t s) {
+  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, MC, chunk_off, chunk_tab, flags);
   SSLA_CHECK_LAUNCH("chunk_gla chunk_offsets");
   return SSLA_OK;
 }
@@ -820,7 +824,7 @@ extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, c
   cudaStream_t s = (cudaStream_t)stream;
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, w.flags, s))) return rc;
   const void* in[4] = {q, k, v, g};
   const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 4);
   if (MC > 0) {
@@ -870,7 +874,7 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
   cudaStream_t s = (cudaStream_t)stream;
   Workspace w = carve(workspace, n_seqs, T, H, K, V);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, s))) return rc;
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, w.flags, s))) return rc;
   const void* in[5] = {q, k, v, g, dout};
   const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 5);
   if (MC > 0) {

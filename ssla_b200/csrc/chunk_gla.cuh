@@ -28,14 +28,15 @@ struct Workspace {
   float* dS;           // [MC,H,K,V]  per-chunk state increment (fwd) / its adjoint (bwd)
   float* decay;        // [MC,H,K]    exp(g summed over the chunk)
   float* dstates;      // [MC,H,K,V]  adjoint of the state at the end of each chunk (bwd)
-  int* flags;          // [MC,H]      1 = chunk left to the exact CUDA-core kernel
+  int* flags;          // [1+MC*H]    [0] = number of (chunk, head) items left to the exact
+                       //             CUDA-core kernels, then their ids chunk*H + head
 };
 
 inline size_t workspace_bytes(int64_t N, int64_t T, int64_t H, int64_t K, int64_t V) {
   const int64_t MC = max_chunks(N, T);
   return align256(8 * (N + 1)) + align256(16 * (size_t)(MC > 0 ? MC : 1)) +
          2 * align256(4 * (size_t)MC * H * K * V) +
-         align256(4 * (size_t)MC * H * K) + align256(4 * (size_t)MC * H);
+         align256(4 * (size_t)MC * H * K) + align256(4 * ((size_t)MC * H + 1));
 }
 
 inline Workspace carve(void* base, int64_t N, int64_t T, int64_t H, int64_t K, int64_t V) {
@@ -69,14 +70,15 @@ __device__ __forceinline__ bool locate_chunk(int64_t cid, const longlong2* __res
 }
 
 // Host launchers shared by the CUDA-core and tensor-core implementations (chunk_gla.cu).
+// Also resets the exact-item count flags[0] of the call.
 int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chunk_off,
-                         longlong2* chunk_tab, cudaStream_t s);
+                         longlong2* chunk_tab, int* flags, cudaStream_t s);
 int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_off, int64_t N,
                       int64_t H, int64_t K, int64_t V, const float* init, float* per_chunk,
                       float* final_state, bool reverse, cudaStream_t s);
 
-// CUDA-core per-chunk kernels (chunk_gla.cu).  With `flags` non-null only the chunks whose
-// flag is set are processed (fallback of the tensor-core kernels).
+// CUDA-core per-chunk kernels (chunk_gla.cu).  With `flags` non-null only the items listed
+// there are processed (fallback of the tensor-core kernels).
 int simt_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
                const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
                int64_t K, int64_t V, float scale, const float* states, void* o, const int* flags,
@@ -88,7 +90,7 @@ int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v
              cudaStream_t s);
 
 // Tensor-core (tcgen05) implementation for 16-bit inputs with K = V = 64 (chunk_gla_tc.cu).
-// tc_fwd_o / tc_bwd write flags[cid*H+head] = 1 for chunks they leave to the exact kernels.
+// tc_fwd_o / tc_bwd append the items they leave to the exact kernels to `flags`.
 int tc_supported(int dtype, int dtype_g, int64_t K, int64_t V);
 // 1 when every pointer is 16-byte aligned (TMA base addresses).
 int tc_aligned(const void* const* ptrs, int n);

@@ -25,7 +25,8 @@
 // and for the per-chunk state increments (local_state): mode 0 dS = (k exp(gL - gc))^T v,
 // mode 1 dS = (scale q exp(gc))^T do, with per-element exponents.  Every factor of the output
 // and backward kernels is bounded by exp(span/2), span = the chunk's decay range; a chunk with
-// span > kTcSpan is flagged and recomputed by the exact CUDA-core kernels (chunk_gla.cu).
+// span > kTcSpan is listed in `flags` and recomputed by the exact CUDA-core kernels
+// (chunk_gla.cu).
 #include <cuda.h>
 
 #include "chunk_gla.cuh"
@@ -121,7 +122,7 @@ struct Own {
   __device__ __forceinline__ Own() : tr(threadIdx.x & 63), tc((threadIdx.x >> 6) << 3), off(toff(tr, tc)) {}
 };
 
-// Issued by warp 0: n16 16-bit tiles (tensor maps m16[i], 3-D views (D, H, T) of the token
+// Issued by one warp: n16 16-bit tiles (tensor maps m16[i], 3-D views (D, H, T) of the token
 // arrays, box 64 x 1 x 64) into dst16 + i*TILE, the raw gate (map mg, unswizzled), and nstate
 // fp32 states (2-D map ms over [items * 64 rows, 64], two 32-column boxes each) into sdst[i],
 // all completing on `bar`.
@@ -319,13 +320,15 @@ __device__ __forceinline__ bool decode_item(const Cursor& c, longlong2 e, Item& 
 }
 
 // Valid chunks form a prefix of the chunk table, so a CTA stops at its first invalid item.
-// `issue(item, stage)` runs on warp 0 and starts the item's copies on full[stage];
-// `zero(item, stage)` clears rows past a partial chunk; `proc(item, stage)` computes.
+// `issue(item, stage)` runs on the last warp and starts the item's copies on full[stage];
+// `zero(item, stage)` clears rows past a partial chunk; `proc(item, stage, next)` computes and
+// calls next() (all threads) once its last MMA batch is issued: the last warp then starts the
+// next item's copies while the tensor core runs.  If proc returns without calling it, the loop does.
 template <class Issue, class Zero, class Proc>
 __device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* __restrict__ tab, uint64_t* full,
                                                 Issue issue, Zero zero, Proc proc) {
   const int G = gridDim.x, gq = G / H, gr = G % H;
-  const bool w0 = threadIdx.x < 32;
+  const bool w0 = threadIdx.x >= NT - 32;  // the last warp issues copies (thread 0 issues MMAs)
   Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
   Cursor c1 = c, c2;
   c1.advance(gq, gr, H);
@@ -339,13 +342,18 @@ __device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* 
     const longlong2 e_after = item_entry(c2, MC, tab);
     Item nxt;
     const bool nhave = decode_item(c1, e_next, nxt);
-    if (nhave && w0) issue(nxt, (i + 1) & 1);
+    bool issued = false;
+    auto next = [&] {
+      if (!issued && nhave && w0) issue(nxt, (i + 1) & 1);
+      issued = true;
+    };
     mbar_wait(&full[i & 1], (i >> 1) & 1);
     if (cur.len < BT) {
       zero(cur, i & 1);
       __syncthreads();
     }
-    proc(cur, i & 1);
+    proc(cur, i & 1, next);
+    next();
     fence_proxy_async();  // generic writes to this stage before the TMA refills it
     __syncthreads();
     cur = nxt;
@@ -386,6 +394,8 @@ __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
   const Epi ep;
   const Own me;
   const CUtensorMap* m16[2] = {&ma, &mb};
+  if (tid == 0)
+    for (const CUtensorMap* m : {&ma, &mb, &mg}) prefetch_tensormap(m);
   persistent_loop(
       MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
@@ -397,7 +407,8 @@ __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
         unsigned char* b = smem + st * STAGE;
         zero_tail<Tg>(b, 2, b + 2 * TILE, x.len);
       },
-      [&](const Item& x, int st) {
+      [&](const Item& x, int st, auto& next) {
+        next();  // short items: the next item's copies start right away
         unsigned char* sA = smem + st * STAGE;
         unsigned char* sB = sA + TILE;
         gate_prep<Tg, true>(G, sB + TILE);
@@ -469,6 +480,8 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
   const Epi ep;
   const Own me;
   const CUtensorMap* m16[3] = {&mq, &mk, &mv};
+  if (tid == 0)
+    for (const CUtensorMap* m : {&mq, &mk, &mv, &mg, &mh}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
   persistent_loop(
       MC, H, chunk_tab, full,
@@ -483,7 +496,8 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
         unsigned char* b = smem + st * STAGE;
         zero_tail<Tg>(b, 3, b + 3 * TILE + STATE, x.len);
       },
-      [&](const Item& x, int st) {
+      [&](const Item& x, int st, auto& next) {
+        next();  // short items: the next item's copies start right away
         unsigned char* sQ = smem + st * STAGE;
         unsigned char* sK = sQ + TILE;
         unsigned char* sV = sK + TILE;
@@ -492,8 +506,10 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
         state_regs(sH, me, hreg);
         gate_prep<Tg, false>(G, sH + STATE);  // its barriers order the state reads before sH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
-        if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
-        if (exact) return;
+        if (exact) {
+          if (tid == 0) flags[1 + atomicAdd(flags, 1)] = x.cid * H + x.head;
+          return;
+        }
         gate_qk<T>(sQ, sK, sQ, sK, G, me, scale);
         operands_ready();
         if (tid == 0) mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);  // A = Q^ K^^T
@@ -582,6 +598,8 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
   const Epi ep;
   const Own me;
   const CUtensorMap* m16[4] = {&mq, &mk, &mv, &mdo};
+  if (tid == 0)
+    for (const CUtensorMap* m : {&mq, &mk, &mv, &mdo, &mg, &mh, &mdh}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
   persistent_loop(
       MC, H, chunk_tab, full,
@@ -596,7 +614,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         unsigned char* b = smem + st * STAGE;
         zero_tail<Tg>(b, 4, b + 4 * TILE + 2 * STATE, x.len);
       },
-      [&](const Item& x, int st) {
+      [&](const Item& x, int st, auto& next) {
         unsigned char* rQ = smem + st * STAGE;
         unsigned char* rK = rQ + TILE;
         unsigned char* sV = rK + TILE;
@@ -608,8 +626,10 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         state_regs(sDH, me, dhreg);
         gate_prep<Tg, false>(G, sDH + STATE);  // its barriers order the state reads before sH/sDH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
-        if (tid == 0) flags[(int64_t)x.cid * H + x.head] = exact ? 1 : 0;
-        if (exact) return;
+        if (exact) {
+          if (tid == 0) flags[1 + atomicAdd(flags, 1)] = x.cid * H + x.head;
+          return;
+        }
         gate_qk<T>(rQ, rK, sQg, sKg, G, me, scale);
         operands_ready();
         if (tid == 0) {
@@ -673,6 +693,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
           mma64(tb + 64, sdA, 1, sQg, 1, idesc_f16(64, 64, F, 1, 1), true);   //     + dA^T Q^
           commit(&mbar[0]);
         }
+        next();
         // dgL per key index: exp(gL) h.dh + dh'.(K^^T v)
         if (tid < D) {
           float sp = 0.f, hdh = 0.f;

@@ -100,6 +100,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* mbar, uint32_t b
                : "memory");
 }
 
+// Fetch a tensor-map descriptor (kernel parameter) ahead of its first TMA use.
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 // TMA tiled load of a 3-D box (no multicast) into shared memory, completing on `mbar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* mbar) {
   asm volatile(
