@@ -154,6 +154,19 @@ int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_
                         int64_t C, void* out, void* workspace, size_t workspace_bytes,
                         ssla_stream_t stream);
 
+/* ---------------------------------------------------------------- MoS layer (inference)
+ * Fused per-patch work of MosAttention.forward (layers/mos_attention.py:97-136) for fp32:
+ * for every patch sequence (cu_seqlens, events in time order) and patch event t,
+ *   [q | v | g] = y[key[t], 0:3C];  h = sigmoid(g) * h + v;  z[dst[t], :] = q * h
+ * y rows hold 3C floats (the q/v/g projections of the scattered event); C % 4 == 0. */
+int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const int64_t* dst,
+                            const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
+                            ssla_stream_t stream);
+/* out = LayerNorm(x + r) * w + b over rows of C channels (r may be NULL); 1 <= C <= 1024.  Replaces the residual add + nn.LayerNorm closing MosAttention
+ * and LinearAttention (layers/mos_attention.py:144, layers/linear_attention.py:100). */
+int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, const float* b,
+                                int64_t rows, int64_t C, float eps, float* out, ssla_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops import mos as _mos
 from ..ops.common.scan import scan
 from ..ops.segment import gather_rows_ad, index_add_rows_ad
 from ..utils.async_utils import get_patch2pixel_lut
@@ -91,6 +92,8 @@ class MosAttention(nn.Module):
         src, pos_id = r["src"], r["pos_id"]
         E = residual.shape[0]
         C = self.hidden_size
+        if not torch.is_grad_enabled() and residual.dtype == torch.float32 and C % 4 == 0:
+            return self._forward_fused(inputs, residual, r)
         # scatter projection: all positions at once on the pixel events, then the routing gather
         ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
         P = ws.shape[0]
@@ -117,6 +120,40 @@ class MosAttention(nn.Module):
         if self.input_proj is not None:
             residual = self.input_proj(residual)
         out = self.norm(out + residual)
+        return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
+                "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}
+
+    def _forward_fused(self, inputs, residual, r):
+        """Inference path.  The q/v/g projections are folded into the per-position scatter
+        weights ([Wq; Wv; Wg] Ws_p) and o_proj into the gather weights (Wg_p Wo), so the only
+        per-patch-event work is the fused gather + gate + scan + q*h kernel; one GEMM over the
+        pixel events feeds it and one GEMM over the [E, P*C] buffer closes it."""
+        src, pos_id = r["src"], r["pos_id"]
+        E, C = residual.shape[0], self.hidden_size
+        ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
+        P = ws.shape[0]
+        wqvg = torch.cat([self.q_proj.weight, self.v_proj.weight, self.g_proj.weight], 0)  # [3C, C]
+        w_all = torch.matmul(wqvg, ws)  # [P, 3C, I]
+        y = residual @ w_all.reshape(P * 3 * C, self.input_size).t()  # [E, P*3C] = rows (e, p) of 3C
+        key = src if P == 1 else src * P + pos_id
+        lengths = r["lengths"]
+        cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
+        cu[1:] = lengths.cumsum(0)
+        wg = self.gather_conv_weights.reshape(-1, C, C)
+        Pg = wg.shape[0]
+        wgo = torch.matmul(wg, self.o_proj.weight)  # [Pg, C, C]
+        if Pg == 1:
+            qh = torch.empty((src.numel(), C), device=residual.device, dtype=torch.float32)
+            dst = torch.arange(src.numel(), device=residual.device)
+            _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
+            out = index_add_rows_ad(qh, src, E) @ wgo[0].t()
+        else:
+            z = torch.zeros((E * Pg, C), device=residual.device, dtype=torch.float32)
+            _mos.patch_scan(y.view(-1, 3 * C), key, src * Pg + pos_id, cu, C, z)  # unique (event, position)
+            out = z.view(E, Pg * C) @ wgo.permute(0, 2, 1).reshape(Pg * C, C)
+        if self.input_proj is not None:
+            residual = self.input_proj(residual)
+        out = _mos.layernorm_residual(out, residual, self.norm.weight, self.norm.bias, self.norm.eps)
         return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
                 "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}
 

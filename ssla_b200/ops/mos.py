@@ -1,0 +1,50 @@
+"""Fused inference ops of the MoS attention layer on the ssla_b200 C ABI (fp32).
+
+``patch_scan`` runs the per-patch part of ``MosAttention.forward``
+(layers/mos_attention.py:97-136): gather of the projected event row, sigmoid gate, the gated
+scan (ops/common/scan.py:35-43 order) and ``q * h``, written straight into the rows of the
+gather-projection buffer.  ``layernorm_residual`` is ``nn.LayerNorm(x + r)`` for narrow rows.
+Both are forward-only; the layers use them when no gradient is needed.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import _lib
+
+
+def patch_scan(y: torch.Tensor, key: torch.Tensor, dst: torch.Tensor, cu_seqlens: torch.Tensor,
+               C: int, z: torch.Tensor) -> torch.Tensor:
+    """For each patch sequence and event t: [q|v|g] = y[key[t]]; h = sigmoid(g) h + v;
+    z[dst[t]] = q * h.  ``y``: [rows, 3C] fp32, ``z``: [*, C] fp32 (written in place)."""
+    _lib.require_cuda(y, key, dst, cu_seqlens, z, what="patch_scan")
+    if y.dtype != torch.float32 or z.dtype != torch.float32:
+        raise TypeError("patch_scan: fp32 tensors expected")
+    if y.shape[-1] != 3 * C or z.shape[-1] != C:
+        raise ValueError("patch_scan: y must have 3C columns and z C columns")
+    y, z = y.contiguous(), z
+    if not z.is_contiguous():
+        raise ValueError("patch_scan: z must be contiguous")
+    key = key.to(torch.int64).contiguous()
+    dst = dst.to(torch.int64).contiguous()
+    cu = cu_seqlens.to(torch.int64).contiguous()
+    _lib.check(_lib.load().ssla_mos_patch_scan_fwd(y.data_ptr(), key.data_ptr(), dst.data_ptr(), cu.data_ptr(),
+                                                   cu.numel() - 1, C, z.data_ptr(), _lib.stream_of(y)),
+               "patch_scan")
+    return z
+
+
+def layernorm_residual(x: torch.Tensor, r: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
+                       eps: float) -> torch.Tensor:
+    """LayerNorm(x + r) * weight + bias over the last dimension (fp32, forward only)."""
+    _lib.require_cuda(x, weight, bias, what="layernorm_residual")
+    C = x.shape[-1]
+    x = x.contiguous()
+    r = None if r is None else r.contiguous()
+    out = torch.empty_like(x)
+    _lib.check(_lib.load().ssla_layernorm_residual_fwd(
+        x.data_ptr(), 0 if r is None else r.data_ptr(), weight.contiguous().data_ptr(), bias.contiguous().data_ptr(),
+        x.numel() // max(C, 1), C, float(eps), out.data_ptr(), _lib.stream_of(x)), "layernorm_residual")
+    return out

@@ -125,3 +125,41 @@ def test_layers_backward_runs():
     out.square().mean().backward()
     g = m.backbone[1].scatter_conv_weights.grad
     assert g is not None and torch.isfinite(g).all() and g.abs().sum() > 0
+
+
+@pytest.mark.parametrize("C", [1, 7, 12, 32, 48, 96, 256])
+def test_layernorm_residual_matches_torch(C):
+    from ssla_b200.ops.mos import layernorm_residual
+
+    gen = torch.Generator().manual_seed(C)
+    x = torch.randn(5000, C, generator=gen).cuda()
+    r = torch.randn(5000, C, generator=gen).cuda()
+    w = torch.randn(C, generator=gen).cuda()
+    b = torch.randn(C, generator=gen).cuda()
+    ref = torch.nn.functional.layer_norm(x + r, (C,), w, b, 1e-5)
+    assert rel_err(layernorm_residual(x, r, w, b, 1e-5), ref) < FP32_TOL
+    assert rel_err(layernorm_residual(x, None, w, b, 1e-5),
+                   torch.nn.functional.layer_norm(x, (C,), w, b, 1e-5)) < FP32_TOL
+
+
+@pytest.mark.parametrize("k,I,C,scatter,gather", [(3, 12, 12, True, True), (3, 12, 24, True, True),
+                                                   (1, 2, 12, True, True), (3, 24, 24, False, False)])
+def test_mos_attention_fused_inference_matches_autograd_path(k, I, C, scatter, gather):
+    """The no-grad path (q/v/g folded into the scatter weights, o into the gather weights, one
+    fused gather + gate + scan kernel, fused residual LayerNorm) against the autograd path of
+    the same layer on the same inputs."""
+    from ssla_b200.layers import MosAttention
+    from ssla_b200.model import preprocess_inputs
+    from ssla_b200.synthetic import seeded_parameters
+
+    ev, ln = _events(1)
+    x = preprocess_inputs(ev, ln, (240, 304))
+    x["events"] = torch.randn(x["events"].shape[0], I, generator=torch.Generator().manual_seed(1)).cuda()
+    layer = MosAttention(I, C, (240, 304), [k, k], scatter_proj=scatter, gather_proj=gather)
+    seeded_parameters(layer, 11)
+    layer = layer.cuda()
+    with torch.enable_grad():
+        ref = layer(dict(x))["events"]
+    with torch.no_grad():
+        fused = layer(dict(x))["events"]
+    assert rel_err(fused, ref.detach()) < FP32_TOL
