@@ -162,6 +162,15 @@ int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_
 int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const int64_t* dst,
                             const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
                             ssla_stream_t stream);
+/* The same with the projection done in the kernel: [q | v | g] = w[pos[t]] @ x[src[t]], with
+ * w [P, 3C, I] fp32 (the q/v/g projections folded into the per-position scatter weights) and
+ * x [*, I] the layer input rows.  w must fit in shared memory
+ * (ssla_mos_patch_scan_proj_smem_bytes(P, C, I) <= 200 KiB). */
+size_t ssla_mos_patch_scan_proj_smem_bytes(int64_t P, int64_t C, int64_t I);
+int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const float* w, int64_t P,
+                                 const int64_t* src, const int64_t* pos, const int64_t* dst,
+                                 const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
+                                 ssla_stream_t stream);
 /* out = LayerNorm(x + r) * w + b over rows of C channels (r may be NULL); 1 <= C <= 1024.  Replaces the residual add + nn.LayerNorm closing MosAttention
  * and LinearAttention (layers/mos_attention.py:144, layers/linear_attention.py:100). */
 int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, const float* b,

@@ -48,6 +48,8 @@ SIGNATURES = {
     "ssla_index_add_rows_workspace_bytes": (sz, [i64, i64]),
     "ssla_index_add_rows": (i32, [p, i32, p, i64, i64, i64, p, p, sz, p]),
     "ssla_mos_patch_scan_fwd": (i32, [p, p, p, p, i64, i64, p, p]),
+    "ssla_mos_patch_scan_proj_smem_bytes": (sz, [i64, i64, i64]),
+    "ssla_mos_patch_scan_proj_fwd": (i32, [p, i64, p, i64, p, p, p, p, i64, i64, p, p]),
     "ssla_layernorm_residual_fwd": (i32, [p, p, p, p, i64, i64, f32, p, p]),
 }
 

@@ -10,6 +10,13 @@
 // so the q/v/g tensors, the scan output and q*h never go through HBM.  One thread owns 4
 // adjacent channels of one sequence.
 //
+// mos_patch_scan_proj: the same, with the projection computed in the kernel instead of read
+// from y: [q | v | g_pre] = W[pos[t]] x[src[t]] with W [P, 3C, I] staged in shared memory as
+// [P, 3, I, C] (float4 reads of 4 consecutive channels) and x the layer's input rows (I
+// floats, read by all threads of a sequence at once).  One thread owns 4 channels of one
+// sequence (each x element feeds 12 FMAs); events are taken U at a time so their loads and
+// projections overlap, only the scan itself is serial.  Used when W fits in shared memory (the narrow, high-volume layers).
+//
 // layernorm_residual: out = LayerNorm(x + r) * w + b over rows of C channels (two-pass mean /
 // variance in fp32).  Rows of up to 32 channels take one thread each, wider rows one warp.
 #include "common.cuh"
@@ -45,6 +52,74 @@ __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __rest
       o[i] = __fmul_rn(qa[i], h[i]);
     }
     *reinterpret_cast<float4*>(z + dst[t] * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+constexpr int PS_U = 4;
+
+__global__ void __launch_bounds__(256) mos_patch_scan_proj_kernel(
+    const float* __restrict__ x, int I, const float* __restrict__ w, int P, const int64_t* __restrict__ src,
+    const int64_t* __restrict__ pos, const int64_t* __restrict__ dst, const int64_t* __restrict__ cu, int64_t n_seqs,
+    int C, float* __restrict__ z) {
+  extern __shared__ float ws[];  // [P][3][I][C]
+  const int n_w = P * 3 * I * C;
+  for (int e = threadIdx.x; e < n_w; e += blockDim.x) {
+    // e enumerates the global layout [P][3C][I]: p, row (= part * C + c), i
+    const int i = e % I, pr = e / I, row = pr % (3 * C), p = pr / (3 * C);
+    const int part = row / C, c = row % C;
+    ws[((p * 3 + part) * I + i) * C + c] = w[e];
+  }
+  __syncthreads();
+  // persistent: the grid covers the GPU once and strides over (sequence, 4-channel group)
+  // pairs, so the weights are staged once per block
+  const int CV = C >> 2;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n_seqs * CV;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t seq = idx / CV;
+    const int c = (int)(idx - seq * CV) << 2;
+    const int64_t bos = cu[seq], eos = cu[seq + 1];
+    float h[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t t0 = bos; t0 < eos; t0 += PS_U) {
+      const int n = (int)((eos - t0) < PS_U ? (eos - t0) : PS_U);
+      float4 q[PS_U], v[PS_U], g[PS_U];
+      int64_t d[PS_U];
+#pragma unroll
+      for (int u = 0; u < PS_U; ++u) {
+        q[u] = v[u] = g[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        d[u] = 0;
+        if (u < n) {
+          const float* xr = x + src[t0 + u] * I;
+          const float* wp = ws + (int)pos[t0 + u] * 3 * I * C + c;
+          d[u] = dst[t0 + u];
+          for (int i = 0; i < I; ++i) {
+            const float xi = xr[i];
+            const float4 wq = *reinterpret_cast<const float4*>(wp + i * C);
+            const float4 wv = *reinterpret_cast<const float4*>(wp + (I + i) * C);
+            const float4 wg = *reinterpret_cast<const float4*>(wp + (2 * I + i) * C);
+            q[u].x = fmaf(wq.x, xi, q[u].x); q[u].y = fmaf(wq.y, xi, q[u].y);
+            q[u].z = fmaf(wq.z, xi, q[u].z); q[u].w = fmaf(wq.w, xi, q[u].w);
+            v[u].x = fmaf(wv.x, xi, v[u].x); v[u].y = fmaf(wv.y, xi, v[u].y);
+            v[u].z = fmaf(wv.z, xi, v[u].z); v[u].w = fmaf(wv.w, xi, v[u].w);
+            g[u].x = fmaf(wg.x, xi, g[u].x); g[u].y = fmaf(wg.y, xi, g[u].y);
+            g[u].z = fmaf(wg.z, xi, g[u].z); g[u].w = fmaf(wg.w, xi, g[u].w);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PS_U; ++u) {
+        if (u < n) {
+          const float qa[4] = {q[u].x, q[u].y, q[u].z, q[u].w}, va[4] = {v[u].x, v[u].y, v[u].z, v[u].w},
+                      ga[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+          float o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            h[k] = __fadd_rn(__fmul_rn(h[k], sigmoid_f(ga[k])), va[k]);
+            o[k] = __fmul_rn(qa[k], h[k]);
+          }
+          *reinterpret_cast<float4*>(z + d[u] * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
   }
 }
 
@@ -119,6 +194,41 @@ extern "C" int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const
   mos_patch_scan_kernel<<<(unsigned)ceil_div(threads, 256), 256, 0, (cudaStream_t)stream>>>(y, key, dst, cu, n_seqs, C,
                                                                                            z);
   SSLA_CHECK_LAUNCH("ssla_mos_patch_scan_fwd");
+  return SSLA_OK;
+}
+
+extern "C" size_t ssla_mos_patch_scan_proj_smem_bytes(int64_t P, int64_t C, int64_t I) {
+  return (size_t)(P * 3 * C * I) * sizeof(float);
+}
+
+extern "C" int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const float* w, int64_t P, const int64_t* src,
+                                            const int64_t* pos, const int64_t* dst, const int64_t* cu, int64_t n_seqs,
+                                            int64_t C, float* z, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(n_seqs >= 0 && C > 0 && C % 4 == 0 && I > 0 && P > 0,
+                 "ssla_mos_patch_scan_proj_fwd: bad sizes (C must be a multiple of 4)");
+  const size_t smem = ssla_mos_patch_scan_proj_smem_bytes(P, C, I);
+  SSLA_CHECK_ARG(smem <= 200 * 1024, "ssla_mos_patch_scan_proj_fwd: weights of %zu bytes exceed shared memory", smem);
+  if (n_seqs == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(x && w && src && pos && dst && cu && z, "ssla_mos_patch_scan_proj_fwd: null pointer");
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(mos_patch_scan_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess) {
+    set_error("ssla_mos_patch_scan_proj_fwd: cannot reserve %zu bytes of shared memory", smem);
+    return SSLA_ERR_CUDA;
+  }
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mos_patch_scan_proj_kernel, 256, smem) != cudaSuccess ||
+      per_sm < 1) {
+    set_error("ssla_mos_patch_scan_proj_fwd: occupancy query failed");
+    return SSLA_ERR_CUDA;
+  }
+  const int64_t blocks = ceil_div(n_seqs * (C / 4), 256);
+  const int64_t cap = (int64_t)per_sm * sms;
+  mos_patch_scan_proj_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, smem, (cudaStream_t)stream>>>(
+      x, (int)I, w, (int)P, src, pos, dst, cu, n_seqs, (int)C, z);
+  SSLA_CHECK_LAUNCH("ssla_mos_patch_scan_proj_fwd");
   return SSLA_OK;
 }
 

@@ -126,31 +126,40 @@ class MosAttention(nn.Module):
     def _forward_fused(self, inputs, residual, r):
         """Inference path.  The q/v/g projections are folded into the per-position scatter
         weights ([Wq; Wv; Wg] Ws_p) and o_proj into the gather weights (Wg_p Wo), so the only
-        per-patch-event work is the fused gather + gate + scan + q*h kernel; one GEMM over the
-        pixel events feeds it and one GEMM over the [E, P*C] buffer closes it."""
+        per-patch-event work is one fused kernel: projection of the event's input row by its
+        position's folded weights (in shared memory; for wide layers a GEMM over the pixel
+        events precomputes them instead), sigmoid gate, scan and q*h written into the
+        [E, P*C] buffer; one GEMM over that buffer closes the layer."""
         src, pos_id = r["src"], r["pos_id"]
         E, C = residual.shape[0], self.hidden_size
         ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
         P = ws.shape[0]
         wqvg = torch.cat([self.q_proj.weight, self.v_proj.weight, self.g_proj.weight], 0)  # [3C, C]
         w_all = torch.matmul(wqvg, ws)  # [P, 3C, I]
-        y = residual @ w_all.reshape(P * 3 * C, self.input_size).t()  # [E, P*3C] = rows (e, p) of 3C
-        key = src if P == 1 else src * P + pos_id
         lengths = r["lengths"]
         cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
         cu[1:] = lengths.cumsum(0)
         wg = self.gather_conv_weights.reshape(-1, C, C)
         Pg = wg.shape[0]
         wgo = torch.matmul(wg, self.o_proj.weight)  # [Pg, C, C]
+        rows = src.numel()
         if Pg == 1:
-            qh = torch.empty((src.numel(), C), device=residual.device, dtype=torch.float32)
-            dst = torch.arange(src.numel(), device=residual.device)
+            qh = torch.empty((rows, C), device=residual.device, dtype=torch.float32)
+            dst = torch.arange(rows, device=residual.device)
+        else:
+            qh = torch.zeros((E * Pg, C), device=residual.device, dtype=torch.float32)
+            dst = src * Pg + pos_id  # unique (event, position) pairs
+        if _mos.patch_scan_proj_fits(P, C, self.input_size):
+            # projection inside the scan kernel (weights in shared memory)
+            _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
+        else:
+            y = residual @ w_all.reshape(P * 3 * C, self.input_size).t()  # [E, P*3C] = rows (e, p) of 3C
+            key = src if P == 1 else src * P + pos_id
             _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
+        if Pg == 1:
             out = index_add_rows_ad(qh, src, E) @ wgo[0].t()
         else:
-            z = torch.zeros((E * Pg, C), device=residual.device, dtype=torch.float32)
-            _mos.patch_scan(y.view(-1, 3 * C), key, src * Pg + pos_id, cu, C, z)  # unique (event, position)
-            out = z.view(E, Pg * C) @ wgo.permute(0, 2, 1).reshape(Pg * C, C)
+            out = qh.view(E, Pg * C) @ wgo.permute(0, 2, 1).reshape(Pg * C, C)
         if self.input_proj is not None:
             residual = self.input_proj(residual)
         out = _mos.layernorm_residual(out, residual, self.norm.weight, self.norm.bias, self.norm.eps)

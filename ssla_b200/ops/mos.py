@@ -36,6 +36,33 @@ def patch_scan(y: torch.Tensor, key: torch.Tensor, dst: torch.Tensor, cu_seqlens
     return z
 
 
+PROJ_SMEM_LIMIT = 112 * 1024  # above this the projection is a separate GEMM
+
+
+def patch_scan_proj_fits(P: int, C: int, I: int) -> bool:
+    return _lib.load().ssla_mos_patch_scan_proj_smem_bytes(P, C, I) <= PROJ_SMEM_LIMIT
+
+
+def patch_scan_proj(x: torch.Tensor, w: torch.Tensor, src: torch.Tensor, pos: torch.Tensor, dst: torch.Tensor,
+                    cu_seqlens: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """``patch_scan`` with the projection in the kernel: [q|v|g] = w[pos[t]] @ x[src[t]];
+    ``x``: [E, I], ``w``: [P, 3C, I], ``z``: [*, C] (written in place)."""
+    _lib.require_cuda(x, w, src, pos, dst, cu_seqlens, z, what="patch_scan_proj")
+    if x.dtype != torch.float32 or w.dtype != torch.float32 or z.dtype != torch.float32:
+        raise TypeError("patch_scan_proj: fp32 tensors expected")
+    P, C3, I = w.shape
+    C = C3 // 3
+    if x.shape[-1] != I or z.shape[-1] != C or not z.is_contiguous():
+        raise ValueError("patch_scan_proj: shape mismatch")
+    x, w = x.contiguous(), w.contiguous()
+    src, pos, dst = (t.to(torch.int64).contiguous() for t in (src, pos, dst))
+    cu = cu_seqlens.to(torch.int64).contiguous()
+    _lib.check(_lib.load().ssla_mos_patch_scan_proj_fwd(
+        x.data_ptr(), I, w.data_ptr(), P, src.data_ptr(), pos.data_ptr(), dst.data_ptr(), cu.data_ptr(),
+        cu.numel() - 1, C, z.data_ptr(), _lib.stream_of(x)), "patch_scan_proj")
+    return z
+
+
 def layernorm_residual(x: torch.Tensor, r: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
                        eps: float) -> torch.Tensor:
     """LayerNorm(x + r) * weight + bias over the last dimension (fp32, forward only)."""
