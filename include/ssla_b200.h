@@ -176,6 +176,32 @@ int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const float* w, int6
 int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, const float* b,
                                 int64_t rows, int64_t C, float eps, float* out, ssla_stream_t stream);
 
+/* ---------------------------------------------------------------- event routing
+ * Pixel groups -> receptive fields with each field's events in time order: the GPU form of
+ * scatter_group_events_to_patch / gather_receptive_fields (utils/async_utils.py:125-240,
+ * utils/farsecnn_utils.py:177-265).  Geometry: frame H x W, window kh x kw, stride sh x sw,
+ * leading padding pt / pl, output oh x ow fields per sample, B samples.
+ *   ssla_route_pixel_map:  map[(b*H + y)*W + x] = group id (map pre-filled with -1); groups
+ *                          outside the frame are skipped and counted in *bad.
+ *   ssla_route_groups_time_sorted: *bad = 1 if some group's times decrease.
+ *   ssla_route_field_lengths: flen[b*oh*ow + f] = events in field f of sample b.
+ *   ssla_route_fill: for the non-empty fields field_ids[F] (ascending) with output offsets
+ *                    field_off[F+1]: src (event index), pos (window position) and time of every
+ *                    routed event, ordered by (time, pos, event) within each field.
+ * kh * kw <= 32. */
+int ssla_route_pixel_map(const int64_t* batch_id, const int64_t* h, const int64_t* w, int64_t G,
+                         int64_t B, int64_t H, int64_t W, int* map, int* bad, ssla_stream_t stream);
+int ssla_route_groups_time_sorted(const int64_t* gstart, const int64_t* glen, const int64_t* gtime,
+                                  int64_t G, int* bad, ssla_stream_t stream);
+int ssla_route_field_lengths(const int* map, const int64_t* glen, int64_t B, int64_t H, int64_t W,
+                             int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                             int64_t oh, int64_t ow, int64_t* flen, ssla_stream_t stream);
+int ssla_route_fill(const int* map, const int64_t* gstart, const int64_t* glen, const int64_t* gtime,
+                    int64_t B, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                    int64_t pt, int64_t pl, int64_t oh, int64_t ow, const int64_t* field_ids,
+                    const int64_t* field_off, int64_t F, int64_t* src, int64_t* pos, int64_t* time,
+                    ssla_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,180 @@
+// Event routing of the sparse layers on the GPU: pixel groups -> receptive fields (MoS patches,
+// pooling windows) with each field's events in time order (utils/async_utils.py:125-240,
+// utils/farsecnn_utils.py:177-265).
+//
+// The reference builds dense [batch * fields, kh*kw] masks, replicates events with
+// repeat_interleave and orders every field's events with a sort.  Here:
+//   1. pixel_map: a dense [B, H, W] int32 map of the active pixel groups (-1 elsewhere);
+//   2. field_lengths: one thread per field adds the lengths of the groups in its window
+//      (window pixel (dy, dx) of field (oy, ox) = (oy*sh - pt + dy, ox*sw - pl + dx));
+//   3. (host) the non-empty fields in ascending id order and their output offsets;
+//   4. fill: one thread per non-empty field merges the time-ordered event lists of its window's
+//      groups, smallest (time, window position, event order) first -- the order a stable sort
+//      by time of the (position, event)-ordered rows gives.
+// A group's events must be in non-decreasing time order (time-ordered event streams keep it
+// through every layer); groups_time_sorted checks it so the caller can fall back otherwise.
+#include "common.cuh"
+
+namespace ssla {
+namespace {
+
+constexpr int kMaxArea = 32;
+
+struct Geo {
+  int B, H, W, kh, kw, sh, sw, pt, pl, oh, ow;
+};
+
+// Groups with coordinates outside [B, H, W] are skipped and counted in *bad.
+__global__ void pixel_map_kernel(const int64_t* __restrict__ bid, const int64_t* __restrict__ h,
+                                 const int64_t* __restrict__ w, int64_t G, int B, int H, int W, int* __restrict__ map,
+                                 int* __restrict__ bad) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= G) return;
+  const int64_t b = bid[g], y = h[g], x = w[g];
+  if (b < 0 || b >= B || y < 0 || y >= H || x < 0 || x >= W) {
+    atomicAdd(bad, 1);
+    return;
+  }
+  map[(b * H + y) * W + x] = (int)g;
+}
+
+__global__ void time_sorted_kernel(const int64_t* __restrict__ start, const int64_t* __restrict__ len,
+                                   const int64_t* __restrict__ t, int64_t G, int* __restrict__ bad) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= G) return;
+  const int64_t s = start[g], e = s + len[g];
+  for (int64_t i = s + 1; i < e; ++i)
+    if (t[i] < t[i - 1]) {
+      atomicExch(bad, 1);
+      return;
+    }
+}
+
+// Window pixel p of field (b, oy, ox) -> group id (-1 if outside the frame or inactive).
+__device__ __forceinline__ int window_group(const int* __restrict__ map, const Geo& g, int b, int oy, int ox, int p) {
+  const int y = oy * g.sh - g.pt + p / g.kw;
+  const int x = ox * g.sw - g.pl + p % g.kw;
+  if (y < 0 || y >= g.H || x < 0 || x >= g.W) return -1;
+  return map[((int64_t)b * g.H + y) * g.W + x];
+}
+
+__global__ void field_lengths_kernel(const int* __restrict__ map, const int64_t* __restrict__ glen, Geo geo,
+                                     int64_t* __restrict__ flen) {
+  const int64_t nf = (int64_t)geo.oh * geo.ow;
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= geo.B * nf) return;
+  const int b = (int)(f / nf);
+  const int r = (int)(f - b * nf);
+  const int oy = r / geo.ow, ox = r - oy * geo.ow;
+  int64_t n = 0;
+  for (int p = 0; p < geo.kh * geo.kw; ++p) {
+    const int gi = window_group(map, geo, b, oy, ox, p);
+    if (gi >= 0) n += glen[gi];
+  }
+  flen[f] = n;
+}
+
+__global__ void fill_kernel(const int* __restrict__ map, const int64_t* __restrict__ gstart,
+                            const int64_t* __restrict__ glen, const int64_t* __restrict__ gtime, Geo geo,
+                            const int64_t* __restrict__ field_ids, const int64_t* __restrict__ field_off, int64_t F,
+                            int64_t* __restrict__ src, int64_t* __restrict__ pos, int64_t* __restrict__ time) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= F) return;
+  const int64_t nf = (int64_t)geo.oh * geo.ow;
+  const int64_t f = field_ids[i];
+  const int b = (int)(f / nf);
+  const int r = (int)(f - b * nf);
+  const int oy = r / geo.ow, ox = r - oy * geo.ow;
+  // the window's non-empty lists, in position order
+  int64_t cur[kMaxArea], end[kMaxArea], head[kMaxArea];
+  int lp[kMaxArea];
+  int n = 0;
+  for (int p = 0; p < geo.kh * geo.kw; ++p) {
+    const int gi = window_group(map, geo, b, oy, ox, p);
+    if (gi >= 0 && glen[gi] > 0) {
+      cur[n] = gstart[gi];
+      end[n] = gstart[gi] + glen[gi];
+      head[n] = gtime[cur[n]];
+      lp[n] = p;
+      ++n;
+    }
+  }
+  int64_t o = field_off[i];
+  const int64_t oe = field_off[i + 1];
+  for (; o < oe; ++o) {
+    // smallest head time; ties -> lowest position (lists are in position order)
+    int best = -1;
+    int64_t bt = 0;
+    for (int j = 0; j < n; ++j)
+      if (cur[j] < end[j] && (best < 0 || head[j] < bt)) {
+        best = j;
+        bt = head[j];
+      }
+    if (best < 0) break;  // offsets inconsistent with the lists (not produced by field_lengths)
+    src[o] = cur[best];
+    pos[o] = lp[best];
+    time[o] = bt;
+    if (++cur[best] < end[best]) head[best] = gtime[cur[best]];
+  }
+}
+
+int check_geo(const Geo& g) {
+  SSLA_CHECK_ARG(g.B >= 0 && g.H > 0 && g.W > 0 && g.kh > 0 && g.kw > 0 && g.sh > 0 && g.sw > 0 && g.oh >= 0 &&
+                     g.ow >= 0,
+                 "ssla_route: bad geometry");
+  SSLA_CHECK_ARG(g.kh * g.kw <= kMaxArea, "ssla_route: window of %d pixels exceeds %d", g.kh * g.kw, kMaxArea);
+  return SSLA_OK;
+}
+
+}  // namespace
+}  // namespace ssla
+
+using namespace ssla;
+
+extern "C" int ssla_route_pixel_map(const int64_t* batch_id, const int64_t* h, const int64_t* w, int64_t G, int64_t B,
+                                    int64_t H, int64_t W, int* map, int* bad, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(G >= 0 && B >= 0 && H > 0 && W > 0, "ssla_route_pixel_map: bad sizes");
+  if (G == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(batch_id && h && w && map && bad, "ssla_route_pixel_map: null pointer");
+  pixel_map_kernel<<<(unsigned)ceil_div(G, 256), 256, 0, (cudaStream_t)stream>>>(batch_id, h, w, G, (int)B, (int)H,
+                                                                                  (int)W, map, bad);
+  SSLA_CHECK_LAUNCH("ssla_route_pixel_map");
+  return SSLA_OK;
+}
+
+extern "C" int ssla_route_groups_time_sorted(const int64_t* gstart, const int64_t* glen, const int64_t* gtime,
+                                             int64_t G, int* bad, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(G >= 0, "ssla_route_groups_time_sorted: bad sizes");
+  if (G == 0) return SSLA_OK;
+  time_sorted_kernel<<<(unsigned)ceil_div(G, 256), 256, 0, (cudaStream_t)stream>>>(gstart, glen, gtime, G, bad);
+  SSLA_CHECK_LAUNCH("ssla_route_groups_time_sorted");
+  return SSLA_OK;
+}
+
+extern "C" int ssla_route_field_lengths(const int* map, const int64_t* glen, int64_t B, int64_t H, int64_t W,
+                                        int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                                        int64_t oh, int64_t ow, int64_t* flen, ssla_stream_t stream) {
+  const Geo geo{(int)B, (int)H, (int)W, (int)kh, (int)kw, (int)sh, (int)sw, (int)pt, (int)pl, (int)oh, (int)ow};
+  int rc = check_geo(geo);
+  if (rc) return rc;
+  const int64_t n = B * oh * ow;
+  if (n == 0) return SSLA_OK;
+  field_lengths_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(map, glen, geo, flen);
+  SSLA_CHECK_LAUNCH("ssla_route_field_lengths");
+  return SSLA_OK;
+}
+
+extern "C" int ssla_route_fill(const int* map, const int64_t* gstart, const int64_t* glen, const int64_t* gtime,
+                               int64_t B, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                               int64_t pt, int64_t pl, int64_t oh, int64_t ow, const int64_t* field_ids,
+                               const int64_t* field_off, int64_t F, int64_t* src, int64_t* pos, int64_t* time,
+                               ssla_stream_t stream) {
+  const Geo geo{(int)B, (int)H, (int)W, (int)kh, (int)kw, (int)sh, (int)sw, (int)pt, (int)pl, (int)oh, (int)ow};
+  int rc = check_geo(geo);
+  if (rc) return rc;
+  if (F == 0) return SSLA_OK;
+  fill_kernel<<<(unsigned)ceil_div(F, 128), 128, 0, (cudaStream_t)stream>>>(map, gstart, glen, gtime, geo, field_ids,
+                                                                            field_off, F, src, pos, time);
+  SSLA_CHECK_LAUNCH("ssla_route_fill");
+  return SSLA_OK;
+}

@@ -88,7 +88,8 @@ class MosAttention(nn.Module):
         if residual.shape[0] != inputs["time"].shape[0]:
             raise ValueError("events and time must have one row per event")
         r = replicate_to_fields(inputs["batch_id"], inputs["h"], inputs["w"], inputs["lengths"], inputs["time"],
-                                self.frame_size, tuple(self.kernel_size), tuple(self.stride))
+                                self.frame_size, tuple(self.kernel_size), tuple(self.stride),
+                                batch_size=inputs.get("batch_size"))
         src, pos_id = r["src"], r["pos_id"]
         E = residual.shape[0]
         C = self.hidden_size

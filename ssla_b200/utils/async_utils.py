@@ -35,7 +35,8 @@ def scatter_group_events_to_patch(pixel_inputs: Dict[str, torch.Tensor], frame_s
         k = int(round(patch2pixel_lut.shape[1] ** 0.5))
         kernel_size = (k, k)
     r = replicate_to_fields(pixel_inputs["batch_id"], pixel_inputs["h"], pixel_inputs["w"],
-                            pixel_inputs["lengths"], pixel_inputs["time"], frame_size, kernel_size, stride)
+                            pixel_inputs["lengths"], pixel_inputs["time"], frame_size, kernel_size, stride,
+                            batch_size=pixel_inputs.get("batch_size"))
     return {
         "events": _seg.gather_rows_ad(pixel_inputs["events"], r["src"]),
         "pos_id": r["pos_id"],

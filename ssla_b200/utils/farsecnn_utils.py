@@ -34,7 +34,7 @@ def gather_receptive_fields(inputs, frame_size, rf2pixel_lut, rf_outcoord, kerne
         stride = kernel_size
     ow = int(rf_outcoord[:, 0].max()) + 1
     r = replicate_to_fields(inputs["batch_id"], inputs["h"], inputs["w"], inputs["lengths"], inputs["time"],
-                            frame_size, kernel_size, stride)
+                            frame_size, kernel_size, stride, batch_size=inputs.get("batch_size"))
     fid = r["field_id"]
     f = fid % n_rf
     return {

@@ -8,10 +8,11 @@ unstable ``torch.sort`` to order the events of a patch by time (utils/async_util
 utils/farsecnn_utils.py:246), ties are broken deterministically here by (look-up-table
 position, event order), i.e. the order the reference builds before sorting.
 
-Replication is done from the active pixel groups outwards: every group is expanded to the
-(patch, position) pairs whose receptive field contains it (at most kh*kw), those pairs are
-ordered by (patch, position), and events follow.  This touches O(groups * kh * kw) entries
-instead of the reference's dense [B * num_patches, kh * kw] masks.
+On CUDA tensors ``replicate_to_fields`` runs the routing kernels of ``csrc/routing.cu``: a
+dense pixel -> group map, per-field event counts, and a per-field merge of the time-ordered
+pixel lists (no sort).  The PyTorch formulation below it (pairs expanded from the active
+groups, ordered by (field, position), then a stable time sort) is kept for windows larger than
+32 pixels and for groups whose events are not in time order; both give the same output.
 """
 from __future__ import annotations
 
@@ -19,6 +20,8 @@ import math
 from typing import Dict, Tuple
 
 import torch
+
+from .. import _lib
 
 
 def compute_padding_1d(in_size: int, kernel_size: int, stride: int, mode: str = "same") -> int:
@@ -113,6 +116,44 @@ def truncate_packed_sequence(data: torch.Tensor, seqlens: torch.Tensor, threshol
     return data[keep], new_lengths
 
 
+def _replicate_gpu(gr_batch_id, gr_h, gr_w, gr_lengths, gr_time, geo, batch_size):
+    """The routing kernels; None when they do not apply (the caller falls back)."""
+    H, W, kh, kw, sh, sw, pt, pl, oh, ow = geo
+    if kh * kw > 32 or not gr_lengths.is_cuda:
+        return None
+    dev = gr_lengths.device
+    G = gr_lengths.numel()
+    i64 = lambda t: t.to(torch.int64).contiguous()
+    bid, hh, ww, glen, gtime = i64(gr_batch_id), i64(gr_h), i64(gr_w), i64(gr_lengths), i64(gr_time)
+    B = int(batch_size) if batch_size is not None else (int(bid.max()) + 1 if G else 0)
+    L, st = _lib.load(), _lib.stream_of(glen)
+    gstart = torch.cumsum(glen, 0) - glen
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)  # [0] groups outside the frame, [1] unsorted times
+    pmap = torch.full((max(B * H * W, 1),), -1, dtype=torch.int32, device=dev)
+    _lib.check(L.ssla_route_pixel_map(bid.data_ptr(), hh.data_ptr(), ww.data_ptr(), G, B, H, W, pmap.data_ptr(),
+                                      flags.data_ptr(), st), "route_pixel_map")
+    _lib.check(L.ssla_route_groups_time_sorted(gstart.data_ptr(), glen.data_ptr(), gtime.data_ptr(), G,
+                                               flags.data_ptr() + 4, st), "route_groups_time_sorted")
+    flen = torch.empty(max(B * oh * ow, 1), dtype=torch.int64, device=dev)
+    _lib.check(L.ssla_route_field_lengths(pmap.data_ptr(), glen.data_ptr(), B, H, W, kh, kw, sh, sw, pt, pl, oh, ow,
+                                          flen.data_ptr(), st), "route_field_lengths")
+    field_ids = torch.nonzero(flen[:B * oh * ow]).squeeze(1)
+    lengths = flen[field_ids]
+    off = torch.zeros(field_ids.numel() + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(lengths, 0, out=off[1:])
+    bad_coord, unsorted, n_ev = torch.cat([flags.to(torch.int64), off[-1:]]).tolist()
+    if bad_coord or unsorted:
+        return None
+    src = torch.empty(n_ev, dtype=torch.int64, device=dev)
+    pos = torch.empty(n_ev, dtype=torch.int64, device=dev)
+    t = torch.empty(n_ev, dtype=torch.int64, device=dev)
+    _lib.check(L.ssla_route_fill(pmap.data_ptr(), gstart.data_ptr(), glen.data_ptr(), gtime.data_ptr(), B, H, W, kh,
+                                 kw, sh, sw, pt, pl, oh, ow, field_ids.data_ptr(), off.data_ptr(), field_ids.numel(),
+                                 src.data_ptr(), pos.data_ptr(), t.data_ptr(), st), "route_fill")
+    return {"field_id": field_ids, "lengths": lengths.to(gr_lengths.dtype), "src": src, "pos_id": pos,
+            "time": t.to(gr_time.dtype)}
+
+
 def replicate_to_fields(
     gr_batch_id: torch.Tensor,
     gr_h: torch.Tensor,
@@ -122,6 +163,7 @@ def replicate_to_fields(
     frame_size,
     kernel_size,
     stride,
+    batch_size=None,
 ):
     """Replicate the events of pixel groups into every receptive field (patch) containing the
     pixel, and order each field's events by time.
@@ -132,8 +174,13 @@ def replicate_to_fields(
       src        [P]  index into the group-ordered event array of each replicated event
       pos_id     [P]  look-up-table position (0 .. kh*kw-1) the event was taken from
       time       [P]  its timestamp
-    with events sorted by (field, time, position, source order)."""
-    H, W, kh, kw, sh, sw, pt, pl, oh, ow = _geometry(frame_size, kernel_size, stride)
+    with events sorted by (field, time, position, source order).  ``batch_size`` (samples in
+    the batch) sizes the GPU pixel map; without it the largest batch id is read back."""
+    geo = _geometry(frame_size, kernel_size, stride)
+    r = _replicate_gpu(gr_batch_id, gr_h, gr_w, gr_lengths, gr_time, geo, batch_size)
+    if r is not None:
+        return r
+    H, W, kh, kw, sh, sw, pt, pl, oh, ow = geo
     dev = gr_lengths.device
     nf = oh * ow
     G = gr_lengths.numel()

@@ -163,3 +163,26 @@ def test_mos_attention_fused_inference_matches_autograd_path(k, I, C, scatter, g
     with torch.no_grad():
         fused = layer(dict(x))["events"]
     assert rel_err(fused, ref.detach()) < FP32_TOL
+
+
+@pytest.mark.parametrize("frame,k,stride", [((40, 52), 3, 1), ((40, 52), 2, 2), ((31, 17), 3, 1), ((30, 38), 4, 4),
+                                            ((12, 12), 5, 1)])
+def test_routing_kernels_match_torch_formulation(frame, k, stride):
+    """GPU routing (pixel map + per-field merge) against the PyTorch formulation run on the CPU:
+    identical fields, lengths, and (src, pos, time) order, with timestamp ties inside and across
+    pixels, frame borders, and an empty sample."""
+    from ssla_b200.utils.routing import replicate_to_fields
+
+    gen = torch.Generator().manual_seed(frame[0] * 100 + k)
+    B, (H, W) = 3, frame
+    pix = torch.randperm(B * H * W, generator=gen)[: B * H * W // 5]
+    pix = pix[pix // (H * W) != 1].sort().values  # sample 1 empty
+    G = pix.numel()
+    lengths = torch.randint(1, 6, (G,), generator=gen)
+    times = torch.cat([torch.randint(0, 8, (int(n),), generator=gen).sort().values for n in lengths])
+    bid, rem = pix // (H * W), pix % (H * W)
+    args = (bid, rem // W, rem % W, lengths, times, frame, (k, k), (stride, stride))
+    ref = replicate_to_fields(*args, batch_size=B)
+    got = replicate_to_fields(*(a.cuda() if torch.is_tensor(a) else a for a in args), batch_size=B)
+    for key in ("field_id", "lengths", "src", "pos_id", "time"):
+        assert torch.equal(got[key].cpu(), ref[key]), key
