@@ -57,17 +57,25 @@ __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __rest
 
 constexpr int PS_U = 4;
 
+// Shared-memory stride between positions: 3*I*C floats rounded up to 4 (mod 32), so the
+// float4 reads of threads on different positions start in different 16-byte bank groups.
+__host__ __device__ __forceinline__ int pstride(int I, int C) {
+  const int n = 3 * I * C;
+  return n + ((4 - n % 32) + 32) % 32;
+}
+
 __global__ void __launch_bounds__(256) mos_patch_scan_proj_kernel(
     const float* __restrict__ x, int I, const float* __restrict__ w, int P, const int64_t* __restrict__ src,
     const int64_t* __restrict__ pos, const int64_t* __restrict__ dst, const int64_t* __restrict__ cu, int64_t n_seqs,
     int C, float* __restrict__ z) {
-  extern __shared__ float ws[];  // [P][3][I][C]
+  extern __shared__ float ws[];  // [P][3][I][C], position stride pstride(I, C) floats
   const int n_w = P * 3 * I * C;
+  const int ps = pstride(I, C);
   for (int e = threadIdx.x; e < n_w; e += blockDim.x) {
     // e enumerates the global layout [P][3C][I]: p, row (= part * C + c), i
     const int i = e % I, pr = e / I, row = pr % (3 * C), p = pr / (3 * C);
     const int part = row / C, c = row % C;
-    ws[((p * 3 + part) * I + i) * C + c] = w[e];
+    ws[p * ps + (part * I + i) * C + c] = w[e];
   }
   __syncthreads();
   // persistent: the grid covers the GPU once and strides over (sequence, 4-channel group)
@@ -89,7 +97,7 @@ __global__ void __launch_bounds__(256) mos_patch_scan_proj_kernel(
         d[u] = 0;
         if (u < n) {
           const float* xr = x + src[t0 + u] * I;
-          const float* wp = ws + (int)pos[t0 + u] * 3 * I * C + c;
+          const float* wp = ws + (int)pos[t0 + u] * ps + c;
           d[u] = dst[t0 + u];
           for (int i = 0; i < I; ++i) {
             const float xi = xr[i];
@@ -198,7 +206,7 @@ extern "C" int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const
 }
 
 extern "C" size_t ssla_mos_patch_scan_proj_smem_bytes(int64_t P, int64_t C, int64_t I) {
-  return (size_t)(P * 3 * C * I) * sizeof(float);
+  return (size_t)(P * pstride((int)I, (int)C)) * sizeof(float);
 }
 
 extern "C" int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const float* w, int64_t P, const int64_t* src,

@@ -74,47 +74,82 @@ __global__ void field_lengths_kernel(const int* __restrict__ map, const int64_t*
   flen[f] = n;
 }
 
-__global__ void fill_kernel(const int* __restrict__ map, const int64_t* __restrict__ gstart,
-                            const int64_t* __restrict__ glen, const int64_t* __restrict__ gtime, Geo geo,
-                            const int64_t* __restrict__ field_ids, const int64_t* __restrict__ field_off, int64_t F,
-                            int64_t* __restrict__ src, int64_t* __restrict__ pos, int64_t* __restrict__ time) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= F) return;
-  const int64_t nf = (int64_t)geo.oh * geo.ow;
-  const int64_t f = field_ids[i];
-  const int b = (int)(f / nf);
-  const int r = (int)(f - b * nf);
-  const int oy = r / geo.ow, ox = r - oy * geo.ow;
-  // the window's non-empty lists, in position order
-  int64_t cur[kMaxArea], end[kMaxArea], head[kMaxArea];
-  int lp[kMaxArea];
-  int n = 0;
-  for (int p = 0; p < geo.kh * geo.kw; ++p) {
-    const int gi = window_group(map, geo, b, oy, ox, p);
-    if (gi >= 0 && glen[gi] > 0) {
-      cur[n] = gstart[gi];
-      end[n] = gstart[gi] + glen[gi];
-      head[n] = gtime[cur[n]];
-      lp[n] = p;
-      ++n;
+// Outputs of a block's fields form one contiguous range; up to kStage of them are staged in
+// shared memory and written out coalesced (the rest, for blocks with very long fields, go
+// straight to global memory).
+constexpr int kFillThreads = 128, kStage = 2048;
+
+// A >= window size: the per-list state lives in registers (every access is an unrolled loop
+// over compile-time indices).
+template <int A>
+__global__ void __launch_bounds__(kFillThreads) fill_kernel(
+    const int* __restrict__ map, const int64_t* __restrict__ gstart, const int64_t* __restrict__ glen,
+    const int64_t* __restrict__ gtime, Geo geo, const int64_t* __restrict__ field_ids,
+    const int64_t* __restrict__ field_off, int64_t F, int64_t* __restrict__ src, int64_t* __restrict__ pos,
+    int64_t* __restrict__ time) {
+  __shared__ int64_t s_src[kStage], s_time[kStage];
+  __shared__ unsigned char s_pos[kStage];
+  const int64_t f0 = (int64_t)blockIdx.x * kFillThreads;
+  const int64_t i = f0 + threadIdx.x;
+  const int64_t flast = (f0 + kFillThreads < F ? f0 + kFillThreads : F);
+  const int64_t base = field_off[f0], span = field_off[flast] - base;
+  if (i < F) {
+    const int64_t nf = (int64_t)geo.oh * geo.ow;
+    const int64_t f = field_ids[i];
+    const int b = (int)(f / nf);
+    const int r = (int)(f - b * nf);
+    const int oy = r / geo.ow, ox = r - oy * geo.ow;
+    // list j = window position j: events [cur, end) of the group there (empty if none)
+    int64_t cur[A], end[A], head[A];
+#pragma unroll
+    for (int j = 0; j < A; ++j) {
+      cur[j] = end[j] = head[j] = 0;
+      if (j < geo.kh * geo.kw) {
+        const int gi = window_group(map, geo, b, oy, ox, j);
+        if (gi >= 0) {
+          cur[j] = gstart[gi];
+          end[j] = cur[j] + glen[gi];
+          if (end[j] > cur[j]) head[j] = gtime[cur[j]];
+        }
+      }
+    }
+    const int64_t oe = field_off[i + 1];
+    for (int64_t o = field_off[i]; o < oe; ++o) {
+      // smallest head time; ties -> lowest position
+      int best = -1;
+      int64_t bt = 0;
+#pragma unroll
+      for (int j = 0; j < A; ++j)
+        if (cur[j] < end[j] && (best < 0 || head[j] < bt)) {
+          best = j;
+          bt = head[j];
+        }
+      if (best < 0) break;  // offsets inconsistent with the lists (not produced by field_lengths)
+      int64_t sidx = 0;
+#pragma unroll
+      for (int j = 0; j < A; ++j)
+        if (j == best) {
+          sidx = cur[j]++;
+          if (cur[j] < end[j]) head[j] = gtime[cur[j]];
+        }
+      const int64_t so = o - base;
+      if (so < kStage) {
+        s_src[so] = sidx;
+        s_pos[so] = (unsigned char)best;
+        s_time[so] = bt;
+      } else {
+        src[o] = sidx;
+        pos[o] = best;
+        time[o] = bt;
+      }
     }
   }
-  int64_t o = field_off[i];
-  const int64_t oe = field_off[i + 1];
-  for (; o < oe; ++o) {
-    // smallest head time; ties -> lowest position (lists are in position order)
-    int best = -1;
-    int64_t bt = 0;
-    for (int j = 0; j < n; ++j)
-      if (cur[j] < end[j] && (best < 0 || head[j] < bt)) {
-        best = j;
-        bt = head[j];
-      }
-    if (best < 0) break;  // offsets inconsistent with the lists (not produced by field_lengths)
-    src[o] = cur[best];
-    pos[o] = lp[best];
-    time[o] = bt;
-    if (++cur[best] < end[best]) head[best] = gtime[cur[best]];
+  __syncthreads();
+  const int64_t ns = span < kStage ? span : kStage;
+  for (int64_t k = threadIdx.x; k < ns; k += kFillThreads) {
+    src[base + k] = s_src[k];
+    pos[base + k] = s_pos[k];
+    time[base + k] = s_time[k];
   }
 }
 
@@ -173,8 +208,15 @@ extern "C" int ssla_route_fill(const int* map, const int64_t* gstart, const int6
   int rc = check_geo(geo);
   if (rc) return rc;
   if (F == 0) return SSLA_OK;
-  fill_kernel<<<(unsigned)ceil_div(F, 128), 128, 0, (cudaStream_t)stream>>>(map, gstart, glen, gtime, geo, field_ids,
-                                                                            field_off, F, src, pos, time);
+  const unsigned grid = (unsigned)ceil_div(F, kFillThreads);
+  const int area = (int)(kh * kw);
+  cudaStream_t s = (cudaStream_t)stream;
+#define SSLA_FILL(A) fill_kernel<A><<<grid, kFillThreads, 0, s>>>(map, gstart, glen, gtime, geo, field_ids, field_off, F, src, pos, time)
+  if (area <= 4) SSLA_FILL(4);
+  else if (area <= 9) SSLA_FILL(9);
+  else if (area <= 16) SSLA_FILL(16);
+  else SSLA_FILL(32);
+#undef SSLA_FILL
   SSLA_CHECK_LAUNCH("ssla_route_fill");
   return SSLA_OK;
 }
