@@ -127,10 +127,11 @@ class MosAttention(nn.Module):
     def _forward_fused(self, inputs, residual, r):
         """Inference path.  The q/v/g projections are folded into the per-position scatter
         weights ([Wq; Wv; Wg] Ws_p) and o_proj into the gather weights (Wg_p Wo), so the only
-        per-patch-event work is one fused kernel: projection of the event's input row by its
-        position's folded weights (in shared memory; for wide layers a GEMM over the pixel
-        events precomputes them instead), sigmoid gate, scan and q*h written into the
-        [E, P*C] buffer; one GEMM over that buffer closes the layer."""
+        per-patch-event work is one fused kernel: gather of the event's projected row (one GEMM
+        over the pixel events computes all positions; when that buffer would be very large the
+        projection runs inside the kernel from shared-memory weights instead), sigmoid gate,
+        scan and q*h written into the [E, P*C] buffer; one GEMM over that buffer closes the
+        layer."""
         src, pos_id = r["src"], r["pos_id"]
         E, C = residual.shape[0], self.hidden_size
         ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
@@ -150,8 +151,8 @@ class MosAttention(nn.Module):
         else:
             qh = torch.zeros((E * Pg, C), device=residual.device, dtype=torch.float32)
             dst = src * Pg + pos_id  # unique (event, position) pairs
-        if _mos.patch_scan_proj_fits(P, C, self.input_size):
-            # projection inside the scan kernel (weights in shared memory)
+        if _mos.use_patch_scan_proj(E, P, C, self.input_size):
+            # projection inside the scan kernel (weights in shared memory): no [E, P*3C] buffer
             _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
         else:
             y = residual @ w_all.reshape(P * 3 * C, self.input_size).t()  # [E, P*3C] = rows (e, p) of 3C

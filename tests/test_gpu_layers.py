@@ -186,3 +186,24 @@ def test_routing_kernels_match_torch_formulation(frame, k, stride):
     got = replicate_to_fields(*(a.cuda() if torch.is_tensor(a) else a for a in args), batch_size=B)
     for key in ("field_id", "lengths", "src", "pos_id", "time"):
         assert torch.equal(got[key].cpu(), ref[key]), key
+
+
+def test_mos_attention_in_kernel_projection_matches(monkeypatch):
+    """The memory-saving inference variant (projection inside the scan kernel) against the
+    GEMM-fed one on the same layer and inputs."""
+    import ssla_b200.ops.mos as mos
+    from ssla_b200.layers import MosAttention
+    from ssla_b200.model import preprocess_inputs
+    from ssla_b200.synthetic import seeded_parameters
+
+    ev, ln = _events(1)
+    x = preprocess_inputs(ev, ln, (240, 304))
+    x["events"] = torch.randn(x["events"].shape[0], 12, generator=torch.Generator().manual_seed(2)).cuda()
+    layer = MosAttention(12, 24, (240, 304), [3, 3])
+    seeded_parameters(layer, 5)
+    layer = layer.cuda()
+    with torch.no_grad():
+        ref = layer(dict(x))["events"]
+        monkeypatch.setattr(mos, "Y_BYTES_LIMIT", 0)
+        got = layer(dict(x))["events"]
+    assert rel_err(got, ref) < FP32_TOL
