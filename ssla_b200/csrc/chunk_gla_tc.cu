@@ -170,8 +170,8 @@ __device__ __forceinline__ void state_regs(const unsigned char* src, const Own& 
 // From the staged raw gate tile: in-chunk cumulative sums gc, ref (gc of row 31), gL (row 63),
 // exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk, and E = exp(gc - ref)
 // (STORE_GC: gc itself).  Thread (column c = tid % 64, group q = tid / 64) scans rows
-// RG*q .. RG*q+RG-1 of its column serially in registers; the group totals are combined
-// through shared memory.
+// RG*q .. RG*q+RG-1 of its column serially in registers; ref and gL come from the group
+// totals, so one barrier combines them.
 template <typename Tg, bool STORE_GC>
 __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw) {
   static_assert(NT % 64 == 0 && 31 % RG == RG - 1, "row 31 must end a group");
@@ -187,14 +187,21 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   }
   G.part[qt][c] = run;
   __syncthreads();
-  float off = 0.f;
-  for (int j = 0; j < qt; ++j) off += G.part[j][c];
+  // prefix of this group, ref (rows 0..31) and gL (all rows) from the group totals: one barrier
+  float off = 0.f, ref = 0.f, gl = 0.f;
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    const float pj = G.part[j][c];
+    if (j < qt) off += pj;
+    if (j <= 31 / RG) ref += pj;
+    gl += pj;
+  }
 #pragma unroll
   for (int i = 0; i < RG; ++i) x[i] += off;
-  if (qt == 31 / RG) G.ref[c] = x[RG - 1];  // row 31
-  if (qt == NG - 1) G.gl[c] = x[RG - 1];    // row 63
-  __syncthreads();
-  const float ref = G.ref[c];
+  if (qt == 0) {
+    G.ref[c] = ref;
+    G.gl[c] = gl;
+  }
   float m = 0.f;
 #pragma unroll
   for (int i = 0; i < RG; ++i) {
@@ -206,7 +213,7 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   if ((tid & 31) == 0) atomicMax(&G.span_bits, __float_as_uint(m));
   if (qt == 0) {
     G.eref[c] = __expf(ref);
-    G.egl[c] = __expf(G.gl[c] - ref);
+    G.egl[c] = __expf(gl - ref);
   }
   __syncthreads();
 }
