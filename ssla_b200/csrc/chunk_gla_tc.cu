@@ -788,14 +788,27 @@ template <typename K_>
 int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned& grid) {
   int rc = prepare(kern, smem);
   if (rc) return rc;
-  int dev = 0, sms = 0, per_sm = 0;
+  // CTAs per SM from the kernel's own resources (the occupancy query can report the pre-launch
+  // shared-memory configuration on a kernel's first call): 228 KB of shared memory per SM with
+  // 1 KB reserved per CTA, 64K registers allocated per warp in multiples of 8 per thread,
+  // 2048 threads, 512 TMEM columns.
+  int dev = 0, sms = 0;
+  cudaFuncAttributes fa;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem) != cudaSuccess || per_sm < 1) {
-    set_error("chunk_gla tensor-core kernel: occupancy query failed");
+      cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+    set_error("chunk_gla tensor-core kernel: attribute query failed");
     return SSLA_ERR_CUDA;
   }
+  const int by_smem = (int)((228 * 1024) / (smem + fa.sharedSizeBytes + 1024));
+  const int by_regs = 65536 / (((fa.numRegs + 7) / 8) * 8 * NT);
+  int per_sm = by_smem < by_regs ? by_smem : by_regs;
+  if (per_sm > 2048 / NT) per_sm = 2048 / NT;
   if (per_sm * tmem_cols > 512) per_sm = 512 / tmem_cols;
+  if (per_sm < 1) {
+    set_error("chunk_gla tensor-core kernel: %zu bytes of shared memory do not fit an SM", smem);
+    return SSLA_ERR_CUDA;
+  }
   const int64_t cap = (int64_t)per_sm * sms;
   grid = (unsigned)(items < cap ? items : cap);
   return SSLA_OK;
