@@ -47,8 +47,13 @@ FWD_BYTES = 4 * _E * 2 + _S + _E * 2 + _S
 BWD_BYTES = 5 * _E * 2 + 2 * _S + 3 * _E * 2 + _E * 4 + _S
 ALG_BYTES = FWD_BYTES + BWD_BYTES
 ALG_FLOPS = 12 * 2 * K * V * TOKENS * H
+# DRAM bytes (read + write) of one backward call, from the ncu capture summarised in
+# profiles/chunk_gla_c2_dram_traffic.md (cold caches)
+BWD_DRAM_BYTES = 124_600_000
 METRIC = "chunk-GLA fwd+bwd tokens/s"
-LAUNCHES_PER_STEP = 8  # fwd: chunk offsets, local state, state scan, output; bwd: the same four
+# fwd: chunk table, local state, state scan, tensor-core output, exact-path launch; bwd: the
+# same five (chunk table, adjoint increments, reverse scan, tensor-core backward, exact path)
+LAUNCHES_PER_STEP = 10
 
 
 def make_inputs(seed: int, device="cpu"):
@@ -528,6 +533,7 @@ def main():
         return
     hbm, which = peaks()
     fwd_gbs = FWD_BYTES / fwd_s / 1e9
+    bwd_gbs = BWD_BYTES / bwd_s / 1e9
     step_gbs = ALG_BYTES / (secs / args.steps) / 1e9
     cpu = None
     if not args.no_cpu_baseline and world == 1:
@@ -541,11 +547,15 @@ def main():
         "config": {"workload": "chunk_gla fwd+bwd, B=8 H=4 T=2048 K=V=64 bf16, h0+dht (BASELINE config 2)",
                    "per_rank_tokens": TOKENS, "l2": "flushed (256 MB write) before every timed step",
                    "parallelism": f"independent sequence shards x{world}"},
-        "roofline": {"bound": "hbm", "scope": "whole fwd+bwd step (all launches)",
-                     "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
-                     "peak_source": which, "traffic": None, "alg_bytes_per_step": ALG_BYTES,
+        "roofline": {"bound": "hbm",
+                     "scope": "dominant launch: the ssla_chunk_gla_bwd call (chunk table, adjoint increments, "
+                              "reverse state scan, tensor-core backward, exact-path launch), CUDA events",
+                     "achieved": bwd_gbs, "peak": hbm, "unit": "GB/s", "frac": bwd_gbs / hbm,
+                     "peak_source": which, "traffic": BWD_DRAM_BYTES, "alg_bytes": BWD_BYTES,
+                     "backward_ms": bwd_s * 1e3,
                      "forward": {"achieved": fwd_gbs, "frac": fwd_gbs / hbm, "ms": fwd_s * 1e3},
-                     "backward_ms": bwd_s * 1e3, "tensor_flops_per_step": ALG_FLOPS},
+                     "step": {"achieved": step_gbs, "frac": step_gbs / hbm, "alg_bytes": ALG_BYTES},
+                     "tensor_flops_per_step": ALG_FLOPS},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "cpu_baseline": cpu,
