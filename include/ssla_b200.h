@@ -171,6 +171,11 @@ int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const float* w, int6
                                  const int64_t* src, const int64_t* pos, const int64_t* dst,
                                  const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
                                  ssla_stream_t stream);
+/* out[M, N] (row stride ldo) = A[M, K] (row stride lda) @ B[K, N] (contiguous), fp32, for
+ * skinny shapes (B must fit in 96 KiB of shared memory: ssla_rows_matmul_smem_bytes). */
+size_t ssla_rows_matmul_smem_bytes(int64_t K, int64_t N);
+int ssla_rows_matmul_f32(const float* A, int64_t M, int64_t K, int64_t lda, const float* B, int64_t N,
+                         float* out, int64_t ldo, ssla_stream_t stream);
 /* out = LayerNorm(x + r) * w + b over rows of C channels (r may be NULL); 1 <= C <= 1024.  Replaces the residual add + nn.LayerNorm closing MosAttention
  * and LinearAttention (layers/mos_attention.py:144, layers/linear_attention.py:100). */
 int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, const float* b,

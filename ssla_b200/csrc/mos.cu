@@ -17,6 +17,12 @@
 // sequence (each x element feeds 12 FMAs); events are taken U at a time so their loads and
 // projections overlap, only the scan itself is serial.  Used when W fits in shared memory (the narrow, high-volume layers).
 //
+// rows_matmul: out[M, N] = A[M, K] @ B[K, N] (fp32) for the skinny shapes of the MoS layer
+// (K or N of a few dozen: the folded scatter projection [events, I] x [I, P*3C] and the gather
+// projection [events, P*C] x [P*C, C]), where a tiled library GEMM wastes most of its tile.
+// Persistent blocks stage B once in shared memory; one thread owns one row, streams it in
+// float4 pieces and accumulates 32 output columns at a time from broadcast float4 reads of B.
+//
 // layernorm_residual: out = LayerNorm(x + r) * w + b over rows of C channels (two-pass mean /
 // variance in fp32).  Rows of up to 32 channels take one thread each, wider rows one warp.
 #include "common.cuh"
@@ -131,6 +137,71 @@ __global__ void __launch_bounds__(256) mos_patch_scan_proj_kernel(
   }
 }
 
+constexpr int RM_THREADS = 128, RM_NC = 32;
+
+template <bool VEC_A>
+__global__ void __launch_bounds__(RM_THREADS) rows_matmul_kernel(const float* __restrict__ A, int64_t M, int K, int64_t lda,
+                                                                 const float* __restrict__ B, int N,
+                                                                 float* __restrict__ out, int64_t ldo) {
+  extern __shared__ float bs[];  // [K][Np], Np = N rounded up to RM_NC (zero padded)
+  const int Np = (N + RM_NC - 1) / RM_NC * RM_NC;
+  for (int e = threadIdx.x; e < K * Np; e += RM_THREADS) {
+    const int k = e / Np, n = e - k * Np;
+    bs[e] = n < N ? B[(int64_t)k * N + n] : 0.f;
+  }
+  __syncthreads();
+  for (int64_t row = (int64_t)blockIdx.x * RM_THREADS + threadIdx.x; row < M; row += (int64_t)gridDim.x * RM_THREADS) {
+    const float* a = A + row * lda;
+    float* o = out + row * ldo;
+    for (int n0 = 0; n0 < N; n0 += RM_NC) {
+      float acc[RM_NC];
+#pragma unroll
+      for (int j = 0; j < RM_NC; ++j) acc[j] = 0.f;
+      int k = 0;
+      if (VEC_A) {
+        for (; k + 4 <= K; k += 4) {
+          const float4 av = *reinterpret_cast<const float4*>(a + k);
+          const float ak[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const float* br = bs + (k + kk) * Np + n0;
+#pragma unroll
+            for (int j = 0; j < RM_NC; j += 4) {
+              const float4 b = *reinterpret_cast<const float4*>(br + j);
+              acc[j] = fmaf(ak[kk], b.x, acc[j]);
+              acc[j + 1] = fmaf(ak[kk], b.y, acc[j + 1]);
+              acc[j + 2] = fmaf(ak[kk], b.z, acc[j + 2]);
+              acc[j + 3] = fmaf(ak[kk], b.w, acc[j + 3]);
+            }
+          }
+        }
+      }
+      for (; k < K; ++k) {
+        const float ak = a[k];
+        const float* br = bs + k * Np + n0;
+#pragma unroll
+        for (int j = 0; j < RM_NC; j += 4) {
+          const float4 b = *reinterpret_cast<const float4*>(br + j);
+          acc[j] = fmaf(ak, b.x, acc[j]);
+          acc[j + 1] = fmaf(ak, b.y, acc[j + 1]);
+          acc[j + 2] = fmaf(ak, b.z, acc[j + 2]);
+          acc[j + 3] = fmaf(ak, b.w, acc[j + 3]);
+        }
+      }
+      const int nn = N - n0 < RM_NC ? N - n0 : RM_NC;
+      if (nn == RM_NC && ((reinterpret_cast<uintptr_t>(o + n0) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < RM_NC; j += 4)
+          *reinterpret_cast<float4*>(o + n0 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < RM_NC; ++j)
+          if (j < nn) o[n0 + j] = acc[j];
+      }
+    }
+  }
+}
+
 // One thread per row (C <= 32).
 __global__ void __launch_bounds__(256) ln_row_thread_kernel(const float* __restrict__ x, const float* __restrict__ r,
                                                             const float* __restrict__ w, const float* __restrict__ b,
@@ -238,6 +309,38 @@ extern "C" int ssla_mos_patch_scan_proj_fwd(const float* x, int64_t I, const flo
       x, (int)I, w, (int)P, src, pos, dst, cu, n_seqs, (int)C, z);
   SSLA_CHECK_LAUNCH("ssla_mos_patch_scan_proj_fwd");
   return SSLA_OK;
+}
+
+extern "C" size_t ssla_rows_matmul_smem_bytes(int64_t K, int64_t N) {
+  return (size_t)K * (size_t)((N + RM_NC - 1) / RM_NC * RM_NC) * sizeof(float);
+}
+
+extern "C" int ssla_rows_matmul_f32(const float* A, int64_t M, int64_t K, int64_t lda, const float* B, int64_t N,
+                                    float* out, int64_t ldo, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(M >= 0 && K > 0 && N > 0 && lda >= K && ldo >= N, "ssla_rows_matmul_f32: bad sizes");
+  const size_t smem = ssla_rows_matmul_smem_bytes(K, N);
+  SSLA_CHECK_ARG(smem <= 96 * 1024, "ssla_rows_matmul_f32: B of %zu bytes exceeds shared memory", smem);
+  if (M == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(A && B && out, "ssla_rows_matmul_f32: null pointer");
+  const bool vec = lda % 4 == 0 && aligned_to(A, 16);
+  auto launch = [&](auto kern) -> int {
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      set_error("ssla_rows_matmul_f32: cannot reserve %zu bytes of shared memory", smem);
+      return SSLA_ERR_CUDA;
+    }
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, RM_THREADS, smem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    const int64_t blocks = ceil_div(M, RM_THREADS);
+    const int64_t cap = (int64_t)per_sm * sms;
+    kern<<<(unsigned)(blocks < cap ? blocks : cap), RM_THREADS, smem, (cudaStream_t)stream>>>(A, M, (int)K, lda, B,
+                                                                                            (int)N, out, ldo);
+    SSLA_CHECK_LAUNCH("ssla_rows_matmul_f32");
+    return SSLA_OK;
+  };
+  return vec ? launch(rows_matmul_kernel<true>) : launch(rows_matmul_kernel<false>);
 }
 
 extern "C" int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, const float* b,

@@ -155,15 +155,15 @@ class MosAttention(nn.Module):
             # projection inside the scan kernel (weights in shared memory): no [E, P*3C] buffer
             _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
         else:
-            y = residual @ w_all.reshape(P * 3 * C, self.input_size).t()  # [E, P*3C] = rows (e, p) of 3C
+            y = _mos.matmul_rows(residual, w_all.reshape(P * 3 * C, self.input_size).t())  # rows (e, p) of 3C
             key = src if P == 1 else src * P + pos_id
             _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
         if Pg == 1:
-            out = index_add_rows_ad(qh, src, E) @ wgo[0].t()
+            out = _mos.matmul_rows(index_add_rows_ad(qh, src, E), wgo[0].t())
         else:
-            out = qh.view(E, Pg * C) @ wgo.permute(0, 2, 1).reshape(Pg * C, C)
+            out = _mos.matmul_rows(qh.view(E, Pg * C), wgo.permute(0, 2, 1).reshape(Pg * C, C))
         if self.input_proj is not None:
-            residual = self.input_proj(residual)
+            residual = _mos.matmul_rows(residual, self.input_proj.weight.t())
         out = _mos.layernorm_residual(out, residual, self.norm.weight, self.norm.bias, self.norm.eps)
         return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
                 "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}

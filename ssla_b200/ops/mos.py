@@ -70,6 +70,24 @@ def patch_scan_proj(x: torch.Tensor, w: torch.Tensor, src: torch.Tensor, pos: to
     return z
 
 
+ROWS_MATMUL_SMEM = 64 * 1024
+
+
+def matmul_rows(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a [M, K] @ b [K, N] in fp32: the row kernel for skinny shapes (b fits in shared memory),
+    torch.matmul otherwise."""
+    K, N = b.shape
+    if (a.dtype != torch.float32 or b.dtype != torch.float32 or a.dim() != 2 or a.stride(1) != 1
+            or _lib.load().ssla_rows_matmul_smem_bytes(K, N) > ROWS_MATMUL_SMEM):
+        return a @ b
+    _lib.require_cuda(a, b, what="matmul_rows")
+    b = b.contiguous()
+    out = torch.empty((a.shape[0], N), device=a.device, dtype=torch.float32)
+    _lib.check(_lib.load().ssla_rows_matmul_f32(a.data_ptr(), a.shape[0], K, a.stride(0), b.data_ptr(), N,
+                                                out.data_ptr(), N, _lib.stream_of(a)), "matmul_rows")
+    return out
+
+
 def layernorm_residual(x: torch.Tensor, r: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
                        eps: float) -> torch.Tensor:
     """LayerNorm(x + r) * weight + bias over the last dimension (fp32, forward only)."""

@@ -207,3 +207,20 @@ def test_mos_attention_in_kernel_projection_matches(monkeypatch):
         monkeypatch.setattr(mos, "Y_BYTES_LIMIT", 0)
         got = layer(dict(x))["events"]
     assert rel_err(got, ref) < FP32_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(4097, 12, 324), (3000, 108, 12), (513, 7, 45), (1000, 216, 24), (0, 12, 12)])
+def test_matmul_rows_matches_torch(M, K, N):
+    """The skinny fp32 row kernel (MoS inference projections) against a float64 product, on
+    vectorised (K % 4 == 0) and scalar row paths, a strided A and an empty A."""
+    from ssla_b200.ops.mos import matmul_rows
+
+    gen = torch.Generator().manual_seed(M + K + N)
+    a_full = torch.randn(M, K + 3, generator=gen)
+    a = a_full[:, :K] if K % 4 else torch.randn(M, K, generator=gen)
+    b = torch.randn(K, N, generator=gen)
+    ref = (a.double() @ b.double()).float()
+    got = matmul_rows(a.cuda(), b.cuda())
+    assert got.shape == (M, N)
+    if M:
+        assert rel_err(got, ref) < 1e-6
