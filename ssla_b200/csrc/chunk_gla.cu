@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_launch_dependents();
+  griddep_wait();  // the previous call's kernels may still read the table
   if (tid == 0) {
     carry = 0;
     if (exact_count) *exact_count = 0;
@@ -108,6 +110,8 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
     bool reverse, int nseg) {
   __shared__ float sA[SCAN_MAXSEG][SCAN_EL], sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
   const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t KV = (int64_t)K * V, HKV = (int64_t)H * KV, HK = (int64_t)H * K;
   const int64_t idx = (int64_t)blockIdx.x * SCAN_EL + el;
   const bool valid = idx < N * HKV;
@@ -425,6 +429,8 @@ __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
     const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
     T* __restrict__ o, const int* __restrict__ flags, int64_t MC) {
+  griddep_launch_dependents();
+  griddep_wait();
   if (!flags) {
     fwd_o_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
     return;
@@ -644,6 +650,8 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
     const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
     T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ flags, int64_t MC) {
+  griddep_launch_dependents();
+  griddep_wait();
   if (!flags) {
     bwd_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
     return;
@@ -687,8 +695,8 @@ int run_fwd_o(const void* q, const void* k, const void* v, const void* g, const 
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
                           : dim3((unsigned)MC, H);
-  kern<<<grid, NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H,
-                                K, V, scale, states, (T*)o, flags, MC);
+  launch_pdl(kern, grid, dim3(NTHR), smem, s, (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K,
+             V, scale, states, (T*)o, flags, MC);
   SSLA_CHECK_LAUNCH("chunk_gla fwd_o");
   return SSLA_OK;
 }
@@ -703,9 +711,8 @@ int run_bwd(const void* q, const void* k, const void* v, const void* g, const in
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
                           : dim3((unsigned)MC, H);
-  kern<<<grid, NTHR, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H,
-                                K, V, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk,
-                                (T*)dv, dg, flags, MC);
+  launch_pdl(kern, grid, dim3(NTHR), smem, s, (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K,
+             V, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, flags, MC);
   SSLA_CHECK_LAUNCH("chunk_gla bwd");
   return SSLA_OK;
 }
@@ -760,7 +767,7 @@ int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v
 
 int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chunk_off,
                          longlong2* chunk_tab, int* flags, cudaStream_t s) {
-  chunk_offsets_kernel<<<1, 1024, 0, s>>>(cu, N, MC, chunk_off, chunk_tab, flags);
+  launch_pdl(chunk_offsets_kernel, dim3(1), dim3(1024), 0, s, cu, N, MC, chunk_off, chunk_tab, flags);
   SSLA_CHECK_LAUNCH("chunk_gla chunk_offsets");
   return SSLA_OK;
 }
@@ -773,8 +780,8 @@ int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_
   // segments per element: enough threads for about one resident wave (148 SMs x 2048)
   int64_t nseg = (int64_t)kNumSMs * 2048 / threads;
   nseg = nseg < 1 ? 1 : (nseg > SCAN_MAXSEG ? SCAN_MAXSEG : nseg);
-  state_scan_kernel<<<ceil_div(threads, SCAN_EL), SCAN_EL * (int)nseg, 0, s>>>(
-      dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk, final_state, reverse, (int)nseg);
+  launch_pdl(state_scan_kernel, dim3(ceil_div(threads, SCAN_EL)), dim3(SCAN_EL * (int)nseg), 0, s, dS, decay, chunk_off,
+             N, (int)H, (int)K, (int)V, init, per_chunk, final_state, reverse, (int)nseg);
   SSLA_CHECK_LAUNCH("chunk_gla state_scan");
   return SSLA_OK;
 }

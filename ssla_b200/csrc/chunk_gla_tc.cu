@@ -387,6 +387,7 @@ __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
   __shared__ uint64_t mbar, full[2];
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
+  griddep_launch_dependents();
   if (warp == 0) tmem_alloc(&tbase_s, 64);
   if (tid == 0) {
     mbar_init(&mbar, 1);
@@ -403,6 +404,7 @@ __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
   const CUtensorMap* m16[2] = {&ma, &mb};
   if (tid == 0)
     for (const CUtensorMap* m : {&ma, &mb, &mg}) prefetch_tensormap(m);
+  griddep_wait();  // predecessors wrote the chunk table / states this kernel reads
   persistent_loop(
       MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
@@ -473,6 +475,7 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
   __shared__ uint64_t mbar, full[2];
   __shared__ uint32_t tbase_s;
   const int tid = threadIdx.x, warp = tid >> 5;
+  griddep_launch_dependents();
   if (warp == 0) tmem_alloc(&tbase_s, 128);
   if (tid == 0) {
     mbar_init(&mbar, 1);
@@ -490,6 +493,7 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
   if (tid == 0)
     for (const CUtensorMap* m : {&mq, &mk, &mv, &mg, &mh}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
+  griddep_wait();  // predecessors wrote the chunk table / states this kernel reads
   persistent_loop(
       MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
@@ -590,6 +594,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
   __shared__ uint32_t tbase_s;
   __shared__ float s_hd8[8][D], s_dgl[D];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  griddep_launch_dependents();
   if (warp == 0) tmem_alloc(&tbase_s, 256);
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -608,6 +613,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
   if (tid == 0)
     for (const CUtensorMap* m : {&mq, &mk, &mv, &mdo, &mg, &mh, &mdh}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
+  griddep_wait();  // predecessors wrote the chunk table / states this kernel reads
   persistent_loop(
       MC, H, chunk_tab, full,
       [&](const Item& x, int st) {
@@ -923,7 +929,7 @@ int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const vo
     unsigned grid = 0;
     int rc2 = persistent_grid(kern, smem, 64, MC * H, grid);
     if (rc2) return rc2;
-    kern<<<grid, NT, smem, s>>>(ma, mb, mg, mode, chunk_tab, (int)MC, (int)H, scale, dS, decay);
+    launch_pdl(kern, dim3(grid), dim3(NT), smem, s, ma, mb, mg, mode, chunk_tab, (int)MC, (int)H, scale, dS, decay);
     SSLA_CHECK_LAUNCH("chunk_gla tc_local_state");
     return SSLA_OK;
   });
@@ -946,7 +952,8 @@ int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v
     unsigned grid = 0;
     int rc2 = persistent_grid(kern, smem, 128, MC * H, grid);
     if (rc2) return rc2;
-    kern<<<grid, NT, smem, s>>>(mq, mk, mv, mg, mh, chunk_tab, (int)MC, (int)H, scale, (T_*)o, flags);
+    launch_pdl(kern, dim3(grid), dim3(NT), smem, s, mq, mk, mv, mg, mh, chunk_tab, (int)MC, (int)H, scale, (T_*)o,
+               flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_fwd_o");
     return SSLA_OK;
   });
@@ -971,8 +978,8 @@ int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, 
     unsigned grid = 0;
     int rc2 = persistent_grid(kern, smem, 256, MC * H, grid);
     if (rc2) return rc2;
-    kern<<<grid, NT, smem, s>>>(mq, mk, mv, mdo, mg, mh, mdh, chunk_tab, (int)MC, (int)H, scale, (T_*)dq,
-                                (T_*)dk, (T_*)dv, dg, flags);
+    launch_pdl(kern, dim3(grid), dim3(NT), smem, s, mq, mk, mv, mdo, mg, mh, mdh, chunk_tab, (int)MC, (int)H, scale,
+               (T_*)dq, (T_*)dk, (T_*)dv, dg, flags);
     SSLA_CHECK_LAUNCH("chunk_gla tc_bwd");
     return SSLA_OK;
   });

@@ -8,6 +8,8 @@
 #include <stdio.h>
 #include <stdarg.h>
 
+#include <utility>
+
 #include "../../include/ssla_b200.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -53,6 +55,30 @@ template <> struct Io<__half> {
 
 template <typename T> __device__ __forceinline__ float ldf(const T* p) { return Io<T>::ld(p); }
 template <typename T> __device__ __forceinline__ void stf(T* p, float x) { Io<T>::st(p, x); }
+
+// Programmatic dependent launch (chunk path).  A kernel launched with launch_pdl may start
+// while its stream predecessor is still running: it calls griddep_launch_dependents() early
+// (letting its own successor launch once all of its CTAs have started) and griddep_wait()
+// after its prologue, before reading anything a predecessor wrote or writing anything a
+// predecessor may still read.  Both are no-ops for an ordinary launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 inline size_t dtype_size(int dt) { return dt == SSLA_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == SSLA_F32 || dt == SSLA_BF16 || dt == SSLA_F16; }
