@@ -26,6 +26,8 @@ inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 // off[s] = first row r with index[r] >= s, for s in [0, S]; index non-decreasing.
 __global__ void offsets_sorted_kernel(const int64_t* __restrict__ index, int64_t R, int64_t S,
                                       int64_t* __restrict__ off) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r > R) return;
   int64_t prev = r == 0 ? -1 : index[r - 1];
@@ -147,6 +149,8 @@ __global__ void __launch_bounds__(256) reduce_kernel(const T* __restrict__ src,
                                                      const int64_t* __restrict__ rows, int64_t R,
                                                      int64_t S, int64_t C, T* __restrict__ out,
                                                      int64_t* __restrict__ arg) {
+  griddep_launch_dependents();
+  griddep_wait();
   constexpr int U = 4;
   const int64_t s = (int64_t)blockIdx.x * blockDim.y + threadIdx.y;
   if (s >= S) return;
@@ -211,6 +215,8 @@ __global__ void __launch_bounds__(256) reduce_sorted_tiled_kernel(const T* __res
                                                                   int64_t R, int64_t S, int64_t C,
                                                                   int win_rows, T* __restrict__ out,
                                                                   int64_t* __restrict__ arg) {
+  griddep_launch_dependents();
+  griddep_wait();
   extern __shared__ uint4 stage4[];
   const T* stage = reinterpret_cast<const T*>(stage4);
   const int CV = (int)(C / VEC);
@@ -278,6 +284,8 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(256) gather_kernel(const T* __restrict__ src,
                                                      const int64_t* __restrict__ index, int64_t R,
                                                      int64_t C, T* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t CV = C / VEC;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= R * CV) return;
@@ -310,7 +318,7 @@ int run_reduce(const void* src, const int64_t* off, const int64_t* rows, int64_t
     }
     const size_t smem = (size_t)win * C * sizeof(T);
 #define SSLA_RED(VEC, OP)                                                                   \
-  reduce_sorted_tiled_kernel<T, VEC, OP><<<grid, 256, smem, s>>>((const T*)src, off, R, S, C, win, \
+  launch_pdl(reduce_sorted_tiled_kernel<T, VEC, OP>, dim3(grid), dim3(256), smem, s, (const T*)src, off, R, S, C, win, \
                                                                  (T*)out, arg)
     if (v4) {
       if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
@@ -321,7 +329,7 @@ int run_reduce(const void* src, const int64_t* off, const int64_t* rows, int64_t
   } else {
     const dim3 block((unsigned)CV, (unsigned)segs);
 #define SSLA_RED(VEC, OP) \
-  reduce_kernel<T, VEC, OP><<<grid, block, 0, s>>>((const T*)src, off, rows, R, S, C, (T*)out, arg)
+  launch_pdl(reduce_kernel<T, VEC, OP>, dim3(grid), block, 0, s, (const T*)src, off, rows, R, S, C, (T*)out, arg)
     if (v4) {
       if (op == 0) SSLA_RED(4, 0); else if (op == 1) SSLA_RED(4, 1); else SSLA_RED(4, 2);
     } else {
@@ -377,7 +385,7 @@ extern "C" int ssla_segment_offsets_sorted(const int64_t* index, int64_t R, int6
   SSLA_CHECK_ARG(R >= 0 && S >= 0, "ssla_segment_offsets_sorted: negative size");
   SSLA_CHECK_ARG(seg_offsets && (R == 0 || index), "ssla_segment_offsets_sorted: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  offsets_sorted_kernel<<<ceil_div(R + 1, 256), 256, 0, s>>>(index, R, S, seg_offsets);
+  launch_pdl(offsets_sorted_kernel, dim3(ceil_div(R + 1, 256)), dim3(256), 0, s, index, R, S, seg_offsets);
   SSLA_CHECK_LAUNCH("ssla_segment_offsets_sorted");
   return SSLA_OK;
 }
@@ -422,9 +430,9 @@ extern "C" int ssla_gather_rows(const void* src, int dtype, const int64_t* index
     const bool v4 = C % 4 == 0 && aligned_to(src, 4 * sizeof(T)) && aligned_to(out, 4 * sizeof(T));
     const int64_t threads = R * (v4 ? C / 4 : C);
     if (v4)
-      gather_kernel<T, 4><<<ceil_div(threads, 256), 256, 0, s>>>((const T*)src, index, R, C, (T*)out);
+      launch_pdl(gather_kernel<T, 4>, dim3(ceil_div(threads, 256)), dim3(256), 0, s, (const T*)src, index, R, C, (T*)out);
     else
-      gather_kernel<T, 1><<<ceil_div(threads, 256), 256, 0, s>>>((const T*)src, index, R, C, (T*)out);
+      launch_pdl(gather_kernel<T, 1>, dim3(ceil_div(threads, 256)), dim3(256), 0, s, (const T*)src, index, R, C, (T*)out);
     SSLA_CHECK_LAUNCH("ssla_gather_rows");
     return SSLA_OK;
   });
