@@ -26,6 +26,7 @@ import types
 from pathlib import Path
 
 import torch
+import yaml
 
 OUT = Path(__file__).resolve().parent
 ROOT = OUT.parent.parent
@@ -68,6 +69,30 @@ def install_shims():
         return oseg.scatter_mean(src, idx, int(dim_size))
 
     _stub("torch_scatter", scatter_max=scatter_max, scatter_mean=scatter_mean)
+
+
+def linear_attention(ref_root: str):
+    """Reference LinearAttention (layers/linear_attention.py:39-102) on one synthetic sample's
+    pixel groups: (input 2 -> hidden 12, with input / residual projections) and (12 -> 12, on
+    seeded N(0,1) features).  Saved: the output events of both layers."""
+    import layers.linear_attention as lin_mod
+    from model_mos import MosModel  # noqa: F401  (imports the layer stack and its stubs)
+
+    torch.set_grad_enabled(False)
+    events, lengths = event_batch(1, seed=11)
+    model = MosModel(yaml.safe_load(open(Path(ref_root) / "configs" / "model" / "MOS_S.yaml")), hot_pixel_thres=50,
+                     dataset="Gen1")
+    x = model.preprocess_inputs(events.clone(), lengths.clone())
+    out = {}
+    for I, C in ((2, 12), (12, 12)):
+        layer = lin_mod.LinearAttention(I, C, (240, 304)).eval()
+        seeded_parameters(layer, 500 + I)
+        xi = dict(x)
+        if I != 2:
+            xi["events"] = torch.randn(x["events"].shape[0], I, generator=torch.Generator().manual_seed(13))
+        out[f"in{I}_h{C}"] = layer(xi)["events"].clone()
+    torch.save(dict(seed=11, **out), OUT / "linear_attention.pt")
+    print("linear attention", {k: tuple(v.shape) for k, v in out.items()})
 
 
 def main(ref_root: str):
@@ -132,6 +157,20 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden_model.py <path to the ssla sources>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden_model.py <path to the ssla sources> [--linear-attention-only]")
+    if len(sys.argv) == 3:
+        install_shims()
+        _sort = torch.sort
+        torch.sort = lambda input, dim=-1, descending=False, stable=True, *, out=None: _sort(
+            input, dim=dim, descending=descending, stable=True)
+        sys.path.insert(0, sys.argv[1])
+        import yaml  # noqa: F401
+        import ops.common.scan as scan_mod
+        import layers.linear_attention as lin_mod
+
+        scan_mod.scan = lambda u, g, cu_seqlens: og.scan_ref_vectorized(u, g, cu_seqlens)
+        lin_mod.scan = scan_mod.scan
+        linear_attention(sys.argv[1])
+    else:
+        main(sys.argv[1])

@@ -224,3 +224,23 @@ def test_matmul_rows_matches_torch(M, K, N):
     assert got.shape == (M, N)
     if M:
         assert rel_err(got, ref) < 1e-6
+
+
+@pytest.mark.parametrize("I,C", [(2, 12), (12, 12)])
+def test_linear_attention_matches_reference(I, C):
+    """LinearAttention (layers/linear_attention.py:39-102) against the reference layer's output
+    on the same pixel groups and seeded weights (tests/golden/make_golden_model.py)."""
+    from ssla_b200.layers import LinearAttention
+    from ssla_b200.model import preprocess_inputs
+    from ssla_b200.synthetic import event_batch, seeded_parameters
+
+    gold = torch.load(GOLDEN / "linear_attention.pt")
+    ev, ln = event_batch(1, seed=gold["seed"])
+    x = preprocess_inputs(ev.cuda(), ln.cuda(), (240, 304))
+    if I != 2:
+        x["events"] = torch.randn(x["events"].shape[0], I, generator=torch.Generator().manual_seed(13)).cuda()
+    layer = LinearAttention(I, C, (240, 304)).eval()
+    seeded_parameters(layer, 500 + I)
+    with torch.no_grad():
+        out = layer.cuda()(x)["events"]
+    assert rel_err(out, gold[f"in{I}_h{C}"]) < FP32_TOL
