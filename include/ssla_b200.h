@@ -207,6 +207,18 @@ int ssla_route_fill(const int* map, const int64_t* gstart, const int64_t* glen, 
                     const int64_t* field_off, int64_t F, int64_t* src, int64_t* pos, int64_t* time,
                     ssla_stream_t stream);
 
+/* ---------------------------------------------------------------- detection post-processing
+ * Batched greedy NMS (MosModel.postprocess_with_nms, model_mos.py:232-299; torchvision nms on
+ * class-offset boxes, model_mos.py:20-29): for each of B images, the candidates (score >= conf
+ * when filtering) sorted by descending score (ascending index among equal scores), a box is
+ * kept unless an earlier kept box has IoU > iou_thr with it; at most max_det kept.
+ * boxes [B, N, 4] fp32 xyxy (class offsets applied), scores [B, N]; keep [B, max_det] anchor
+ * indices in score order, count [B].  N <= 4096. */
+size_t ssla_batched_nms_workspace_bytes(int64_t B);
+int ssla_batched_nms(const float* boxes, const float* scores, int64_t B, int64_t N, int filtering,
+                     float conf, float iou_thr, int64_t max_det, int64_t* keep, int64_t* count,
+                     void* workspace, size_t workspace_bytes, ssla_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,8 @@ SIGNATURES = {
     "ssla_mos_patch_scan_proj_fwd": (i32, [p, i64, p, i64, p, p, p, p, i64, i64, p, p]),
     "ssla_layernorm_residual_fwd": (i32, [p, p, p, p, i64, i64, f32, p, p]),
     "ssla_rows_matmul_smem_bytes": (sz, [i64, i64]),
+    "ssla_batched_nms_workspace_bytes": (sz, [i64]),
+    "ssla_batched_nms": (i32, [p, p, i64, i64, i32, f32, f32, i64, p, p, p, sz, p]),
     "ssla_rows_matmul_f32": (i32, [p, i64, i64, i64, p, i64, p, i64, p]),
 }
 

@@ -18,6 +18,7 @@ import torch.nn as nn
 
 from .layers import (LinearAttention, MosAttention, SparseAdaptiveAvgPool, SparseAdaptiveMaxPool, SparseAvgPool,
                      SparseMaxPool, TemporalDropout)
+from . import _lib
 from .ops import segment as _seg
 from .utils.farsecnn_utils import group_events, truncate_packed_sequence
 
@@ -149,6 +150,41 @@ class YOLOXHead(nn.Module):
         return torch.cat(outs, 1)
 
 
+@torch.no_grad()
+def postprocess_with_nms(preds: torch.Tensor, num_classes: int, frame_size, conf_thres: float = 0.001,
+                         iou_thres: float = 0.65, filtering: bool = True, max_det: int = 100) -> List[Dict]:
+    """Detections per image (model_mos.py:232-299): boxes xyxy, score = sigmoid(obj) *
+    max(sigmoid(cls)), labels; candidates below ``conf_thres`` dropped (``filtering``), greedy
+    NMS per class (class-offset boxes, model_mos.py:20-29) at ``iou_thres`` on the GPU
+    (``ssla_batched_nms``), at most ``max_det`` per image, in score order."""
+    if preds.dim() != 3 or preds.size(-1) < 6:
+        raise ValueError("preds must be (B, N, 4 + 1 + C)")
+    B, N, _ = preds.shape
+    cx, cy, w, h = preds[..., :4].unbind(dim=-1)
+    boxes = torch.stack([cx - 0.5 * w, cy - 0.5 * h, cx + 0.5 * w, cy + 0.5 * h], dim=-1)
+    obj = preds[..., 4].sigmoid()
+    class_conf, class_pred = preds[..., 5:5 + num_classes].sigmoid().max(dim=-1)
+    scores = obj * class_conf
+    labels = class_pred.to(torch.int64)
+    max_dim = max(int(frame_size[0]), int(frame_size[1]))
+    shifted = (boxes + (labels * float(max_dim + 1))[..., None]).float().contiguous()
+    _lib.require_cuda(shifted, what="postprocess_with_nms")
+    L = _lib.load()
+    keep = torch.empty((B, max_det), device=preds.device, dtype=torch.int64)
+    count = torch.empty(B, device=preds.device, dtype=torch.int64)
+    nb = L.ssla_batched_nms_workspace_bytes(B)
+    ws = torch.empty(max(nb, 1), device=preds.device, dtype=torch.uint8)
+    sc = scores.float().contiguous()
+    _lib.check(L.ssla_batched_nms(shifted.data_ptr(), sc.data_ptr(), B, N, int(filtering), float(conf_thres),
+                                  float(iou_thres), max_det, keep.data_ptr(), count.data_ptr(), ws.data_ptr(), nb,
+                                  _lib.stream_of(shifted)), "postprocess_with_nms")
+    out = []
+    for b, n in enumerate(count.tolist()):
+        idx = keep[b, :n]
+        out.append({"boxes": boxes[b][idx], "scores": scores[b][idx], "labels": labels[b][idx]})
+    return out
+
+
 class MosDetector(nn.Module):
     """Preprocessing + layer stack + grids + head (MosModel.forward, model_mos.py:157-170)."""
 
@@ -172,3 +208,8 @@ class MosDetector(nn.Module):
 
     def forward(self, events: torch.Tensor, lengths: torch.Tensor) -> torch.Tensor:
         return self.head(self.backbone_grids(events, lengths))
+
+    def postprocess_with_nms(self, preds: torch.Tensor, conf_thres: float = 0.001, iou_thres: float = 0.65,
+                             filtering: bool = True, max_det: int = 100) -> List[Dict]:
+        return postprocess_with_nms(preds, self.num_classes, self.frame_size, conf_thres, iou_thres, filtering,
+                                    max_det)

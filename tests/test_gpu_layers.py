@@ -244,3 +244,48 @@ def test_linear_attention_matches_reference(I, C):
     with torch.no_grad():
         out = layer.cuda()(x)["events"]
     assert rel_err(out, gold[f"in{I}_h{C}"]) < FP32_TOL
+
+
+def _nms_reference(preds, C, frame, conf, iou, filtering, max_det):
+    """The reference post-processing (model_mos.py:20-29, 232-299) on torchvision's nms."""
+    from torchvision.ops import nms
+
+    cx, cy, w, h = preds[..., :4].unbind(-1)
+    boxes = torch.stack([cx - 0.5 * w, cy - 0.5 * h, cx + 0.5 * w, cy + 0.5 * h], -1)
+    obj = preds[..., 4].sigmoid()
+    cc, cp = preds[..., 5:5 + C].sigmoid().max(-1)
+    scores = obj * cc
+    out = []
+    for b in range(preds.shape[0]):
+        bb, bs, bl = boxes[b], scores[b], cp[b].to(torch.int64)
+        if filtering:
+            k = bs >= conf
+            bb, bs, bl = bb[k], bs[k], bl[k]
+        keep = nms(bb + (bl * float(max(frame) + 1))[:, None], bs, iou)[:max_det]
+        out.append((bb[keep], bs[keep], bl[keep]))
+    return out
+
+
+@pytest.mark.parametrize("N,filtering,max_det", [(1140, True, 100), (1140, False, 100), (300, True, 5), (3000, True, 300)])
+def test_batched_nms_matches_torchvision(N, filtering, max_det):
+    """GPU batched NMS against the reference post-processing on torchvision's nms (clustered
+    boxes so many overlap, continuous scores so the order has no ties).  torchvision is a
+    third-party library of the reference, used here only as the checker."""
+    from ssla_b200.model import postprocess_with_nms
+
+    gen = torch.Generator().manual_seed(N + max_det)
+    B, C, frame = 6, 2, (240, 304)
+    centers = torch.rand(B, 12, 2, generator=gen) * torch.tensor([304.0, 240.0])
+    pick = torch.randint(0, 12, (B, N), generator=gen)
+    cxy = torch.gather(centers, 1, pick[..., None].expand(B, N, 2)) + 6 * torch.randn(B, N, 2, generator=gen)
+    wh = 20 + 30 * torch.rand(B, N, 2, generator=gen)
+    logits = torch.randn(B, N, 1 + C, generator=gen) * 2 - 1
+    preds = torch.cat([cxy, wh, logits], -1)
+    # the checker runs on the same device so scores (sigmoid) are bit-identical on both sides
+    ref = _nms_reference(preds.cuda(), C, frame, 0.2, 0.65, filtering, max_det)
+    got = postprocess_with_nms(preds.cuda(), C, frame, 0.2, 0.65, filtering, max_det)
+    for (rb, rs, rl), g in zip(ref, got):
+        assert len(rl) > 0
+        assert torch.equal(g["labels"], rl)
+        assert torch.equal(g["scores"], rs)
+        assert torch.equal(g["boxes"], rb)
