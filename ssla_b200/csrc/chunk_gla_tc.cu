@@ -218,12 +218,6 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   __syncthreads();
 }
 
-__device__ __forceinline__ void mbar_setup(uint64_t* mbar, int n) {
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < n; ++i) mbar_init(mbar + i, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-}
 
 // All threads: publish smem operand writes to the tensor core and order them before the MMA.
 __device__ __forceinline__ void operands_ready() {

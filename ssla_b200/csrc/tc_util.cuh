@@ -1,11 +1,9 @@
 // Minimal tcgen05 (5th-generation tensor core) helpers for sm_100a, written as inline PTX.
 //
-// Conventions used by the chunked-GLA kernels:
-//  * operands are 16-bit tiles in shared memory stored "8x8 blocked": element (r, c) of an
-//    R x C tile lives at byte ((r/8)*(C/8) + c/8)*128 + (r%8)*16 + (c%8)*2, i.e. 128-byte core
-//    matrices of 8 rows x 16 bytes.  One such tile serves as a K-major operand (rows = M/N,
-//    columns = K) or, read the other way, as an MN-major operand (rows = K, columns = M/N),
-//    with no swizzle (SWIZZLE_NONE descriptors);
+// Conventions used by the chunked-GLA kernels (chunk_gla_tc.cu):
+//  * operands are 64x64 16-bit tiles in shared memory in the 128-byte-swizzled layout TMA
+//    writes; one tile serves as a K-major or an MN-major operand through SWIZZLE_128B
+//    descriptors (built in chunk_gla_tc.cu on smem_desc below);
 //  * accumulators are fp32 in tensor memory (TMEM); an M=64 MMA with cta_group::1 writes row m
 //    to TMEM lane (m % 16) + 32 * (m / 16), column n, so warp w of a 4-warp group reads rows
 //    16w .. 16w+15 with its lanes 0..15;
@@ -20,26 +18,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Shared-memory matrix descriptor, SWIZZLE_NONE, version 1 (Blackwell).
+// Shared-memory matrix descriptor (Blackwell, version 1): start address, leading / stride
+// byte offsets; the layout-type field (bits 61-63) is left 0 (no swizzle) for callers to set.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);
   d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version
-  return d;                // base offset 0, lbo mode 0, layout type 0 (no swizzle)
-}
-
-// Descriptor of a 64-column blocked tile used K-major: K-adjacent core matrices 128 B apart,
-// M/N-adjacent ones (cols/8)*128 B apart.  k-step s (16 elements) starts 256*s bytes later.
-__device__ __forceinline__ uint64_t desc_kmajor(const void* tile, int cols, int kstep) {
-  return smem_desc(smem_u32(tile) + 256u * kstep, 128u, (uint32_t)(cols / 8) * 128u);
-}
-// The same storage read MN-major (tile rows = K): M/N-adjacent core matrices 128 B apart,
-// K-adjacent ones (cols/8)*128 B apart; k-step s starts 2*(cols/8)*128*s bytes later.
-__device__ __forceinline__ uint64_t desc_mnmajor(const void* tile, int cols, int kstep) {
-  const uint32_t kstride = (uint32_t)(cols / 8) * 128u;
-  return smem_desc(smem_u32(tile) + 2u * kstride * kstep, kstride, 128u);
+  return d;                // base offset 0, lbo mode 0
 }
 
 // Instruction descriptor: kind::f16, fp32 accumulate.  in_fmt 0 = f16, 1 = bf16.
@@ -123,15 +110,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
-// Bulk (non-tensor) copy global -> shared of `bytes` (multiple of 16, both addresses 16-byte
-// aligned), completing on `mbar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(mbar))
-               : "memory");
-}
-
 // Warp-collective TMEM allocation (ncols: power of two >= 32); address written to *dst.
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
@@ -142,19 +120,6 @@ __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
-}
-
-// 16 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 16x256b.x2 load (warp-collective): 16 TMEM lanes x 16 columns spread over the 32 threads.
@@ -175,10 +140,6 @@ __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp, int col) 
   return base + ((uint32_t)(32 * warp) << 16) + (uint32_t)col;
 }
 
-// Byte offset of element (r, c) in an 8x8-blocked tile with `cols` columns (16-bit elements).
-__host__ __device__ __forceinline__ int blk_off(int r, int c, int cols) {
-  return ((r >> 3) * (cols >> 3) + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2;
-}
 
 }  // namespace tc
 }  // namespace ssla
