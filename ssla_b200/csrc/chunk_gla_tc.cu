@@ -104,7 +104,7 @@ template <typename T> __device__ __forceinline__ void st2_global(T* p, float a, 
 
 
 struct GateSmem {
-  float E[BT * LDG];  // exp(gc - ref) (or gc itself for local_state); dgc scratch in the backward
+  float E[BT * LDG];  // exp(gc - ref); dgc scratch in the backward
   float ref[D];       // gc of row 31
   float eref[D];      // exp(ref)
   float egl[D];       // exp(gL - ref), gL = gc of row 63
@@ -168,11 +168,10 @@ __device__ __forceinline__ void state_regs(const unsigned char* src, const Own& 
 }
 
 // From the staged raw gate tile: in-chunk cumulative sums gc, ref (gc of row 31), gL (row 63),
-// exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk, and E = exp(gc - ref)
-// (STORE_GC: gc itself).  Thread (column c = tid % 64, group q = tid / 64) scans rows
+// exp(ref), exp(gL - ref), the largest |gc - ref| of the chunk, and E = exp(gc - ref).  Thread (column c = tid % 64, group q = tid / 64) scans rows
 // RG*q .. RG*q+RG-1 of its column serially in registers; ref and gL come from the group
 // totals, so one barrier combines them.
-template <typename Tg, bool STORE_GC>
+template <typename Tg>
 __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw) {
   static_assert(NT % 64 == 0 && 31 % RG == RG - 1, "row 31 must end a group");
   const int tid = threadIdx.x, c = tid & 63, qt = tid >> 6;
@@ -206,7 +205,7 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
 #pragma unroll
   for (int i = 0; i < RG; ++i) {
     m = fmaxf(m, fabsf(x[i] - ref));
-    G.E[(RG * qt + i) * LDG + c] = STORE_GC ? x[i] : __expf(x[i] - ref);
+    G.E[(RG * qt + i) * LDG + c] = __expf(x[i] - ref);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -218,6 +217,41 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
   __syncthreads();
 }
 
+
+// Local-state gating fused into the in-chunk prefix sums: thread (column c = tid % 64, group
+// q = tid / 64) computes gc for rows RG*q .. RG*q+RG-1 of column c and scales those elements of
+// the 16-bit tile in place: mode 0 (state increment) by exp(gL - gc), mode 1 (adjoint
+// increment) by scale * exp(gc).  Writes G.gl; one barrier.
+template <typename T, typename Tg>
+__device__ __forceinline__ void gate_apply_local(GateSmem& G, const unsigned char* raw, unsigned char* tile, int mode,
+                                                 float scale) {
+  const int tid = threadIdx.x, c = tid & 63, qt = tid >> 6;
+  const Tg* gr = reinterpret_cast<const Tg*>(raw);
+  float x[RG];
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < RG; ++i) {
+    run += ldf(gr + (RG * qt + i) * D + c);
+    x[i] = run;
+  }
+  G.part[qt][c] = run;
+  __syncthreads();
+  float off = 0.f, gl = 0.f;
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    const float pj = G.part[j][c];
+    if (j < qt) off += pj;
+    gl += pj;
+  }
+#pragma unroll
+  for (int i = 0; i < RG; ++i) {
+    const float gc = x[i] + off;
+    T* e = reinterpret_cast<T*>(tile + toff(RG * qt + i, c));
+    const float f = mode == 0 ? __expf(gl - gc) : scale * __expf(gc);
+    stf(e, ldf(e) * f);
+  }
+  if (qt == 0) G.gl[c] = gl;
+}
 
 // All threads: publish smem operand writes to the tensor core and order them before the MMA.
 __device__ __forceinline__ void operands_ready() {
@@ -414,22 +448,7 @@ __global__ void __launch_bounds__(NT, 2) tc_local_state_kernel(
         next();  // short items: the next item's copies start right away
         unsigned char* sA = smem + st * STAGE;
         unsigned char* sB = sA + TILE;
-        gate_prep<Tg, true>(G, sB + TILE);
-        {
-          uint4* p = reinterpret_cast<uint4*>(sA + me.off);
-          const uint4 u = *p;
-          const T* xs = reinterpret_cast<const T*>(&u);
-          const float* gc = G.E + me.tr * LDG + me.tc;
-          float y[8];
-          if (mode == 0) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * __expf(G.gl[me.tc + i] - gc[i]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = ldf(xs + i) * (scale * __expf(gc[i]));
-          }
-          *p = pack8<T>(y);
-        }
+        gate_apply_local<T, Tg>(G, sB + TILE, sA, mode, scale);
         operands_ready();
         if (tid == 0) {
           mma64(tb, sA, 1, sB, 1, idesc_f16(64, 64, Fmt<T>::v, 1, 1), false);
@@ -509,7 +528,7 @@ __global__ void __launch_bounds__(NT, 1) tc_fwd_o_kernel(
         unsigned char* sH = sV + TILE;
         float hreg[8];
         state_regs(sH, me, hreg);
-        gate_prep<Tg, false>(G, sH + STATE);  // its barriers order the state reads before sH writes
+        gate_prep<Tg>(G, sH + STATE);  // its barriers order the state reads before sH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
         if (exact) {
           if (tid == 0) flags[1 + atomicAdd(flags, 1)] = x.cid * H + x.head;
@@ -631,7 +650,7 @@ __global__ void __launch_bounds__(NT, 1) tc_bwd_kernel(
         float hreg[8], dhreg[8];
         state_regs(sH, me, hreg);
         state_regs(sDH, me, dhreg);
-        gate_prep<Tg, false>(G, sDH + STATE);  // its barriers order the state reads before sH/sDH writes
+        gate_prep<Tg>(G, sDH + STATE);  // its barriers order the state reads before sH/sDH writes
         const bool exact = __uint_as_float(G.span_bits) > kTcSpan;
         if (exact) {
           if (tid == 0) flags[1 + atomicAdd(flags, 1)] = x.cid * H + x.head;
