@@ -102,8 +102,8 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
 // map (prod decay, local sum), segment start values are chained in shared memory, then every
 // segment re-walks its chunks from its start value writing the per-chunk states.  Loads are
 // issued 16 chunks at a time (they do not depend on the running state).
-constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 16;
-__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
+constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 8;
+__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
     const float* __restrict__ init, float* __restrict__ per_chunk, float* __restrict__ fin,
@@ -115,42 +115,58 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
   const int64_t KV = (int64_t)K * V, HKV = (int64_t)H * KV, HK = (int64_t)H * K;
   const int64_t idx = (int64_t)blockIdx.x * SCAN_EL + el;
   const bool valid = idx < N * HKV;
-  int64_t cs = 0, n = 0, ebase = 0, dbase = 0;
+  int64_t len = 0;
+  // pointers to this thread's element of its segment's first chunk; steps between chunks
+  const float* pa = dS;
+  const float* pd = decay;
+  float* po = per_chunk;
+  int64_t sa = 0, sd = 0;
   if (valid) {
     const int64_t seq = idx / HKV;
     const int64_t rem = idx - seq * HKV;
     const int64_t head = rem / KV;
     const int64_t kv = rem - head * KV;
     const int64_t c0 = chunk_off[seq];
-    n = chunk_off[seq + 1] - c0;
-    cs = reverse ? c0 + n - 1 : c0;
-    ebase = head * KV + kv;
-    dbase = head * K + kv / V;
+    const int64_t n = chunk_off[seq + 1] - c0;
+    const int64_t Ls = (n + nseg - 1) / nseg;
+    const int64_t i0 = sg * Ls, i1 = (i0 + Ls < n) ? i0 + Ls : n;
+    len = i1 > i0 ? i1 - i0 : 0;
+    const int64_t dir = reverse ? -1 : 1;
+    const int64_t cfirst = (reverse ? c0 + n - 1 : c0) + dir * i0;
+    const int64_t ebase = head * KV + kv, dbase = head * K + kv / V;
+    if (len > 0) {
+      pa = dS + cfirst * HKV + ebase;
+      pd = decay + cfirst * HK + dbase;
+      po = per_chunk + cfirst * HKV + ebase;
+    }
+    sa = dir * HKV;
+    sd = dir * HK;
   }
-  const int64_t dir = reverse ? -1 : 1;
-  const int64_t Ls = (n + nseg - 1) / nseg;
-  const int64_t i0 = sg * Ls, i1 = (i0 + Ls < n) ? i0 + Ls : n;
+  // 1. compose this segment's affine map x -> A x + B (loads issued SCAN_U chunks at a time)
   float A = 1.f, B = 0.f;
   {
-    int64_t i = i0;
-    for (; i + SCAN_U <= i1; i += SCAN_U) {
+    const float* qa = pa;
+    const float* qd = pd;
+    int64_t i = 0;
+    for (; i + SCAN_U <= len; i += SCAN_U) {
       float d[SCAN_U], a[SCAN_U];
 #pragma unroll
       for (int u = 0; u < SCAN_U; ++u) {
-        const int64_t c = cs + dir * (i + u);
-        d[u] = decay[c * HK + dbase];
-        a[u] = dS[c * HKV + ebase];
+        d[u] = qd[u * sd];
+        a[u] = qa[u * sa];
       }
 #pragma unroll
       for (int u = 0; u < SCAN_U; ++u) { B = fmaf(d[u], B, a[u]); A *= d[u]; }
+      qa += SCAN_U * sa;
+      qd += SCAN_U * sd;
     }
-    for (; i < i1; ++i) {
-      const int64_t c = cs + dir * i;
-      const float d = decay[c * HK + dbase];
-      B = fmaf(d, B, dS[c * HKV + ebase]);
+    for (; i < len; ++i, qa += sa, qd += sd) {
+      const float d = *qd;
+      B = fmaf(d, B, *qa);
       A *= d;
     }
   }
+  // 2. chain the segment start values
   float x;
   if (nseg > 1) {
     sA[sg][el] = A;
@@ -170,26 +186,28 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
     x = (valid && init) ? init[idx] : 0.f;
     if (valid && fin) fin[idx] = fmaf(A, x, B);
   }
-  int64_t i = i0;
-  for (; i + SCAN_U <= i1; i += SCAN_U) {
+  // 3. re-walk from the start value, writing the state at every chunk
+  int64_t i = 0;
+  for (; i + SCAN_U <= len; i += SCAN_U) {
     float d[SCAN_U], a[SCAN_U];
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
-      const int64_t c = cs + dir * (i + u);
-      d[u] = decay[c * HK + dbase];
-      a[u] = dS[c * HKV + ebase];
+      d[u] = pd[u * sd];
+      a[u] = pa[u * sa];
     }
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
-      per_chunk[(cs + dir * (i + u)) * HKV + ebase] = x;
+      po[u * sa] = x;
       x = fmaf(d[u], x, a[u]);
     }
+    pa += SCAN_U * sa;
+    pd += SCAN_U * sd;
+    po += SCAN_U * sa;
   }
-  for (; i < i1; ++i) {
-    const int64_t c = cs + dir * i;
-    const float d = decay[c * HK + dbase];
-    const float a = dS[c * HKV + ebase];
-    per_chunk[c * HKV + ebase] = x;
+  for (; i < len; ++i, pa += sa, pd += sd, po += sa) {
+    const float d = *pd;
+    const float a = *pa;
+    *po = x;
     x = fmaf(d, x, a);
   }
 }
