@@ -103,20 +103,44 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
 // segment re-walks its chunks from its start value writing the per-chunk states.  Loads are
 // issued 16 chunks at a time (they do not depend on the running state).
 constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 8;
+
+// VEC consecutive state elements (one key row, consecutive value columns) per thread.
+template <int VEC> struct SVec;
+template <> struct SVec<1> {
+  using type = float;
+  static __device__ __forceinline__ float ld(const float* p) { return *p; }
+  static __device__ __forceinline__ void st(float* p, float x) { *p = x; }
+  static __device__ __forceinline__ float fma(float d, float x, float a) { return fmaf(d, x, a); }
+  static __device__ __forceinline__ float zero() { return 0.f; }
+};
+template <> struct SVec<4> {
+  using type = float4;
+  static __device__ __forceinline__ float4 ld(const float* p) { return *reinterpret_cast<const float4*>(p); }
+  static __device__ __forceinline__ void st(float* p, float4 x) { *reinterpret_cast<float4*>(p) = x; }
+  static __device__ __forceinline__ float4 fma(float d, float4 x, float4 a) {
+    return make_float4(fmaf(d, x.x, a.x), fmaf(d, x.y, a.y), fmaf(d, x.z, a.z), fmaf(d, x.w, a.w));
+  }
+  static __device__ __forceinline__ float4 zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+
+template <int VEC>
 __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
     const float* __restrict__ init, float* __restrict__ per_chunk, float* __restrict__ fin,
     bool reverse, int nseg) {
-  __shared__ float sA[SCAN_MAXSEG][SCAN_EL], sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
+  using S = SVec<VEC>;
+  using vec = typename S::type;
+  __shared__ float sA[SCAN_MAXSEG][SCAN_EL];
+  __shared__ vec sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
   const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
   griddep_launch_dependents();
   griddep_wait();
   const int64_t KV = (int64_t)K * V, HKV = (int64_t)H * KV, HK = (int64_t)H * K;
-  const int64_t idx = (int64_t)blockIdx.x * SCAN_EL + el;
+  const int64_t idx = ((int64_t)blockIdx.x * SCAN_EL + el) * VEC;  // first element of this thread
   const bool valid = idx < N * HKV;
   int64_t len = 0;
-  // pointers to this thread's element of its segment's first chunk; steps between chunks
+  // pointers to this thread's elements of its segment's first chunk; steps between chunks
   const float* pa = dS;
   const float* pd = decay;
   float* po = per_chunk;
@@ -143,62 +167,65 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     sd = dir * HK;
   }
   // 1. compose this segment's affine map x -> A x + B (loads issued SCAN_U chunks at a time)
-  float A = 1.f, B = 0.f;
+  float A = 1.f;
+  vec B = S::zero();
   {
     const float* qa = pa;
     const float* qd = pd;
     int64_t i = 0;
     for (; i + SCAN_U <= len; i += SCAN_U) {
-      float d[SCAN_U], a[SCAN_U];
+      float d[SCAN_U];
+      vec a[SCAN_U];
 #pragma unroll
       for (int u = 0; u < SCAN_U; ++u) {
         d[u] = qd[u * sd];
-        a[u] = qa[u * sa];
+        a[u] = S::ld(qa + u * sa);
       }
 #pragma unroll
-      for (int u = 0; u < SCAN_U; ++u) { B = fmaf(d[u], B, a[u]); A *= d[u]; }
+      for (int u = 0; u < SCAN_U; ++u) { B = S::fma(d[u], B, a[u]); A *= d[u]; }
       qa += SCAN_U * sa;
       qd += SCAN_U * sd;
     }
     for (; i < len; ++i, qa += sa, qd += sd) {
       const float d = *qd;
-      B = fmaf(d, B, *qa);
+      B = S::fma(d, B, S::ld(qa));
       A *= d;
     }
   }
   // 2. chain the segment start values
-  float x;
+  vec x;
   if (nseg > 1) {
     sA[sg][el] = A;
     sB[sg][el] = B;
     __syncthreads();
     if (sg == 0) {
-      float y = (valid && init) ? init[idx] : 0.f;
+      vec y = (valid && init) ? S::ld(init + idx) : S::zero();
       for (int s2 = 0; s2 < nseg; ++s2) {
         sX[s2][el] = y;
-        y = fmaf(sA[s2][el], y, sB[s2][el]);
+        y = S::fma(sA[s2][el], y, sB[s2][el]);
       }
-      if (valid && fin) fin[idx] = y;
+      if (valid && fin) S::st(fin + idx, y);
     }
     __syncthreads();
     x = sX[sg][el];
   } else {
-    x = (valid && init) ? init[idx] : 0.f;
-    if (valid && fin) fin[idx] = fmaf(A, x, B);
+    x = (valid && init) ? S::ld(init + idx) : S::zero();
+    if (valid && fin) S::st(fin + idx, S::fma(A, x, B));
   }
   // 3. re-walk from the start value, writing the state at every chunk
   int64_t i = 0;
   for (; i + SCAN_U <= len; i += SCAN_U) {
-    float d[SCAN_U], a[SCAN_U];
+    float d[SCAN_U];
+    vec a[SCAN_U];
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
       d[u] = pd[u * sd];
-      a[u] = pa[u * sa];
+      a[u] = S::ld(pa + u * sa);
     }
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
-      po[u * sa] = x;
-      x = fmaf(d[u], x, a[u]);
+      S::st(po + u * sa, x);
+      x = S::fma(d[u], x, a[u]);
     }
     pa += SCAN_U * sa;
     pd += SCAN_U * sd;
@@ -206,9 +233,9 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
   }
   for (; i < len; ++i, pa += sa, pd += sd, po += sa) {
     const float d = *pd;
-    const float a = *pa;
-    *po = x;
-    x = fmaf(d, x, a);
+    const vec a = S::ld(pa);
+    S::st(po, x);
+    x = S::fma(d, x, a);
   }
 }
 
@@ -793,13 +820,21 @@ int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chun
 int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_off, int64_t N,
                       int64_t H, int64_t K, int64_t V, const float* init, float* per_chunk,
                       float* final_state, bool reverse, cudaStream_t s) {
-  const int64_t threads = N * H * K * V;
+  // 4 consecutive value columns per thread when rows split evenly and the state arrays align
+  const bool v4 = V % 4 == 0 && ((uintptr_t)dS | (uintptr_t)per_chunk | (uintptr_t)init | (uintptr_t)final_state) % 16 == 0;
+  const int vec = v4 ? 4 : 1;
+  const int64_t threads = N * H * K * V / vec;
   if (threads == 0) return SSLA_OK;
   // segments per element: enough threads for about one resident wave (148 SMs x 2048)
   int64_t nseg = (int64_t)kNumSMs * 2048 / threads;
   nseg = nseg < 1 ? 1 : (nseg > SCAN_MAXSEG ? SCAN_MAXSEG : nseg);
-  launch_pdl(state_scan_kernel, dim3(ceil_div(threads, SCAN_EL)), dim3(SCAN_EL * (int)nseg), 0, s, dS, decay, chunk_off,
-             N, (int)H, (int)K, (int)V, init, per_chunk, final_state, reverse, (int)nseg);
+  const dim3 grid(ceil_div(threads, SCAN_EL)), block(SCAN_EL * (int)nseg);
+  if (v4)
+    launch_pdl(state_scan_kernel<4>, grid, block, 0, s, dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk,
+               final_state, reverse, (int)nseg);
+  else
+    launch_pdl(state_scan_kernel<1>, grid, block, 0, s, dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk,
+               final_state, reverse, (int)nseg);
   SSLA_CHECK_LAUNCH("chunk_gla state_scan");
   return SSLA_OK;
 }
