@@ -134,16 +134,11 @@ class MosAttention(nn.Module):
         layer."""
         src, pos_id = r["src"], r["pos_id"]
         E, C = residual.shape[0], self.hidden_size
-        ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
-        P = ws.shape[0]
-        wqvg = torch.cat([self.q_proj.weight, self.v_proj.weight, self.g_proj.weight], 0)  # [3C, C]
-        w_all = torch.matmul(wqvg, ws)  # [P, 3C, I]
+        w_all, w_rows, w_back = self._folded_weights()
+        P, Pg = w_all.shape[0], w_back.shape[0] // C
         lengths = r["lengths"]
         cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
         cu[1:] = lengths.cumsum(0)
-        wg = self.gather_conv_weights.reshape(-1, C, C)
-        Pg = wg.shape[0]
-        wgo = torch.matmul(wg, self.o_proj.weight)  # [Pg, C, C]
         rows = src.numel()
         if Pg == 1:
             qh = torch.empty((rows, C), device=residual.device, dtype=torch.float32)
@@ -155,18 +150,38 @@ class MosAttention(nn.Module):
             # projection inside the scan kernel (weights in shared memory): no [E, P*3C] buffer
             _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
         else:
-            y = _mos.matmul_rows(residual, w_all.reshape(P * 3 * C, self.input_size).t())  # rows (e, p) of 3C
+            y = _mos.matmul_rows(residual, w_rows)  # rows (e, p) of 3C
             key = src if P == 1 else src * P + pos_id
             _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
         if Pg == 1:
-            out = _mos.matmul_rows(index_add_rows_ad(qh, src, E), wgo[0].t())
+            out = _mos.matmul_rows(index_add_rows_ad(qh, src, E), w_back)
         else:
-            out = _mos.matmul_rows(qh.view(E, Pg * C), wgo.permute(0, 2, 1).reshape(Pg * C, C))
+            out = _mos.matmul_rows(qh.view(E, Pg * C), w_back)
         if self.input_proj is not None:
             residual = _mos.matmul_rows(residual, self.input_proj.weight.t())
         out = _mos.layernorm_residual(out, residual, self.norm.weight, self.norm.bias, self.norm.eps)
         return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
                 "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}
+
+    def _folded_weights(self):
+        """Folded inference weights: w_all [P, 3C, I] = [Wq; Wv; Wg] Ws_p, its [I, P*3C] GEMM
+        form, and the gather-back operand [Pg*C, C] (row block p = (Wg_p Wo)^T).  Recomputed
+        only when a parameter changed (tensor version counters) or moved."""
+        params = (self.scatter_conv_weights, self.gather_conv_weights, self.q_proj.weight, self.v_proj.weight,
+                  self.g_proj.weight, self.o_proj.weight)
+        key = tuple((p.data_ptr(), p._version) for p in params)
+        cached = getattr(self, "_folded", None)
+        if cached is not None and cached[0] == key:
+            return cached[1], cached[2], cached[3]
+        C = self.hidden_size
+        ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
+        wqvg = torch.cat([self.q_proj.weight, self.v_proj.weight, self.g_proj.weight], 0)  # [3C, C]
+        w_all = torch.matmul(wqvg, ws).contiguous()
+        wgo = torch.matmul(self.gather_conv_weights.reshape(-1, C, C), self.o_proj.weight)  # [Pg, C, C]
+        w_rows = w_all.reshape(-1, self.input_size).t().contiguous()
+        w_back = wgo.permute(0, 2, 1).reshape(-1, C).contiguous()
+        self._folded = (key, w_all, w_rows, w_back)
+        return w_all, w_rows, w_back
 
     def _apply_scatter_proj(self, x, pos_id):
         w = self.scatter_conv_weights.reshape(-1, self.hidden_size, self.input_size)

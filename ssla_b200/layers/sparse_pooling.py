@@ -2,8 +2,9 @@
 timestamp are merged by max or mean.
 
 The merge is a segment reduction over rows that are already grouped: after the receptive-field
-gather, rows are ordered by (field, time), so the unique (field, time) keys give non-decreasing
-segment ids and the reduction runs on ``ssla_segment_reduce`` with offsets from
+gather, rows are ordered by (field, time), so a segment opens at every field start and every
+change of time, the running count of openings is a non-decreasing segment id, and the reduction
+runs on ``ssla_segment_reduce`` with offsets from
 ``ssla_segment_offsets_sorted`` — no sort, no atomics, bit-exact against the CPU reduction
 (the reference calls torch_scatter.scatter_max / scatter_mean, layers/sparse_pooling.py:33).
 """
@@ -29,18 +30,24 @@ class SparsePool(AsyncSparseModule):
         time = inputs["time"]
         events = inputs["events"]
         dev = time.device
-        n_rf = lengths.shape[0]
-        rf = torch.repeat_interleave(torch.arange(n_rf, device=dev), lengths)
-        max_v = time.max() + 1 if time.numel() else torch.tensor(1, device=dev)
-        key = time + rf * max_v
-        ukey, inverse, counts = torch.unique_consecutive(key, return_inverse=True, return_counts=True)
-        S = ukey.numel()
-        off = torch.zeros(S + 1, dtype=torch.int64, device=dev)
-        off[1:] = counts.cumsum(0)
-        new_events = _seg.segment_reduce_ad(events, inverse, off, None, self.op)
-        u_rf = ukey // max_v
-        new_time = ukey - u_rf * max_v
-        new_lengths = torch.bincount(u_rf, minlength=n_rf).to(lengths.dtype)
+        N = time.numel()
+        # A row opens a segment where its time differs from the previous row's or where a
+        # receptive field starts; segment ids are the running count of openings.
+        ends = torch.cumsum(lengths.to(torch.int64), 0)
+        starts = ends - lengths
+        opens = torch.zeros(N + 1, dtype=torch.bool, device=dev)
+        opens.index_fill_(0, starts, True)  # empty fields mark the next start (or the sentinel)
+        opens = opens[:N]
+        if N:
+            opens[1:] |= time[1:] != time[:-1]
+        cnt = torch.zeros(N + 1, dtype=torch.int64, device=dev)
+        torch.cumsum(opens, 0, out=cnt[1:])
+        seg = cnt[1:] - 1
+        S = int(cnt[-1])  # the one host read of the layer: output size
+        off = _seg.segment_offsets_sorted(seg, S)
+        new_events = _seg.segment_reduce_ad(events, seg, off, None, self.op)
+        new_time = time[off[:-1]]
+        new_lengths = (cnt[ends] - cnt[starts]).to(lengths.dtype)
         return {"events": new_events, "time": new_time, "lengths": new_lengths, "batch_id": inputs["batch_id"],
                 "h": inputs["h"], "w": inputs["w"], "batch_size": inputs["batch_size"]}
 

@@ -22,9 +22,11 @@ class TemporalDropout(AsyncSparseModule):
         with torch.no_grad():
             start = torch.cumsum(lengths, 0) - lengths
             keep_n = torch.div(lengths + (w - 1), w, rounding_mode="floor")
-            seq = torch.repeat_interleave(torch.arange(lengths.numel(), device=dev), keep_n)
-            kstart = torch.cumsum(keep_n, 0) - keep_n
-            j = torch.arange(int(keep_n.sum()), device=dev) - kstart[seq]
+            kend = torch.cumsum(keep_n, 0)
+            total = int(kend[-1]) if kend.numel() else 0  # the one host read: output size
+            seq = torch.repeat_interleave(torch.arange(lengths.numel(), device=dev), keep_n, output_size=total)
+            kstart = kend - keep_n
+            j = torch.arange(total, device=dev) - kstart[seq]
             first = torch.remainder(lengths - 1, w)  # offset of the first kept event
             idx = start[seq] + first[seq] + j * w
         return {"events": inputs["events"][idx], "time": inputs["time"][idx], "lengths": keep_n,

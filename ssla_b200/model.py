@@ -20,7 +20,7 @@ from .layers import (LinearAttention, MosAttention, SparseAdaptiveAvgPool, Spars
                      SparseMaxPool, TemporalDropout)
 from . import _lib
 from .ops import segment as _seg
-from .utils.farsecnn_utils import group_events, truncate_packed_sequence
+from .utils.farsecnn_utils import group_events
 
 FRAME_SIZES = {"Gen1": ((240, 304), 2), "NCaltech101": ((180, 240), 101)}
 
@@ -75,10 +75,13 @@ def get_modulelist(config_layers, sensor_size, in_channels, expected_strides):
 def preprocess_inputs(events: torch.Tensor, lengths: torch.Tensor, frame_size, hot_pixel_thres: int = 50):
     """<x, y, t, p> events -> pixel groups with per-event features <dt, p> (model_mos.py:173-209):
     dt = time since the previous event of the pixel / 1e5, clamped to 1, 1 for the first event;
-    with hot_pixel_thres > 0 only the first `hot_pixel_thres` events of a pixel are kept."""
+    with hot_pixel_thres > 0 only the first `hot_pixel_thres` events of a pixel are kept (the
+    reference truncates after computing dt; a pixel's kept events are a prefix of its grouped
+    events, so truncating during the grouping gives the same dt)."""
     with torch.no_grad():
         x = torch.cat([events[..., :3], events[..., 2:3], events[..., 3:]], dim=-1)
-        grouped = group_events((x, lengths), frame_size)
+        grouped = group_events((x, lengths), frame_size,
+                               keep_first=hot_pixel_thres if hot_pixel_thres > 0 else None)
         feats = grouped["events"].clone()
         t = feats[:, 0]
         dt = torch.empty_like(t)
@@ -91,9 +94,6 @@ def preprocess_inputs(events: torch.Tensor, lengths: torch.Tensor, frame_size, h
         dt[first] = 1
         feats[:, 0] = dt
         grouped["events"] = feats
-        if hot_pixel_thres > 0:
-            grouped["events"], grouped["lengths"], grouped["time"] = truncate_packed_sequence(
-                grouped["events"], grouped["lengths"], threshold=hot_pixel_thres, others=grouped["time"])
     return grouped
 
 

@@ -6,7 +6,7 @@ import math
 import torch
 
 from ..ops import segment as _seg
-from .routing import compute_padding_1d, group_events, receptive_field_lut, replicate_to_fields, truncate_packed_sequence
+from .routing import _geometry, compute_padding_1d, group_events, receptive_field_lut, replicate_to_fields, truncate_packed_sequence
 
 __all__ = ["compute_padding_1d", "compute_output_size_1d", "compute_rf2pixels", "group_events",
            "gather_receptive_fields", "truncate_packed_sequence"]
@@ -32,7 +32,7 @@ def gather_receptive_fields(inputs, frame_size, rf2pixel_lut, rf_outcoord, kerne
         kernel_size = (k, k)
     if stride is None:
         stride = kernel_size
-    ow = int(rf_outcoord[:, 0].max()) + 1
+    ow = _geometry(frame_size, kernel_size, stride)[-1]
     r = replicate_to_fields(inputs["batch_id"], inputs["h"], inputs["w"], inputs["lengths"], inputs["time"],
                             frame_size, kernel_size, stride, batch_size=inputs.get("batch_size"))
     fid = r["field_id"]

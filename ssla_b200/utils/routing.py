@@ -61,44 +61,65 @@ def receptive_field_lut(frame_size, kernel_size, stride) -> Tuple[torch.Tensor, 
     return lut.to(torch.int64), outcoord.reshape(oh * ow, 2).to(torch.int64)
 
 
-def group_events(inputs, frame_size, max_events_per_px: int = 512) -> Dict[str, torch.Tensor]:
+def group_events(inputs, frame_size, max_events_per_px: int = 512, keep_first=None) -> Dict[str, torch.Tensor]:
     """Group events [B, N, C] (rows <x, y, t, features...>, per-sample lengths) by pixel
     (utils/farsecnn_utils.py:130-174, utils/async_utils.py:10-84): stable order by
-    (sample, pixel), at most the last `max_events_per_px` events of a pixel kept."""
+    (sample, pixel), at most the last `max_events_per_px` events of a pixel kept.  With
+    ``keep_first`` only the first ``keep_first`` of those are kept, which is the grouping
+    followed by ``truncate_packed_sequence`` (model_mos.py:173-209) in one pass.
+
+    Works on the padded [B * N] rows directly (padding sorts after every pixel) and reads the
+    device once, for the group and kept-event counts."""
     events, lengths = inputs
     events = events.float()
-    B, Nmax = events.shape[0], events.shape[1]
+    B, Nmax, C = events.shape
     H, W = int(frame_size[0]), int(frame_size[1])
     dev = events.device
-    lengths = lengths.to(dev)
-    mask = torch.arange(Nmax, device=dev).unsqueeze(0) < lengths.unsqueeze(1)
-    ev = events[mask]
-    batch_id = torch.arange(B, device=dev).repeat_interleave(lengths.to(torch.int64))
-    pid = batch_id * (H * W) + ev[:, 1].to(torch.int64) * W + ev[:, 0].to(torch.int64)
+    lengths = lengths.to(dev).to(torch.int64)
+    N = B * Nmax
+    rows = events.reshape(N, C)
+    row = torch.arange(N, device=dev)
+    valid = (torch.arange(Nmax, device=dev).unsqueeze(0) < lengths.unsqueeze(1)).reshape(N)
+    batch_of_row = row // max(Nmax, 1)
+    pid = batch_of_row * (H * W) + rows[:, 1].to(torch.int64) * W + rows[:, 0].to(torch.int64)
+    pid = torch.where(valid, pid, B * H * W)
     order = torch.sort(pid, stable=True)[1]
     spid = pid[order]
-    _, gid, counts = torch.unique_consecutive(spid, return_inverse=True, return_counts=True)
-    ev = ev[order]
-    G = counts.numel()
-    first = torch.zeros(G, dtype=torch.int64, device=dev)
-    if G:
-        first[1:] = counts.cumsum(0)[:-1]
-    gr_lengths = counts.clamp(max=max_events_per_px)
-    skip = counts - gr_lengths
-    keep = torch.arange(int(gr_lengths.sum()), device=dev)
-    start_new = torch.zeros(G, dtype=torch.int64, device=dev)
-    if G:
-        start_new[1:] = gr_lengths.cumsum(0)[:-1]
-    grp = torch.repeat_interleave(torch.arange(G, device=dev), gr_lengths)
-    src = keep - start_new[grp] + first[grp] + skip[grp]
-    rep = first  # one representative event per group
-    kept = ev[src]
+    svalid = valid[order]  # valid rows first
+    bound = torch.ones(N, dtype=torch.bool, device=dev)  # a group (or the padding) starts here
+    if N:
+        bound[1:] = spid[1:] != spid[:-1]
+    opens = bound & svalid
+    # start row of every group (the padding counts as one): a scatter to the running count of
+    # boundaries; slots past the last group hold N, slot N + 1 takes the non-boundary rows
+    gidx = torch.cumsum(bound, 0) - 1
+    bstart = torch.full((N + 2,), N, dtype=torch.int64, device=dev)
+    bstart.scatter_(0, torch.where(bound, gidx, N + 1), row)
+    gstart = bstart[gidx]
+    gend = bstart[gidx + 1]
+    cnt = gend - gstart
+    rank = row - gstart
+    skip = cnt - cnt.clamp(max=max_events_per_px)
+    keep = svalid & (rank >= skip)
+    if keep_first is not None:
+        keep &= rank - skip < keep_first
+    n_kept = torch.cumsum(keep, 0)
+    G, K = (torch.stack([opens.sum(), n_kept[-1]]).tolist() if N else (0, 0))
+    first = bstart[:G]  # valid groups precede the padding
+    kept_row = torch.empty(K + 1, dtype=torch.int64, device=dev)
+    kept_row.scatter_(0, torch.where(keep, n_kept - 1, K), row)
+    kept_row = kept_row[:K]
+    gr_lengths = cnt[first].clamp(max=max_events_per_px)
+    if keep_first is not None:
+        gr_lengths = gr_lengths.clamp(max=keep_first)
+    kept = rows[order[kept_row]]
+    rep = rows[order[first]]
     return {
         "events": kept[:, 3:],
         "time": kept[:, 2].to(torch.int64),
-        "batch_id": batch_id[order][rep],
-        "h": ev[rep, 1].to(torch.int64),
-        "w": ev[rep, 0].to(torch.int64),
+        "batch_id": batch_of_row[order[first]],
+        "h": rep[:, 1].to(torch.int64),
+        "w": rep[:, 0].to(torch.int64),
         "lengths": gr_lengths,
         "batch_size": B,
     }
@@ -137,13 +158,21 @@ def _replicate_gpu(gr_batch_id, gr_h, gr_w, gr_lengths, gr_time, geo, batch_size
     flen = torch.empty(max(B * oh * ow, 1), dtype=torch.int64, device=dev)
     _lib.check(L.ssla_route_field_lengths(pmap.data_ptr(), glen.data_ptr(), B, H, W, kh, kw, sh, sw, pt, pl, oh, ow,
                                           flen.data_ptr(), st), "route_field_lengths")
-    field_ids = torch.nonzero(flen[:B * oh * ow]).squeeze(1)
-    lengths = flen[field_ids]
-    off = torch.zeros(field_ids.numel() + 1, dtype=torch.int64, device=dev)
-    torch.cumsum(lengths, 0, out=off[1:])
-    bad_coord, unsorted, n_ev = torch.cat([flags.to(torch.int64), off[-1:]]).tolist()
+    # non-empty fields in ascending id order, compacted by a scatter to their running count
+    # (the one host read of the routing: flags, field count and event count together)
+    nf_all = B * oh * ow
+    nonempty = flen[:nf_all] > 0
+    rank = torch.cumsum(nonempty, 0)
+    stats = torch.cat([flags.to(torch.int64), rank[-1:] if nf_all else rank.new_zeros(1), flen[:nf_all].sum().view(1)])
+    bad_coord, unsorted, F, n_ev = stats.tolist()
     if bad_coord or unsorted:
         return None
+    field_ids = torch.empty(F + 1, dtype=torch.int64, device=dev)
+    field_ids.scatter_(0, torch.where(nonempty, rank - 1, F), torch.arange(nf_all, device=dev))
+    field_ids = field_ids[:F]
+    lengths = flen[field_ids]
+    off = torch.zeros(F + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(lengths, 0, out=off[1:])
     src = torch.empty(n_ev, dtype=torch.int64, device=dev)
     pos = torch.empty(n_ev, dtype=torch.int64, device=dev)
     t = torch.empty(n_ev, dtype=torch.int64, device=dev)
