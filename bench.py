@@ -391,6 +391,60 @@ def run_other(args):
                              "frac": k2["frac"], "peak_source": which, "alg_bytes_per_step": k2["alg_bytes_per_step"],
                              "traffic": None},
                 "gpu_launches": 4 * args.steps, "cpu_baseline": cpu}), flush=True)
+    elif args.workload == "events":
+        import numpy as np
+
+        from ssla_b200.synthetic import dat_recording
+        from ssla_b200.utils.io import EventStore
+
+        # 8 resident 60 s recordings of 20M events (Gen1-like rate), 64 labels per batch, 100 ms
+        # windows (configs/train_cfg_gen1_s.yaml:12): ranges kernel, one host read, decode kernel
+        R_EV, DUR, B, WIN = 20_000_000, 60_000_000, 64, 100_000
+        recs = [dat_recording(100 * rank + i, R_EV, DUR) for i in range(8)]
+        store = EventStore(dev, capacity_events=8 * R_EV)
+        ids = [store.add(w) for w in recs]
+        rs = np.random.default_rng(rank)
+        batches = [([ids[int(i)] for i in rs.integers(0, 8, B)], [int(v) for v in rs.integers(WIN, DUR, B)])
+                   for _ in range(max(args.steps, 1))]
+        it = [0]
+        rows = [0]
+
+        def step():
+            ri, ts = batches[it[0] % len(batches)]
+            ev, lens = store.windows(ri, ts, WIN)
+            rows[0] += ev.shape[0] * ev.shape[1]
+            it[0] += 1
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        rows[0] = 0
+        it[0] = 0
+        with Clocks(local) as clk:
+            secs = _max_over_ranks(_event_time(step, args.steps, stream), dist, dev)
+        # events delivered (rows of the padded batch, padding included, as the collation writes)
+        alg = rows[0] * (8 + 16) / args.steps
+        if rank == 0:
+            cpu = None
+            if not args.no_cpu_baseline and world == 1:
+                from oracle import events_io as oev
+
+                ri, ts = batches[0]
+                t0 = time.perf_counter()
+                ev_c, _ = oev.gen1_batch([recs[i] for i in ri[:16]], ts[:16], WIN)
+                cpu = {"value": ev_c.shape[0] * ev_c.shape[1] / (time.perf_counter() - t0), "unit": "events/s",
+                       "cores": 1, "kind": "port", "sample": "16 of the 64 windows of one batch (numpy)"}
+            gbs = alg * args.steps / secs / 1e9
+            print(json.dumps({
+                "metric": "Gen1 batch assembly events/s (window search + decode + collation)",
+                "value": world * rows[0] / secs, "unit": "events/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u32->f32", "data": "synthetic",
+                "config": {"workload": "8 resident recordings x 20M events / 60 s, batch of 64 labels, 100 ms windows",
+                           "l2": "1.28 GB of resident payload > L2; windows drawn at random"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                             "peak_source": which, "alg_bytes_per_step": alg, "traffic": None},
+                "gpu_launches": 2 * args.steps, "cpu_baseline": cpu, "clocks": clk.summary()}), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
@@ -402,7 +456,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="chunk", choices=["chunk", "recurrent", "pool", "model"],
+    ap.add_argument("--workload", default="chunk", choices=["chunk", "recurrent", "pool", "model", "events"],
                     help="chunk: headline (BASELINE config 2); recurrent: config 3; pool: config 4; "
                          "model: config 5 frames/s")
     ap.add_argument("--no-model", action="store_true", help="skip the SSLA-S frames/s field of the headline")

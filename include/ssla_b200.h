@@ -219,6 +219,23 @@ int ssla_batched_nms(const float* boxes, const float* scores, int64_t B, int64_t
                      float conf, float iou_thr, int64_t max_det, int64_t* keep, int64_t* count,
                      void* workspace, size_t workspace_bytes, ssla_stream_t stream);
 
+/* ---------------------------------------------------------------- event-stream input
+ * Prophesee .dat (Event2D) payloads resident in device memory: `words` holds events as pairs of
+ * 32-bit words (t, packed x | y << 14 | p << 28; utils/io/dat_events_tools.py:14, :40-44);
+ * recording b of a batch starts at event rec_start[b] and has rec_count[b] events.
+ * ssla_dat_window_ranges replaces PSEELoader.seek_time(t_end - window) followed by
+ * load_delta_t(window + 1) (utils/io/psee_loader.py:109-219, as called by
+ * dataset/gen1.py:190-193): range [B, 2] gets each sample's [begin, end) event range (relative
+ * to rec_start), lengths [B] its size.  term_criterion is seek_time's bisection stop (100000).
+ * ssla_dat_decode_windows replaces the Gen1 collation (model_base.py:82-117): out [B, Nmax, 4]
+ * fp32 rows <x, y, t, 2p - 1>, rows past a sample's length (0, 0, 0, -1).  words 8-byte and
+ * out 16-byte aligned. */
+int ssla_dat_window_ranges(const uint32_t* words, const int64_t* rec_start, const int64_t* rec_count,
+                           const int64_t* t_end, int64_t B, int64_t window, int64_t term_criterion,
+                           int64_t* range, int64_t* lengths, ssla_stream_t stream);
+int ssla_dat_decode_windows(const uint32_t* words, const int64_t* rec_start, const int64_t* range,
+                            int64_t B, int64_t Nmax, float* out, ssla_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

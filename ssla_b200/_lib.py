@@ -58,6 +58,8 @@ SIGNATURES = {
     "ssla_rows_matmul_smem_bytes": (sz, [i64, i64]),
     "ssla_batched_nms_workspace_bytes": (sz, [i64]),
     "ssla_batched_nms": (i32, [p, p, i64, i64, i32, f32, f32, i64, p, p, p, sz, p]),
+    "ssla_dat_window_ranges": (i32, [p, p, p, p, i64, i64, i64, p, p, p]),
+    "ssla_dat_decode_windows": (i32, [p, p, p, i64, i64, p, p]),
     "ssla_rows_matmul_f32": (i32, [p, i64, i64, i64, p, i64, p, i64, p]),
 }
 

@@ -103,3 +103,18 @@ def seeded_parameters(model: torch.nn.Module, seed: int) -> None:
                 fan_in = p[0].numel() if p.dim() > 1 else p.numel()
                 x *= fan_in ** -0.5
             p.copy_(x.to(p.dtype))
+
+
+def dat_recording(seed: int, events: int, duration_us: int, frame=(240, 304)):
+    """Seeded Event2D payload words (uint32 [2 * events]: t, x | y << 14 | p << 28) of a
+    recording with `events` events, timestamps uniform in [0, duration_us) and sorted (equal
+    timestamps occur when events > duration_us / few), uniform pixels and polarities."""
+    import numpy as np
+
+    g = torch.Generator().manual_seed(seed)
+    t = torch.sort(torch.randint(0, max(int(duration_us), 1), (events,), generator=g))[0]
+    x = torch.randint(0, frame[1], (events,), generator=g)
+    y = torch.randint(0, frame[0], (events,), generator=g)
+    p = torch.randint(0, 2, (events,), generator=g)
+    words = torch.stack([t, x | (y << 14) | (p << 28)], 1).reshape(-1)
+    return words.numpy().astype(np.uint32)
