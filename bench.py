@@ -645,6 +645,7 @@ def main():
                 "schedule": "chunk_gla + autograd from pinned host buffers; step i+1's upload and step i-1's "
                             "download on two copy streams overlap step i's compute; L2 flushed before the run"},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "wait_timeouts": _lib.tc_wait_timeouts(),
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "ssla_s": model_line,

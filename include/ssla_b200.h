@@ -236,6 +236,22 @@ int ssla_dat_window_ranges(const uint32_t* words, const int64_t* rec_start, cons
 int ssla_dat_decode_windows(const uint32_t* words, const int64_t* rec_start, const int64_t* range,
                             int64_t B, int64_t Nmax, float* out, ssla_stream_t stream);
 
+/* ---------------------------------------------------------------- fp32 GEMM on tensor cores
+ * C[M, N] = A[M, K] * B[N, K]^T in fp32 by split TF32 (A B^T ~ Ahi Bhi^T + Ahi Blo^T + Alo Bhi^T,
+ * hi = TF32 rounding, lo = remainder; relative error near 2^-21 per product), for the MoS
+ * layers' per-position projections (layers/mos_attention.py:148-167, fp32 F.linear there).
+ * B is given pre-split (ssla_split_tf32 of the fp32 weights, same [N, ldb] layout).  A, B_hi,
+ * B_lo 16-byte aligned with lda, ldb multiples of 4; *err (device int) is set to 1 if a
+ * pipeline wait timed out. */
+int ssla_split_tf32(const float* x, int64_t n, float* hi, float* lo, ssla_stream_t stream);
+int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* B_hi, const float* B_lo,
+                     int64_t N, int64_t ldb, float* C, int64_t ldc, int* err, ssla_stream_t stream);
+
+/* Number of bounded shared-memory barrier waits in the tensor-core chunk kernels that gave up
+ * since the last reset (synchronous device read; 0 in a healthy run).  A nonzero count marks
+ * the results of the launches since the reset as untrustworthy. */
+int ssla_chunk_gla_tc_timeouts(int reset, unsigned* count);
+
 #ifdef __cplusplus
 }
 #endif

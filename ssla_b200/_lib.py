@@ -60,6 +60,9 @@ SIGNATURES = {
     "ssla_batched_nms": (i32, [p, p, i64, i64, i32, f32, f32, i64, p, p, p, sz, p]),
     "ssla_dat_window_ranges": (i32, [p, p, p, p, i64, i64, i64, p, p, p]),
     "ssla_dat_decode_windows": (i32, [p, p, p, i64, i64, p, p]),
+    "ssla_split_tf32": (i32, [p, i64, p, p, p]),
+    "ssla_chunk_gla_tc_timeouts": (i32, [i32, p]),
+    "ssla_gemm_f32_tc": (i32, [p, i64, i64, i64, p, p, i64, i64, p, i64, p, p]),
     "ssla_rows_matmul_f32": (i32, [p, i64, i64, i64, p, i64, p, i64, p]),
 }
 
@@ -116,3 +119,11 @@ def require_cuda(*ts, what: str = "ssla_b200") -> None:
     for t in ts:
         if t is not None and not t.is_cuda:
             raise RuntimeError(f"{what}: tensors must be on a CUDA device (no CPU path)")
+
+
+def tc_wait_timeouts(reset: bool = True) -> int:
+    """Bounded barrier waits of the tensor-core chunk kernels that gave up since the last reset
+    (a device read; 0 in a healthy run)."""
+    n = C.c_uint(0)
+    check(load().ssla_chunk_gla_tc_timeouts(1 if reset else 0, C.addressof(n)), "chunk_gla_tc_timeouts")
+    return int(n.value)

@@ -31,6 +31,7 @@
 
 #include "chunk_gla.cuh"
 #include "tc_util.cuh"
+#include "tma_map.cuh"
 
 namespace ssla {
 namespace chunk {
@@ -261,8 +262,16 @@ __device__ __forceinline__ void operands_ready() {
   fence_after();
 }
 
+// Bounded waits that give up are counted here (read and reset by ssla_chunk_gla_tc_timeouts);
+// a nonzero count means results of that launch are not to be trusted.
+__device__ unsigned int g_wait_timeouts = 0;
+
+__device__ __forceinline__ void counted_wait(uint64_t* mbar, uint32_t parity) {
+  if (!mbar_wait(mbar, parity)) atomicAdd(&g_wait_timeouts, 1u);
+}
+
 __device__ __forceinline__ void wait_mma(uint64_t* mbar, uint32_t& phase) {
-  mbar_wait(mbar, phase);
+  counted_wait(mbar, phase);
   phase ^= 1u;
   fence_after();
 }
@@ -382,7 +391,7 @@ __device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* 
       if (!issued && nhave && w0) issue(nxt, (i + 1) & 1);
       issued = true;
     };
-    mbar_wait(&full[i & 1], (i >> 1) & 1);
+    counted_wait(&full[i & 1], (i >> 1) & 1);
     if (cur.len < BT) {
       zero(cur, i & 1);
       __syncthreads();
@@ -834,37 +843,9 @@ int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned
 }
 
 // ---------------------------------------------------------------------------- tensor maps
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static EncodeTiled fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<EncodeTiled>(p);
-  }();
-  return fn;
-}
-
 int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
-  const EncodeTiled enc = encode_fn();
-  if (!enc) {
-    set_error("chunk_gla: cuTensorMapEncodeTiled is unavailable");
-    return SSLA_ERR_CUDA;
-  }
-  const cuuint32_t es[3] = {1u, 1u, 1u};
-  const CUresult r = enc(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("chunk_gla: cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return SSLA_ERR_CUDA;
-  }
-  return SSLA_OK;
+  return tma::encode(m, dt, rank, base, dims, strides, box, sw, "chunk_gla");
 }
 
 // 3-D view (D = 64, H, T) of a [T, H, 64] token array, box 64 x 1 x 64: 16-bit operands with
@@ -998,5 +979,22 @@ int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, 
   });
 }
 
+int tc_timeouts(int reset, unsigned* count) {
+  if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned)) != cudaSuccess) {
+    set_error("chunk_gla: cannot read the wait-timeout counter");
+    return SSLA_ERR_CUDA;
+  }
+  if (reset) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(unsigned)) != cudaSuccess) {
+      set_error("chunk_gla: cannot reset the wait-timeout counter");
+      return SSLA_ERR_CUDA;
+    }
+  }
+  return SSLA_OK;
+}
+
 }  // namespace chunk
 }  // namespace ssla
+
+extern "C" int ssla_chunk_gla_tc_timeouts(int reset, unsigned* count) { return ssla::chunk::tc_timeouts(reset, count); }

@@ -13,7 +13,8 @@ patch, so
     has no patch) with the concatenated weights.
 The reference does 9 boolean-masked F.linear calls per projection and an atomics-based
 index_add_ (layers/mos_attention.py:148-167, utils/async_utils.py:262-263).  GPU work:
-routing (ssla_b200.utils.routing), GEMMs (cuBLAS), the scan (``ssla_scan_fwd/bwd``) and row
+routing (ssla_b200.utils.routing), GEMMs (cuBLAS; in the inference path the split-TF32
+tensor-core GEMM of ``csrc/gemm_tf32.cu``), the scan (``ssla_scan_fwd/bwd``) and row
 gathers (``ssla_gather_rows``)."""
 from __future__ import annotations
 
@@ -134,8 +135,8 @@ class MosAttention(nn.Module):
         layer."""
         src, pos_id = r["src"], r["pos_id"]
         E, C = residual.shape[0], self.hidden_size
-        w_all, w_rows, w_back = self._folded_weights()
-        P, Pg = w_all.shape[0], w_back.shape[0] // C
+        w_all, g_rows, g_back, g_in = self._folded_weights()
+        P, Pg = w_all.shape[0], g_back.K // C
         lengths = r["lengths"]
         cu = torch.zeros(lengths.numel() + 1, dtype=torch.int64, device=lengths.device)
         cu[1:] = lengths.cumsum(0)
@@ -150,38 +151,41 @@ class MosAttention(nn.Module):
             # projection inside the scan kernel (weights in shared memory): no [E, P*3C] buffer
             _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
         else:
-            y = _mos.matmul_rows(residual, w_rows)  # rows (e, p) of 3C
+            y = g_rows(residual)  # rows (e, p) of 3C
             key = src if P == 1 else src * P + pos_id
             _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
         if Pg == 1:
-            out = _mos.matmul_rows(index_add_rows_ad(qh, src, E), w_back)
+            out = g_back(index_add_rows_ad(qh, src, E))
         else:
-            out = _mos.matmul_rows(qh.view(E, Pg * C), w_back)
+            out = g_back(qh.view(E, Pg * C))
         if self.input_proj is not None:
-            residual = _mos.matmul_rows(residual, self.input_proj.weight.t())
+            residual = g_in(residual)
         out = _mos.layernorm_residual(out, residual, self.norm.weight, self.norm.bias, self.norm.eps)
         return {"events": out, "time": inputs["time"], "w": inputs["w"], "h": inputs["h"],
                 "batch_id": inputs["batch_id"], "lengths": inputs["lengths"], "batch_size": inputs["batch_size"]}
 
     def _folded_weights(self):
-        """Folded inference weights: w_all [P, 3C, I] = [Wq; Wv; Wg] Ws_p, its [I, P*3C] GEMM
-        form, and the gather-back operand [Pg*C, C] (row block p = (Wg_p Wo)^T).  Recomputed
-        only when a parameter changed (tensor version counters) or moved."""
+        """Folded inference weights: w_all [P, 3C, I] = [Wq; Wv; Wg] Ws_p, and as GEMM operands
+        (``RowsGemm``) its [I, P*3C] form, the gather-back operand [Pg*C, C] (row block p =
+        (Wg_p Wo)^T) and the input projection (None without one).  Recomputed only when a
+        parameter changed (tensor version counters) or moved."""
         params = (self.scatter_conv_weights, self.gather_conv_weights, self.q_proj.weight, self.v_proj.weight,
-                  self.g_proj.weight, self.o_proj.weight)
+                  self.g_proj.weight, self.o_proj.weight) + (
+                      (self.input_proj.weight,) if self.input_proj is not None else ())
         key = tuple((p.data_ptr(), p._version) for p in params)
         cached = getattr(self, "_folded", None)
         if cached is not None and cached[0] == key:
-            return cached[1], cached[2], cached[3]
+            return cached[1:]
         C = self.hidden_size
         ws = self.scatter_conv_weights.reshape(-1, C, self.input_size)
         wqvg = torch.cat([self.q_proj.weight, self.v_proj.weight, self.g_proj.weight], 0)  # [3C, C]
         w_all = torch.matmul(wqvg, ws).contiguous()
         wgo = torch.matmul(self.gather_conv_weights.reshape(-1, C, C), self.o_proj.weight)  # [Pg, C, C]
-        w_rows = w_all.reshape(-1, self.input_size).t().contiguous()
-        w_back = wgo.permute(0, 2, 1).reshape(-1, C).contiguous()
-        self._folded = (key, w_all, w_rows, w_back)
-        return w_all, w_rows, w_back
+        g_rows = _mos.RowsGemm(w_all.reshape(-1, self.input_size).t())
+        g_back = _mos.RowsGemm(wgo.permute(0, 2, 1).reshape(-1, C))
+        g_in = _mos.RowsGemm(self.input_proj.weight.t()) if self.input_proj is not None else None
+        self._folded = (key, w_all, g_rows, g_back, g_in)
+        return w_all, g_rows, g_back, g_in
 
     def _apply_scatter_proj(self, x, pos_id):
         w = self.scatter_conv_weights.reshape(-1, self.hidden_size, self.input_size)

@@ -100,3 +100,80 @@ def layernorm_residual(x: torch.Tensor, r: Optional[torch.Tensor], weight: torch
         x.data_ptr(), 0 if r is None else r.data_ptr(), weight.contiguous().data_ptr(), bias.contiguous().data_ptr(),
         x.numel() // max(C, 1), C, float(eps), out.data_ptr(), _lib.stream_of(x)), "layernorm_residual")
     return out
+
+
+def split_tf32(w: torch.Tensor):
+    """(hi, lo) with hi = w rounded to TF32 and lo = w - hi, both fp32 like ``w`` (contiguous):
+    the pre-split right-hand operand of ``matmul_tc``."""
+    _lib.require_cuda(w, what="split_tf32")
+    w = w.contiguous().float()
+    hi, lo = torch.empty_like(w), torch.empty_like(w)
+    _lib.check(_lib.load().ssla_split_tf32(w.data_ptr(), w.numel(), hi.data_ptr(), lo.data_ptr(), _lib.stream_of(w)),
+               "split_tf32")
+    return hi, lo
+
+
+_ERR = {}
+
+
+def _dev_index(dev) -> int:
+    dev = torch.device(dev)
+    return dev.index if dev.index is not None else torch.cuda.current_device()
+
+
+def _err_flag(dev) -> torch.Tensor:
+    i = _dev_index(dev)
+    f = _ERR.get(i)
+    if f is None:
+        f = _ERR[i] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", i))
+    return f
+
+
+def tc_gemm_ok(a: torch.Tensor, k: int) -> bool:
+    """Whether ``matmul_tc`` takes ``a`` (fp32 rows, 16-byte aligned, K a multiple of 4)."""
+    return (a.dtype == torch.float32 and a.dim() == 2 and a.stride(1) == 1 and a.stride(0) % 4 == 0
+            and a.data_ptr() % 16 == 0 and k % 4 == 0 and a.shape[1] == k)
+
+
+def matmul_tc(a: torch.Tensor, bt_split) -> torch.Tensor:
+    """a [M, K] @ B^T in fp32 on the tensor cores (split TF32), B given as ``split_tf32`` of
+    B [N, K].  The device error flag of the kernel's bounded waits is checked lazily by
+    ``check_tc_errors``."""
+    bh, bl = bt_split
+    _lib.require_cuda(a, bh, bl, what="matmul_tc")
+    M, K = a.shape
+    N = bh.shape[0]
+    if not tc_gemm_ok(a, K) or bh.shape[1] != K:
+        raise ValueError("matmul_tc: a must be fp32 [M, K] with 16-byte aligned rows, K % 4 == 0, B [N, K]")
+    out = torch.empty((M, N), device=a.device, dtype=torch.float32)
+    _lib.check(_lib.load().ssla_gemm_f32_tc(a.data_ptr(), M, K, a.stride(0), bh.data_ptr(), bl.data_ptr(), N, K,
+                                            out.data_ptr(), N, _err_flag(a.device).data_ptr(), _lib.stream_of(a)),
+               "gemm_f32_tc")
+    return out
+
+
+def check_tc_errors(dev) -> None:
+    """Raise if a ``matmul_tc`` launch on ``dev`` reported a pipeline timeout (one host read)."""
+    f = _ERR.get(_dev_index(dev))
+    if f is not None and int(f.item()):
+        f.zero_()
+        raise RuntimeError("matmul_tc: a tensor-core GEMM pipeline wait timed out")
+
+
+TC_MIN_ROWS = 4096  # below this the CUDA-core row kernel's single launch is as fast
+
+
+class RowsGemm:
+    """Right-hand operand B [K, N] of ``a @ B`` prepared for both fp32 paths: the tensor-core
+    GEMM (``matmul_tc``, B^T split to TF32 once) for many rows with K a multiple of 4, the
+    CUDA-core row kernel (``matmul_rows``) otherwise."""
+
+    def __init__(self, b_kn: torch.Tensor):
+        self.b = b_kn.contiguous().float()
+        self.K = self.b.shape[0]
+        self.split = split_tf32(self.b.t().contiguous()) if self.K % 4 == 0 else None
+
+    def __call__(self, a: torch.Tensor) -> torch.Tensor:
+        if self.split is not None and a.shape[0] >= TC_MIN_ROWS and tc_gemm_ok(a, self.K):
+            return matmul_tc(a, self.split)
+        return matmul_rows(a, self.b)

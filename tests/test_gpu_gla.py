@@ -12,6 +12,16 @@ pytestmark = pytest.mark.gpu
 FP32_TOL, BF16_TOL = 1e-5, 2e-2
 
 
+@pytest.fixture(autouse=True)
+def no_wait_timeouts():
+    """Every test leaves the tensor-core chunk kernels' bounded-wait counter at zero."""
+    from ssla_b200 import _lib
+
+    _lib.tc_wait_timeouts(reset=True)
+    yield
+    assert _lib.tc_wait_timeouts(reset=True) == 0
+
+
 def make(T, H, K, V, cu, dtype, seed=0, h0=True, gscale=16.0):
     gen = torch.Generator().manual_seed(seed)
     q = torch.randn(T, H, K, generator=gen)

@@ -226,6 +226,28 @@ def test_matmul_rows_matches_torch(M, K, N):
         assert rel_err(got, ref) < 1e-6
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,N", [(1, 4, 16), (300, 12, 324), (5000, 48, 1296), (4097, 864, 96), (70000, 36, 40),
+                                   (130, 100, 130)])
+def test_matmul_tc_split_tf32(M, K, N):
+    """The split-TF32 tensor-core GEMM (csrc/gemm_tf32.cu) against a float64 product: partial
+    tiles in M, N and K, N below and above one tile, K up to 864.  Bound: 2e-5 of the largest
+    output magnitude (the fp32 cuBLAS product lands near 1e-6 here)."""
+    from ssla_b200.ops.mos import RowsGemm, check_tc_errors, matmul_tc, split_tf32
+
+    gen = torch.Generator().manual_seed(M + K + N)
+    a = torch.randn(M, K, generator=gen)
+    b = torch.randn(N, K, generator=gen) / K ** 0.5
+    ref = a.double() @ b.double().t()
+    got = matmul_tc(a.cuda(), split_tf32(b.cuda()))
+    check_tc_errors("cuda")
+    assert got.shape == (M, N)
+    err = (got.cpu().double() - ref).abs().max() / ref.abs().max()
+    assert err < 2e-5, float(err)
+    rg = RowsGemm(b.t().cuda())  # dispatch: tensor cores from TC_MIN_ROWS rows, row kernel below
+    assert ((rg(a.cuda()).cpu().double() - ref).abs().max() / ref.abs().max()) < 2e-5
+
+
 @pytest.mark.parametrize("I,C", [(2, 12), (12, 12)])
 def test_linear_attention_matches_reference(I, C):
     """LinearAttention (layers/linear_attention.py:39-102) against the reference layer's output
