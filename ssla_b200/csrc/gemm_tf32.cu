@@ -11,11 +11,12 @@
 // a K = 128 product whatever K is.  B (the weights) is split once on the host side
 // (ssla_split_tf32); A is split in shared memory as it arrives.
 //
-// Persistent, warp-specialised CTA of 14 warps on a 128 x bn output tile per item (bn = 128,
-// or N rounded up to 16 when N is smaller) (items
-// walk n fastest, so the CTAs resident together share A row panels in L2):
+// Persistent, warp-specialised CTA of 14 warps on a 128 x bn output tile per item (items walk n
+// fastest, so the CTAs resident together share A row panels in L2).  K of one partial sum
+// (<= 128, the pixel-event projections) with N > 128: N split evenly into tiles of at most 256
+// columns, 2 stages; otherwise bn = 128 (or N rounded up to 16 when smaller), 3 stages:
 //   warp 0      TMA: A (128 x 32 fp32) and the two B tiles per 32-wide k block, into a
-//               3-stage ring (swizzle 128B, zero fill past the matrix edges);
+//               2- or 3-stage ring (swizzle 128B, zero fill past the matrix edges);
 //   warps 2-5   split: each thread rounds one 128-byte row of the A tile to TF32 in place and
 //               writes the remainder to the stage's lo tile;
 //   warp 1      MMA: one thread issues 3 x 4 tcgen05.mma.kind::tf32 (M = 128, N = bn, K = 8)
@@ -35,15 +36,16 @@ namespace {
 
 using namespace ssla::tc;
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
-constexpr int TILE = BM * BK * 4;  // 16 KB; B tiles have the same size (BN = BM)
-constexpr int STAGE_BYTES = 4 * TILE;  // A (hi in place) | A lo | B hi | B lo
+constexpr int BM = 128, BN = 128, BK = 32;
+constexpr int TILE = BM * BK * 4;  // 16 KB A tile
+// stage: A (hi in place) | A lo | B hi | B lo, B tiles of BNT rows
+__host__ __device__ constexpr int stage_bytes(int bnt) { return 2 * TILE + 2 * bnt * BK * 4; }
 constexpr int KB_PARTIAL = 4;  // k blocks (K = 128) per tensor-core partial sum, then fp32 adds
 constexpr int NT = 448;       // 14 warps
 constexpr int EPI_WARPS = 8;  // warps 6..13
 constexpr int STAGING = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 fp32, 128-byte swizzle
 constexpr uint32_t kWaitIters = 1u << 24;
-constexpr size_t kSmemBytes = STAGES * STAGE_BYTES + EPI_WARPS * STAGING + 1024;
+constexpr size_t smem_bytes(int bnt, int st) { return (size_t)st * stage_bytes(bnt) + EPI_WARPS * STAGING + 1024; }
 
 __device__ __forceinline__ uint64_t desc_sw128(const void* tile) {
   return smem_desc(smem_u32(tile), 1024u, 1024u) | ((uint64_t)2 << 61);
@@ -55,13 +57,15 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+template <int ST>
 struct Bars {
-  uint64_t full[STAGES], split[STAGES], empty[STAGES], accf[2], acce[2];
+  uint64_t full[ST], split[ST], empty[ST], accf[2], acce[2];
   uint32_t tbase;
   volatile int abort;  // read in every role's loop condition
 };
 
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Bars& S, int* err) {
+template <class BarsT>
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, BarsT& S, int* err) {
   if (mbar_wait(bar, parity, kWaitIters)) return true;
   if (!S.abort) {
     S.abort = 1;
@@ -71,8 +75,9 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Ba
 }
 
 // MULTI: K spans more than one partial sum (the epilogue adds partial sums in registers);
-// without it the accumulator is read once, straight into the output registers.
-template <bool MULTI>
+// without it the accumulator is read once, 32 columns at a time, straight into the stores.
+// BNT: the largest N tile (B tile rows, TMEM columns per accumulator); ST: pipeline stages.
+template <bool MULTI, int BNT, int ST>
 __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ma,
                                                              const __grid_constant__ CUtensorMap mbh,
                                                              const __grid_constant__ CUtensorMap mbl,
@@ -81,11 +86,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
                                                              int64_t ldc, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ Bars S;
+  constexpr int STAGES = ST, STAGE_BYTES = stage_bytes(BNT), BTILE = BNT * BK * 4;
+  __shared__ Bars<ST> S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int mtiles = (M + BM - 1) / BM, ntiles = (N + bn - 1) / bn, kblocks = (K + BK - 1) / BK;
   const int items = mtiles * ntiles;
-  if (warp == 1) tmem_alloc(&S.tbase, 2 * BN);
+  if (warp == 1) tmem_alloc(&S.tbase, 2 * BNT);
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&S.full[s], 1);
@@ -117,10 +123,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
           const uint32_t use = it / STAGES;
           if (use > 0 && !wait_or_abort(&S.empty[s], (use - 1) & 1, S, err)) break;
           unsigned char* st = smem + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&S.full[s], 3 * TILE);
+          mbar_arrive_expect_tx(&S.full[s], TILE + 2 * BTILE);
           tma_load_2d(st, &ma, k * BK, m0, &S.full[s]);
           tma_load_2d(st + 2 * TILE, &mbh, k * BK, n0, &S.full[s]);
-          tma_load_2d(st + 3 * TILE, &mbl, k * BK, n0, &S.full[s]);
+          tma_load_2d(st + 2 * TILE + BTILE, &mbl, k * BK, n0, &S.full[s]);
         }
       }
     }
@@ -141,7 +147,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
             }
             fence_after();
           }
-          const uint32_t d = tb + a * BN;
+          const uint32_t d = tb + a * BNT;
           const int s = it % STAGES;
           if (!wait_or_abort(&S.split[s], (it / STAGES) & 1, S, err)) {
             ok = false;
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
           fence_after();
           unsigned char* st = smem + s * STAGE_BYTES;
           const uint64_t ah = desc_sw128(st), al = desc_sw128(st + TILE);
-          const uint64_t bh = desc_sw128(st + 2 * TILE), bl = desc_sw128(st + 3 * TILE);
+          const uint64_t bh = desc_sw128(st + 2 * TILE), bl = desc_sw128(st + 2 * TILE + BTILE);
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {  // K = 8 per MMA: 32 bytes along the swizzled row
             const uint64_t o = 2u * kk;
@@ -211,6 +217,51 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
     bool ok = true;
     for (int i = blockIdx.x; ok && i < items && !S.abort; i += gridDim.x) {
       const int m0 = (i / ntiles) * BM, n0 = (i % ntiles) * bn;
+      if constexpr (!MULTI) {
+        // one partial sum: 32-column chunks q = grp, grp + 2, ... straight from TMEM to the
+        // stores; the accumulator is released after the last chunk
+        const uint32_t a = t & 1;
+        if (!wait_or_abort(&S.accf[a], (t >> 1) & 1, S, err)) break;
+        fence_after();
+        const int nch = (bn + 31) / 32;
+        for (int q = grp; q < nch; q += 2) {
+          float w[32];
+          tmem_ld32x32b_x32(tb + ((uint32_t)(sub * 32) << 16) + a * BNT + q * 32, w);
+          const int col0 = n0 + q * 32;
+          if (use_tma_store) {
+            if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging block
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                  make_float4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0 && m0 + sub * 32 < M && col0 < N) {
+              tma_store_2d(&mc, stg, col0, m0 + sub * 32);
+              bulk_commit_group();
+            }
+          } else {
+            const int row = m0 + r;
+            float* crow = C + (int64_t)row * ldc;
+            if (row < M && col0 < N) {
+              if (vec && col0 + 32 <= N) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  *reinterpret_cast<float4*>(crow + col0 + 4 * j) =
+                      make_float4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < N) crow[col0 + j] = w[j];
+              }
+            }
+          }
+        }
+        fence_before();
+        mbar_arrive(&S.acce[a]);
+        ++t;
+        continue;
+      }
       float v[2][32];
       for (int p = 0; p < partials; ++p, ++t) {
         const uint32_t a = t & 1;
@@ -223,7 +274,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
         for (int c = 0; c < 2; ++c) {
           if (c < nc) {
             float w[32];
-            tmem_ld32x32b_x32(tb + ((uint32_t)(sub * 32) << 16) + a * BN + grp * 64 + c * 32, w);
+            tmem_ld32x32b_x32(tb + ((uint32_t)(sub * 32) << 16) + a * BNT + grp * 64 + c * 32, w);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[c][j] = (MULTI && p) ? v[c][j] + w[j] : w[j];
           }
@@ -273,7 +324,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
   }
   __syncthreads();
   fence_after();
-  if (warp == 1) tmem_dealloc(tb, 2 * BN);
+  if (warp == 1) tmem_dealloc(tb, 2 * BNT);
 }
 
 __global__ void split_tf32_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ hi,
@@ -321,38 +372,46 @@ extern "C" int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t ld
   SSLA_CHECK_ARG(lda % 4 == 0 && ldb % 4 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(B_hi) % 16 == 0 && reinterpret_cast<uintptr_t>(B_lo) % 16 == 0,
                  "ssla_gemm_f32_tc: A and B need 16-byte aligned rows (lda, ldb multiples of 4)");
+  // kernel shape: K beyond one partial sum -> 128-column tiles, 3 stages (partial sums held in
+  // registers); otherwise N above 128 -> up to 256-column tiles (N split evenly), 2 stages
+  const bool multi = K > (int64_t)gemm::KB_PARTIAL * gemm::BK;
+  const bool wide = !multi && N > gemm::BN;
+  int bn;
+  if (wide) {
+    const int64_t nt = (N + 255) / 256;
+    bn = (int)(((N + nt - 1) / nt + 31) / 32 * 32);  // whole 32-column epilogue chunks: none spills into the next tile
+  } else {
+    bn = N >= gemm::BN ? gemm::BN : (int)((N + 15) / 16 * 16);
+  }
   CUtensorMap ma, mbh, mbl, mc;
   int rc;
-  if ((rc = gemm::make_map(&ma, A, M, K, lda)) || (rc = gemm::make_map(&mbh, B_hi, N, K, ldb)) ||
-      (rc = gemm::make_map(&mbl, B_lo, N, K, ldb)))
+  const int brows = wide ? 256 : gemm::BN;
+  if ((rc = gemm::make_map(&ma, A, M, K, lda)) || (rc = gemm::make_map(&mbh, B_hi, N, K, ldb, brows)) ||
+      (rc = gemm::make_map(&mbl, B_lo, N, K, ldb, brows)))
     return rc;
   // output through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned
   const int use_tma_store = (ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0) ? 1 : 0;
   memset(&mc, 0, sizeof(mc));
   if (use_tma_store && (rc = gemm::make_map(&mc, C, M, N, ldc, 32))) return rc;
-  // N tile: the whole N when it fits one tile (a multiple of 16 for M = 128), else 128
-  const int bn = N >= gemm::BN ? gemm::BN : (int)((N + 15) / 16 * 16);
-  const bool multi = K > (int64_t)gemm::KB_PARTIAL * gemm::BK;
-  static bool ready[2] = {false, false};
-  if (!ready[multi]) {
-    if (cudaFuncSetAttribute(multi ? gemm::gemm_tf32x3_kernel<true> : gemm::gemm_tf32x3_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm::kSmemBytes) != cudaSuccess) {
-      set_error("ssla_gemm_f32_tc: cannot reserve %zu bytes of shared memory", gemm::kSmemBytes);
+  auto kern = multi ? gemm::gemm_tf32x3_kernel<true, 128, 3>
+                    : (wide ? gemm::gemm_tf32x3_kernel<false, 256, 2> : gemm::gemm_tf32x3_kernel<false, 128, 3>);
+  const size_t smem = multi || !wide ? gemm::smem_bytes(128, 3) : gemm::smem_bytes(256, 2);
+  const int variant = multi ? 0 : (wide ? 1 : 2);
+  static bool ready[3] = {false, false, false};
+  if (!ready[variant]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      set_error("ssla_gemm_f32_tc: cannot reserve %zu bytes of shared memory", smem);
       return SSLA_ERR_CUDA;
     }
-    ready[multi] = true;
+    ready[variant] = true;
   }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t items = ((M + gemm::BM - 1) / gemm::BM) * ((N + bn - 1) / bn);
   const unsigned grid = (unsigned)(items < sms ? items : sms);
-  if (multi)
-    gemm::gemm_tf32x3_kernel<true><<<grid, gemm::NT, gemm::kSmemBytes, (cudaStream_t)stream>>>(
-        ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn, C, ldc, err);
-  else
-    gemm::gemm_tf32x3_kernel<false><<<grid, gemm::NT, gemm::kSmemBytes, (cudaStream_t)stream>>>(
-        ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn, C, ldc, err);
+  kern<<<grid, gemm::NT, smem, (cudaStream_t)stream>>>(ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn,
+                                                      C, ldc, err);
   SSLA_CHECK_LAUNCH("ssla_gemm_f32_tc");
   return SSLA_OK;
 }
