@@ -397,17 +397,20 @@ extern "C" int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t ld
                     : (wide ? gemm::gemm_tf32x3_kernel<false, 256, 2> : gemm::gemm_tf32x3_kernel<false, 128, 3>);
   const size_t smem = multi || !wide ? gemm::smem_bytes(128, 3) : gemm::smem_bytes(256, 2);
   const int variant = multi ? 0 : (wide ? 1 : 2);
-  static bool ready[3] = {false, false, false};
-  if (!ready[variant]) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    set_error("ssla_gemm_f32_tc: device query failed");
+    return SSLA_ERR_CUDA;
+  }
+  // the shared-memory opt-in is a per-device function attribute: set once per (device, variant)
+  static bool ready[64][3] = {};
+  if (dev >= 64 || !ready[dev][variant]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
       set_error("ssla_gemm_f32_tc: cannot reserve %zu bytes of shared memory", smem);
       return SSLA_ERR_CUDA;
     }
-    ready[variant] = true;
+    if (dev < 64) ready[dev][variant] = true;
   }
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t items = ((M + gemm::BM - 1) / gemm::BM) * ((N + bn - 1) / bn);
   const unsigned grid = (unsigned)(items < sms ? items : sms);
   kern<<<grid, gemm::NT, smem, (cudaStream_t)stream>>>(ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn,
