@@ -59,7 +59,7 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 template <int ST>
 struct Bars {
-  uint64_t full[ST], split[ST], empty[ST], accf[2], acce[2];
+  uint64_t full[ST], split[ST], empty[ST], accf[2], acce[2], rd;  // rd: split threads' packed-row reads done
   uint32_t tbase;
   volatile int abort;  // read in every role's loop condition
 };
@@ -82,7 +82,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
                                                              const __grid_constant__ CUtensorMap mbh,
                                                              const __grid_constant__ CUtensorMap mbl,
                                                              const __grid_constant__ CUtensorMap mc, int use_tma_store,
-                                                             int M, int N, int K, int bn, float* __restrict__ C,
+                                                             int M, int N, int K, int bn, int a_cols,
+                                                             float* __restrict__ C,
                                                              int64_t ldc, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
       mbar_init(&S.accf[a], 1);
       mbar_init(&S.acce[a], 32 * EPI_WARPS);
     }
+    mbar_init(&S.rd, 128);
     S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tensormap(&ma);
@@ -123,7 +125,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
           const uint32_t use = it / STAGES;
           if (use > 0 && !wait_or_abort(&S.empty[s], (use - 1) & 1, S, err)) break;
           unsigned char* st = smem + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&S.full[s], TILE + 2 * BTILE);
+          mbar_arrive_expect_tx(&S.full[s], (a_cols ? BM * a_cols * 4 : TILE) + 2 * BTILE);
           tma_load_2d(st, &ma, k * BK, m0, &S.full[s]);
           tma_load_2d(st + 2 * TILE, &mbh, k * BK, n0, &S.full[s]);
           tma_load_2d(st + 2 * TILE + BTILE, &mbl, k * BK, n0, &S.full[s]);
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
     // split: thread r (0..127) owns row r of the A tile (128 bytes: 8 16-byte pieces; the
     // swizzle permutes pieces within the row, and hi / lo share the layout)
     const int r = tid - 64;
-    uint32_t it = 0;
+    uint32_t it = 0, rounds = 0;
     for (int i = blockIdx.x; i < items && !S.abort; i += gridDim.x) {
       bool ok = true;
       for (int k = 0; k < kblocks; ++k, ++it) {
@@ -187,6 +189,30 @@ __global__ void __launch_bounds__(NT, 1) gemm_tf32x3_kernel(const __grid_constan
         }
         float4* hi = reinterpret_cast<float4*>(smem + s * STAGE_BYTES + r * 128);
         float4* lo = reinterpret_cast<float4*>(smem + s * STAGE_BYTES + TILE + r * 128);
+        if (a_cols) {
+          // compact A (K < 32 columns, rows packed at K * 4 bytes): read this row's pieces, wait
+          // until all 128 rows are read (the swizzled rows overwrite the packed data), then write
+          // logical piece j of row r at piece position j ^ (r % 8), zeros past K
+          const float4* src = reinterpret_cast<const float4*>(smem + s * STAGE_BYTES + r * a_cols * 4);
+          float4 x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = 4 * j < a_cols ? src[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+          mbar_arrive(&S.rd);  // a bounded barrier over the 128 split threads
+          if (!wait_or_abort(&S.rd, (rounds++) & 1, S, err)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int q = j ^ (r & 7);
+            const float4 h = make_float4(tf32_rna(x[j].x), tf32_rna(x[j].y), tf32_rna(x[j].z), tf32_rna(x[j].w));
+            hi[q] = h;
+            lo[q] = make_float4(x[j].x - h.x, x[j].y - h.y, x[j].z - h.z, x[j].w - h.w);
+          }
+          fence_proxy_async();
+          mbar_arrive(&S.split[s]);
+          continue;
+        }
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           const int j = (jj + r) & 7;  // rotate the piece order by row: 8 rows hit 8 bank groups
@@ -336,12 +362,15 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, int64_t n, float*
   }
 }
 
-int make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows = BM) {
+// box_cols = BK: 128-byte swizzled k blocks; box_cols < BK: whole rows of a narrow matrix,
+// packed (no swizzle), rearranged by the split warps.
+int make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows = BM,
+             int box_cols = BK) {
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  return tma::encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
-                     "ssla_gemm_f32_tc");
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  return tma::encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                     box_cols == BK ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, "ssla_gemm_f32_tc");
 }
 
 }  // namespace
@@ -386,8 +415,14 @@ extern "C" int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t ld
   CUtensorMap ma, mbh, mbl, mc;
   int rc;
   const int brows = wide ? 256 : gemm::BN;
-  if ((rc = gemm::make_map(&ma, A, M, K, lda)) || (rc = gemm::make_map(&mbh, B_hi, N, K, ldb, brows)) ||
-      (rc = gemm::make_map(&mbl, B_lo, N, K, ldb, brows)))
+  // A narrower than one k block (the first layers' 12 / 24 features): whole packed rows per
+  // copy instead of 32-column boxes that read mostly outside the matrix
+  const int a_cols = K < gemm::BK ? (int)K : 0;
+  // B rows padded to a whole k block (ldb >= 32 with K < 32) are read whole: their extra
+  // columns meet the zero columns of A and must only be finite
+  const int64_t bcols = (K < gemm::BK && ldb >= gemm::BK) ? gemm::BK : K;
+  if ((rc = gemm::make_map(&ma, A, M, K, lda, gemm::BM, a_cols ? a_cols : gemm::BK)) || (rc = gemm::make_map(&mbh, B_hi, N, bcols, ldb, brows)) ||
+      (rc = gemm::make_map(&mbl, B_lo, N, bcols, ldb, brows)))
     return rc;
   // output through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned
   const int use_tma_store = (ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0) ? 1 : 0;
@@ -413,7 +448,7 @@ extern "C" int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t ld
   }
   const int64_t items = ((M + gemm::BM - 1) / gemm::BM) * ((N + bn - 1) / bn);
   const unsigned grid = (unsigned)(items < sms ? items : sms);
-  kern<<<grid, gemm::NT, smem, (cudaStream_t)stream>>>(ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn,
+  kern<<<grid, gemm::NT, smem, (cudaStream_t)stream>>>(ma, mbh, mbl, mc, use_tma_store, (int)M, (int)N, (int)K, bn, a_cols,
                                                       C, ldc, err);
   SSLA_CHECK_LAUNCH("ssla_gemm_f32_tc");
   return SSLA_OK;

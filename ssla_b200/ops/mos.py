@@ -137,16 +137,17 @@ def tc_gemm_ok(a: torch.Tensor, k: int) -> bool:
 
 def matmul_tc(a: torch.Tensor, bt_split) -> torch.Tensor:
     """a [M, K] @ B^T in fp32 on the tensor cores (split TF32), B given as ``split_tf32`` of
-    B [N, K].  The device error flag of the kernel's bounded waits is checked lazily by
+    B [N, K] (or of B zero-padded to [N, 32] when K < 32: whole-row copies).  The device error flag of the kernel's bounded waits is checked lazily by
     ``check_tc_errors``."""
     bh, bl = bt_split
     _lib.require_cuda(a, bh, bl, what="matmul_tc")
     M, K = a.shape
     N = bh.shape[0]
-    if not tc_gemm_ok(a, K) or bh.shape[1] != K:
-        raise ValueError("matmul_tc: a must be fp32 [M, K] with 16-byte aligned rows, K % 4 == 0, B [N, K]")
+    if not tc_gemm_ok(a, K) or bh.shape[1] < K or bh.shape != bl.shape:
+        raise ValueError("matmul_tc: a must be fp32 [M, K] with 16-byte aligned rows, K % 4 == 0, B [N, >= K]")
     out = torch.empty((M, N), device=a.device, dtype=torch.float32)
-    _lib.check(_lib.load().ssla_gemm_f32_tc(a.data_ptr(), M, K, a.stride(0), bh.data_ptr(), bl.data_ptr(), N, K,
+    _lib.check(_lib.load().ssla_gemm_f32_tc(a.data_ptr(), M, K, a.stride(0), bh.data_ptr(), bl.data_ptr(), N,
+                                            bh.shape[1],
                                             out.data_ptr(), N, _err_flag(a.device).data_ptr(), _lib.stream_of(a)),
                "gemm_f32_tc")
     return out
@@ -171,7 +172,10 @@ class RowsGemm:
     def __init__(self, b_kn: torch.Tensor):
         self.b = b_kn.contiguous().float()
         self.K = self.b.shape[0]
-        self.split = split_tf32(self.b.t().contiguous()) if self.K % 4 == 0 else None
+        bt = self.b.t().contiguous()
+        if self.K < 32:  # pad rows to one 128-byte k block: the B tiles then copy whole rows
+            bt = torch.nn.functional.pad(bt, (0, 32 - self.K))
+        self.split = split_tf32(bt) if self.K % 4 == 0 else None
 
     def __call__(self, a: torch.Tensor) -> torch.Tensor:
         if self.split is not None and a.shape[0] >= TC_MIN_ROWS and tc_gemm_ok(a, self.K):

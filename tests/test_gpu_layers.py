@@ -228,7 +228,7 @@ def test_matmul_rows_matches_torch(M, K, N):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,K,N", [(1, 4, 16), (300, 12, 324), (5000, 48, 1296), (4097, 864, 96), (70000, 36, 40),
-                                   (3000, 96, 2592), (700, 24, 648),
+                                   (3000, 96, 2592), (700, 24, 648), (5000, 12, 324), (4500, 8, 130),
                                    (130, 100, 130)])
 def test_matmul_tc_split_tf32(M, K, N):
     """The split-TF32 tensor-core GEMM (csrc/gemm_tf32.cu) against a float64 product: partial
