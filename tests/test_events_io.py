@@ -117,3 +117,13 @@ def test_gpu_windows_large_recording_vs_oracle():
     ev2, _ = store.windows([rid] * 3, ts[:3], 50000, max_len=int(rlens.max()) + 5)
     assert torch.equal(ev2[:, : ev.shape[1]].cpu(), ev[:3].cpu()) or ev.shape[1] == 0
     assert torch.equal(ev2[:, ev.shape[1]:].cpu(), torch.tensor([0., 0., 0., -1.]).expand(3, ev2.shape[1] - ev.shape[1], 4))
+
+
+def test_window_must_be_whole_microseconds():
+    from ssla_b200.utils.io.dat_events_tools import _integral_us
+
+    assert _integral_us(0.1 * 1e6) == 100000  # the Gen1 configs' 0.1 s window
+    with pytest.raises(ValueError):
+        _integral_us(1000.5)
+    with pytest.raises(ValueError):
+        _integral_us(-1)
