@@ -484,10 +484,11 @@ def main():
     host = make_inputs(1000 + rank)
     d = {n: t.to(dev) for n, t in host.items()}
     N = B
-    MC = L.ssla_chunk_gla_max_chunks(N, B * T)
-    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, B * T, H, K, V)
+    BF = _lib.BF16
+    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, B * T, H, K, V, BF, BF)
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
-    states = torch.empty(MC, H, K, V, device=dev)
+    st_bytes = L.ssla_chunk_gla_states_bytes(N, B * T, H, K, V, BF, BF)
+    states = torch.empty(st_bytes, device=dev, dtype=torch.uint8)
     o = torch.empty_like(d["v"])
     ht = torch.empty(B, H, K, V, device=dev)
     dq, dk, dv = torch.empty_like(d["q"]), torch.empty_like(d["k"]), torch.empty_like(d["v"])
@@ -497,16 +498,15 @@ def main():
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     scale = K ** -0.5
-    BF = _lib.BF16
 
     def step():
         _lib.check(L.ssla_chunk_gla_fwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
                                         d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(), N, B * T, H, K, V,
                                         scale, d["h0"].data_ptr(), o.data_ptr(), ht.data_ptr(),
-                                        states.data_ptr(), ws.data_ptr(), ws_bytes, sp), "fwd")
+                                        states.data_ptr(), st_bytes, ws.data_ptr(), ws_bytes, sp), "fwd")
         _lib.check(L.ssla_chunk_gla_bwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
                                         d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(), N, B * T, H, K, V,
-                                        scale, states.data_ptr(), d["do"].data_ptr(), d["dht"].data_ptr(),
+                                        scale, states.data_ptr(), st_bytes, d["do"].data_ptr(), d["dht"].data_ptr(),
                                         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
                                         dh0.data_ptr(), ws.data_ptr(), ws_bytes, sp), "bwd")
 
@@ -549,7 +549,7 @@ def main():
     fwd_only = lambda: _lib.check(L.ssla_chunk_gla_fwd(
         d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["g"].data_ptr(), BF, BF, d["cu"].data_ptr(),
         N, B * T, H, K, V, scale, d["h0"].data_ptr(), o.data_ptr(), ht.data_ptr(), states.data_ptr(),
-        ws.data_ptr(), ws_bytes, sp), "fwd")
+        st_bytes, ws.data_ptr(), ws_bytes, sp), "fwd")
     fwd_s = max_over_ranks(timed(fwd_only, args.steps)) / args.steps
     bwd_s = secs / args.steps - fwd_s
 

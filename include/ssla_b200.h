@@ -86,25 +86,30 @@ int ssla_recurrent_gla_fwd(const void* q, const void* k, const void* v, const vo
 /* ------------------------------------------------------------------ chunked GLA
  * chunk_gla forward / backward (ops/gla/chunk.py:906-1053, ops/common/chunk_h.py:242-347).
  * Layout: q,k,g [T,H,K]; v,o,do [T,H,V]; h0,ht,dht,dh0 [N,H,K,V] fp32 (nullable).
- * `states` [max_chunks,H,K,V] fp32 receives the state at the start of every 64-token
- * chunk (written by fwd, read by bwd); max_chunks = ssla_chunk_gla_max_chunks(N,T).
- * `workspace` is caller-allocated device scratch of ssla_chunk_gla_workspace_bytes().
- * dq,dk,dv are written in `dtype`; dg in fp32 (the reference returns dg in fp32,
- * ops/gla/chunk.py:1116).  K, V <= 64. */
+ * `states` is a caller-allocated device buffer of ssla_chunk_gla_states_bytes() that the
+ * forward fills (the call's chunk table, which 64-token chunks the exact kernels handle, and
+ * the state at every chunk start: fp32, plus the 16-bit scaled copy the tensor-core kernels
+ * read for 16-bit inputs with K = V = 64) and the backward reads; it replaces the reference's
+ * cached chunk indices (ops/utils/index.py:69-86) and saved h (ops/gla/chunk.py:933).
+ * `workspace` is caller-allocated device scratch of ssla_chunk_gla_workspace_bytes() (the
+ * forward needs only a prefix of it).  dq,dk,dv are written in `dtype`; dg in fp32 (the
+ * reference returns dg in fp32, ops/gla/chunk.py:1116).  K, V <= 64. */
 int64_t ssla_chunk_gla_max_chunks(int64_t n_seqs, int64_t T);
+size_t ssla_chunk_gla_states_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
+                                   int dtype, int dtype_g);
 size_t ssla_chunk_gla_workspace_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K,
-                                      int64_t V);
+                                      int64_t V, int dtype, int dtype_g);
 int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, const void* g, int dtype,
                        int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
                        int64_t H, int64_t K, int64_t V, float scale, const float* h0, void* o,
-                       float* ht, float* states, void* workspace, size_t workspace_bytes,
-                       ssla_stream_t stream);
+                       float* ht, void* states, size_t states_bytes, void* workspace,
+                       size_t workspace_bytes, ssla_stream_t stream);
 int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* g, int dtype,
                        int dtype_g, const int64_t* cu_seqlens, int64_t n_seqs, int64_t T,
-                       int64_t H, int64_t K, int64_t V, float scale, const float* states,
-                       const void* dout, const float* dht, void* dq, void* dk, void* dv,
-                       float* dg, float* dh0, void* workspace, size_t workspace_bytes,
-                       ssla_stream_t stream);
+                       int64_t H, int64_t K, int64_t V, float scale, const void* states,
+                       size_t states_bytes, const void* dout, const float* dht, void* dq,
+                       void* dk, void* dv, float* dg, float* dh0, void* workspace,
+                       size_t workspace_bytes, ssla_stream_t stream);
 
 /* chunk_gla forward that allocates nothing: no counterpart in the reference.  For callers
  * that cannot call cudaMalloc (a runtime that owns every allocation and hands the library
@@ -249,8 +254,9 @@ int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t lda, const fl
                      int64_t N, int64_t ldb, float* C, int64_t ldc, int* err, ssla_stream_t stream);
 
 /* Number of bounded shared-memory barrier waits in the tensor-core chunk kernels that gave up
- * since the last reset (synchronous device read; 0 in a healthy run).  A nonzero count marks
- * the results of the launches since the reset as untrustworthy. */
+ * since the last reset (synchronous device read; 0 in a healthy run).  A CTA whose wait gave
+ * up writes NaN into the outputs of the items it still had, so such results are visible
+ * without this read; a nonzero count says why. */
 int ssla_chunk_gla_tc_timeouts(int reset, unsigned* count);
 
 #ifdef __cplusplus

@@ -1,6 +1,7 @@
 """CPU restatements of the reference GLA algorithms (test infrastructure only).
 
-* ``naive_gla_recurrent``  — ops/gla/naive.py:50-111 (token recurrence, fp32 state).
+* ``naive_gla_recurrent``  — ops/gla/naive.py:50-111 (token recurrence, fp32 state);
+  ``naive_gla_recurrent_step`` the same for one token of many sequences at once.
 * ``naive_gla_parallel``   — ops/gla/naive.py:6-47 (O(T^2) parallel form).
 * ``naive_gla_recurrent_scalar`` — ops/gla/naive_scalar.py:7-66.
 * ``chunk_gla_ref``        — the chunked algorithm of ops/gla/chunk.py:906-960 evaluated in
@@ -37,6 +38,20 @@ def naive_gla_recurrent(q, k, v, g, cu_seqlens, scale=None, initial_state=None, 
         finals.append(S)
     o = torch.cat(outs, 0) if outs else q.new_zeros((0, H, V))
     return o, (torch.stack(finals, 0) if output_final_state else None)
+
+
+def naive_gla_recurrent_step(q, k, v, g, state, scale=None):
+    """One token of every sequence through the recurrence of ops/gla/naive.py:50-111 (state
+    update :95, read-out :97-98), vectorised over the sequences: q, k, g [N, H, K], v [N, H, V],
+    state [N, H, K, V] fp32 -> (o [N, H, V] in q's dtype, new state fp32).  Equal to
+    ``naive_gla_recurrent`` on N sequences of one token each (tests/test_oracle.py)."""
+    K = q.shape[-1]
+    if scale is None:
+        scale = K ** -0.5
+    qf, kf, vf, gf = (x.to(torch.float32) for x in (q, k, v, g))
+    S = torch.exp(gf)[..., None] * state.to(torch.float32) + kf[..., None] * vf[..., None, :]
+    o = torch.einsum("nhk,nhkv->nhv", qf * scale, S).to(q.dtype)
+    return o, S
 
 
 def naive_gla_parallel(q, k, v, g, cu_seqlens, scale=None):

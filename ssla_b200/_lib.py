@@ -30,14 +30,15 @@ SIGNATURES = {
     "ssla_gla_scalar_bwd": (i32, [p, p, p, p, i32, i32, p, i64, i64, i64, f32, p, p, p, p, p, p, p, p, p]),
     "ssla_recurrent_gla_fwd": (i32, [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p]),
     "ssla_chunk_gla_max_chunks": (i64, [i64, i64]),
-    "ssla_chunk_gla_workspace_bytes": (sz, [i64, i64, i64, i64, i64]),
+    "ssla_chunk_gla_states_bytes": (sz, [i64, i64, i64, i64, i64, i32, i32]),
+    "ssla_chunk_gla_workspace_bytes": (sz, [i64, i64, i64, i64, i64, i32, i32]),
     "ssla_chunk_gla_fwd": (
         i32,
-        [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p, p, sz, p],
+        [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p, sz, p, sz, p],
     ),
     "ssla_chunk_gla_bwd": (
         i32,
-        [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p, p, p, p, p, p, sz, p],
+        [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, sz, p, p, p, p, p, p, p, p, sz, p],
     ),
     "ssla_chunk_gla_fwd_noalloc": (i32, [p, p, p, p, i32, i32, p, i64, i64, i64, i64, i64, f32, p, p, p, p]),
     "ssla_segment_offsets_sorted": (i32, [p, i64, i64, p, p]),

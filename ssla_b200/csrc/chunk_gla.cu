@@ -22,6 +22,8 @@
 // per-element exponents.  This file is the CUDA-core (fp32 FMA) implementation: it is used
 // for fp32 inputs, where results must match an fp32 reference to ~1e-6, and for shapes the
 // tensor-core kernels (chunk_gla_tc.cu) do not cover.
+#include <type_traits>
+
 #include "chunk_gla.cuh"
 
 namespace ssla {
@@ -31,19 +33,27 @@ namespace {
 constexpr int NTHR = 256;
 
 // --------------------------------------------------------------------------- prep + scans
+// Chunk offsets (exclusive scan of ceil(len / 64) over the sequences) and the chunk table.
+// With up to kOffSmem sequences the offsets are also kept in shared memory and every chunk id
+// finds its sequence by binary search there; with more sequences (typically short ones) each
+// thread fills the table entries of its own sequences.
+constexpr int kOffSmem = 4096;
+
 __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __restrict__ cu,
                                                              int64_t N, int64_t MC,
                                                              int64_t* __restrict__ off,
                                                              longlong2* __restrict__ tab,
-                                                             int* __restrict__ exact_count) {
+                                                             int* __restrict__ xcount) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry;
+  __shared__ int64_t soff[kOffSmem + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool small = N <= kOffSmem;
   griddep_launch_dependents();
   griddep_wait();  // the previous call's kernels may still read the table
   if (tid == 0) {
     carry = 0;
-    if (exact_count) *exact_count = 0;
+    if (xcount) *xcount = 0;
   }
   __syncthreads();
   for (int64_t base = 0; base < N; base += 1024) {
@@ -72,28 +82,41 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
     }
     __syncthreads();
     const int64_t before = carry + (warp > 0 ? warp_sums[warp - 1] : 0);
-    if (n < N) off[n] = before + incl - x;
+    if (n < N) {
+      off[n] = before + incl - x;
+      if (small) soff[n] = before + incl - x;
+    }
     __syncthreads();
     if (tid == 1023) carry = before + incl;
     __syncthreads();
   }
-  if (tid == 0) off[N] = carry;
-  __syncthreads();
-  // chunk table: {first token, valid rows | sequence << 32}, -1 sequence for unused ids.
-  // One thread per chunk id; its sequence is found by binary search over the offsets.
   const int64_t total = carry;
-  for (int64_t c = tid; c < total; c += 1024) {
-    int64_t lo = 0, hi = N - 1;  // last n with off[n] <= c
-    while (lo < hi) {
-      const int64_t mid = (lo + hi + 1) >> 1;
-      if (off[mid] <= c) lo = mid; else hi = mid - 1;
-    }
-    const int64_t t = cu[lo] + (c - off[lo]) * BT;
-    const int64_t e = cu[lo + 1];
-    const int64_t len = (e - t) < BT ? (e - t) : BT;
-    tab[c] = make_longlong2(t, len | (lo << 32));
+  if (tid == 0) {
+    off[N] = total;
+    if (small) soff[N] = total;
   }
-  for (int64_t c = carry + tid; c < MC; c += 1024) tab[c] = make_longlong2(0, (int64_t)-1 << 32);
+  __syncthreads();
+  // chunk table: {first token, valid rows | sequence << 32}, -1 sequence for unused ids
+  if (small) {
+    for (int64_t c = tid; c < total; c += 1024) {
+      int64_t lo = 0, hi = N - 1;  // last n with soff[n] <= c
+      while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (soff[mid] <= c) lo = mid; else hi = mid - 1;
+      }
+      const int64_t t = cu[lo] + (c - soff[lo]) * BT;
+      const int64_t e = cu[lo + 1];
+      const int64_t len = (e - t) < BT ? (e - t) : BT;
+      tab[c] = make_longlong2(t, len | (lo << 32));
+    }
+  } else {
+    for (int64_t n = tid; n < N; n += 1024) {
+      const int64_t s0 = cu[n], e = cu[n + 1];
+      int64_t c = off[n];
+      for (int64_t t = s0; t < e; t += BT, ++c) tab[c] = make_longlong2(t, ((e - t) < BT ? (e - t) : BT) | (n << 32));
+    }
+  }
+  for (int64_t c = total + tid; c < MC; c += 1024) tab[c] = make_longlong2(0, (int64_t)-1 << 32);
 }
 
 // h_{c+1} = decay_c * h_c + dS_c along the chunks of each sequence, element-wise in (k, v).
@@ -101,7 +124,10 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
 // on the host so the grid is about one resident wave); each segment first composes its affine
 // map (prod decay, local sum), segment start values are chained in shared memory, then every
 // segment re-walks its chunks from its start value writing the per-chunk states.  Loads are
-// issued 16 chunks at a time (they do not depend on the running state).
+// issued SCAN_U chunks at a time (they do not depend on the running state).  Per chunk the
+// value is written to h32 (fp32; every chunk when xflag is null, else only flagged items) and,
+// for the tensor-core kernels, escale[chunk][k] * value to h16 in the 16-bit operand dtype T16
+// (T16 = float: no 16-bit output).
 constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 8;
 
 // VEC consecutive state elements (one key row, consecutive value columns) per thread.
@@ -112,6 +138,7 @@ template <> struct SVec<1> {
   static __device__ __forceinline__ void st(float* p, float x) { *p = x; }
   static __device__ __forceinline__ float fma(float d, float x, float a) { return fmaf(d, x, a); }
   static __device__ __forceinline__ float zero() { return 0.f; }
+  template <typename T16> static __device__ __forceinline__ void st16(T16* p, float s, float x) { stf(p, s * x); }
 };
 template <> struct SVec<4> {
   using type = float4;
@@ -121,16 +148,26 @@ template <> struct SVec<4> {
     return make_float4(fmaf(d, x.x, a.x), fmaf(d, x.y, a.y), fmaf(d, x.z, a.z), fmaf(d, x.w, a.w));
   }
   static __device__ __forceinline__ float4 zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <typename T16> static __device__ __forceinline__ void st16(T16* p, float s, float4 x) {
+    T16 y[4];
+    stf(y + 0, s * x.x);
+    stf(y + 1, s * x.y);
+    stf(y + 2, s * x.z);
+    stf(y + 3, s * x.w);
+    *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(y);
+  }
 };
 
-template <int VEC>
+template <int VEC, typename T16>
 __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
-    const float* __restrict__ init, float* __restrict__ per_chunk, float* __restrict__ fin,
+    const float* __restrict__ init, float* __restrict__ h32, const unsigned char* __restrict__ xflag,
+    T16* __restrict__ h16, const float* __restrict__ escale, float* __restrict__ fin,
     bool reverse, int nseg) {
   using S = SVec<VEC>;
   using vec = typename S::type;
+  constexpr bool kOut16 = !std::is_same<T16, float>::value;
   __shared__ float sA[SCAN_MAXSEG][SCAN_EL];
   __shared__ vec sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
   const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
@@ -140,11 +177,9 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
   const int64_t idx = ((int64_t)blockIdx.x * SCAN_EL + el) * VEC;  // first element of this thread
   const bool valid = idx < N * HKV;
   int64_t len = 0;
-  // pointers to this thread's elements of its segment's first chunk; steps between chunks
-  const float* pa = dS;
-  const float* pd = decay;
-  float* po = per_chunk;
-  int64_t sa = 0, sd = 0;
+  // this thread's elements in its segment's first chunk; steps between chunks
+  int64_t ce = 0, cd = 0, cf = 0;  // element offset, decay / escale offset, flag offset
+  int64_t sa = 0, sd = 0, sf = 0;
   if (valid) {
     const int64_t seq = idx / HKV;
     const int64_t rem = idx - seq * HKV;
@@ -157,40 +192,30 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     len = i1 > i0 ? i1 - i0 : 0;
     const int64_t dir = reverse ? -1 : 1;
     const int64_t cfirst = (reverse ? c0 + n - 1 : c0) + dir * i0;
-    const int64_t ebase = head * KV + kv, dbase = head * K + kv / V;
     if (len > 0) {
-      pa = dS + cfirst * HKV + ebase;
-      pd = decay + cfirst * HK + dbase;
-      po = per_chunk + cfirst * HKV + ebase;
+      ce = cfirst * HKV + head * KV + kv;
+      cd = cfirst * HK + head * K + kv / V;
+      cf = cfirst * H + head;
     }
     sa = dir * HKV;
     sd = dir * HK;
+    sf = dir * H;
   }
-  // 1. compose this segment's affine map x -> A x + B (loads issued SCAN_U chunks at a time)
+  // 1. compose this segment's affine map x -> A x + B.  Loads are issued SCAN_U chunks at a time
+  // (predicated, so a short segment still costs one round trip): they do not depend on B.
   float A = 1.f;
   vec B = S::zero();
-  {
-    const float* qa = pa;
-    const float* qd = pd;
-    int64_t i = 0;
-    for (; i + SCAN_U <= len; i += SCAN_U) {
-      float d[SCAN_U];
-      vec a[SCAN_U];
+  for (int64_t i = 0; i < len; i += SCAN_U) {
+    float d[SCAN_U];
+    vec a[SCAN_U];
 #pragma unroll
-      for (int u = 0; u < SCAN_U; ++u) {
-        d[u] = qd[u * sd];
-        a[u] = S::ld(qa + u * sa);
-      }
+    for (int u = 0; u < SCAN_U; ++u) {
+      const bool in = i + u < len;
+      d[u] = in ? decay[cd + (i + u) * sd] : 1.f;
+      a[u] = in ? S::ld(dS + ce + (i + u) * sa) : S::zero();
+    }
 #pragma unroll
-      for (int u = 0; u < SCAN_U; ++u) { B = S::fma(d[u], B, a[u]); A *= d[u]; }
-      qa += SCAN_U * sa;
-      qd += SCAN_U * sd;
-    }
-    for (; i < len; ++i, qa += sa, qd += sd) {
-      const float d = *qd;
-      B = S::fma(d, B, S::ld(qa));
-      A *= d;
-    }
+    for (int u = 0; u < SCAN_U; ++u) { B = S::fma(d[u], B, a[u]); A *= d[u]; }
   }
   // 2. chain the segment start values
   vec x;
@@ -213,29 +238,24 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     if (valid && fin) S::st(fin + idx, S::fma(A, x, B));
   }
   // 3. re-walk from the start value, writing the state at every chunk
-  int64_t i = 0;
-  for (; i + SCAN_U <= len; i += SCAN_U) {
+  auto put = [&](int64_t e, int64_t dd, int64_t f, const vec& val) {
+    if (!xflag || xflag[f]) S::st(h32 + e, val);
+    if constexpr (kOut16) S::template st16<T16>(h16 + e, escale[dd], val);
+  };
+  for (int64_t i = 0; i < len; i += SCAN_U) {
     float d[SCAN_U];
     vec a[SCAN_U];
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
-      d[u] = pd[u * sd];
-      a[u] = S::ld(pa + u * sa);
+      const bool in = i + u < len;
+      d[u] = in ? decay[cd + (i + u) * sd] : 1.f;
+      a[u] = in ? S::ld(dS + ce + (i + u) * sa) : S::zero();
     }
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
-      S::st(po + u * sa, x);
+      if (i + u < len) put(ce + (i + u) * sa, cd + (i + u) * sd, cf + (i + u) * sf, x);
       x = S::fma(d[u], x, a[u]);
     }
-    pa += SCAN_U * sa;
-    pd += SCAN_U * sd;
-    po += SCAN_U * sa;
-  }
-  for (; i < len; ++i, pa += sa, pd += sd, po += sa) {
-    const float d = *pd;
-    const vec a = S::ld(pa);
-    S::st(po, x);
-    x = S::fma(d, x, a);
   }
 }
 
@@ -466,23 +486,23 @@ __device__ __forceinline__ void fwd_o_body(int64_t cid, int head,
       });
 }
 
-// Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
+// Plain launch: grid (chunks, heads).  Gated launch (xlist != null, fallback of the tensor-core
 // kernels): a small grid strides over the listed (chunk, head) items only (none: it exits).
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) fwd_o_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
     const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
-    T* __restrict__ o, const int* __restrict__ flags, int64_t MC) {
+    T* __restrict__ o, const int* __restrict__ xlist, int64_t MC) {
   griddep_launch_dependents();
   griddep_wait();
-  if (!flags) {
+  if (!xlist) {
     fwd_o_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
     return;
   }
-  const int n = flags[0];
+  const int n = xlist[0];
   for (int i = blockIdx.x; i < n; i += gridDim.x) {
-    const int w = flags[1 + i];
+    const int w = xlist[1 + i];
     fwd_o_body<T, Tg, P>(w / H, w % H, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, o);
     __syncthreads();
   }
@@ -686,7 +706,7 @@ __device__ __forceinline__ void bwd_body(int64_t cid, int head,
   }
 }
 
-// Plain launch: grid (chunks, heads).  Gated launch (flags != null, fallback of the tensor-core
+// Plain launch: grid (chunks, heads).  Gated launch (xlist != null, fallback of the tensor-core
 // kernels): a small grid strides over the listed (chunk, head) items only (none: it exits).
 template <typename T, typename Tg, int P>
 __global__ void __launch_bounds__(NTHR) bwd_kernel(
@@ -694,16 +714,17 @@ __global__ void __launch_bounds__(NTHR) bwd_kernel(
     const Tg* __restrict__ g, const int64_t* __restrict__ cu, const longlong2* __restrict__ chunk_tab,
     int64_t N, int H, int K, int V, float scale, const float* __restrict__ states,
     const float* __restrict__ dstates, const T* __restrict__ dout, T* __restrict__ dq,
-    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ flags, int64_t MC) {
+    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg, const int* __restrict__ xlist,
+    int64_t MC) {
   griddep_launch_dependents();
   griddep_wait();
-  if (!flags) {
+  if (!xlist) {
     bwd_body<T, Tg, P>(blockIdx.x, blockIdx.y, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
     return;
   }
-  const int n = flags[0];
+  const int n = xlist[0];
   for (int i = blockIdx.x; i < n; i += gridDim.x) {
-    const int w = flags[1 + i];
+    const int w = xlist[1 + i];
     bwd_body<T, Tg, P>(w / H, w % H, q, k, v, g, cu, chunk_tab, N, H, K, V, scale, states, dstates, dout, dq, dk, dv, dg);
     __syncthreads();
   }
@@ -734,14 +755,14 @@ int run_local(int mode, const void* a_src, const void* b_src, const void* g, con
 template <typename T, typename Tg, int P>
 int run_fwd_o(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
               const longlong2* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
-              const float* states, void* o, const int* flags, cudaStream_t s) {
+              const float* states, void* o, const int* xlist, cudaStream_t s) {
   auto kern = fwd_o_kernel<T, Tg, P>;
   const size_t smem = smem_fwd_o<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
+  const dim3 grid = xlist ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
                           : dim3((unsigned)MC, H);
   launch_pdl(kern, grid, dim3(NTHR), smem, s, (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K,
-             V, scale, states, (T*)o, flags, MC);
+             V, scale, states, (T*)o, xlist, MC);
   SSLA_CHECK_LAUNCH("chunk_gla fwd_o");
   return SSLA_OK;
 }
@@ -750,14 +771,14 @@ template <typename T, typename Tg, int P>
 int run_bwd(const void* q, const void* k, const void* v, const void* g, const int64_t* cu,
             const longlong2* off, int64_t N, int64_t MC, int H, int K, int V, float scale,
             const float* states, const float* dstates, const void* dout, void* dq, void* dk,
-            void* dv, float* dg, const int* flags, cudaStream_t s) {
+            void* dv, float* dg, const int* xlist, cudaStream_t s) {
   auto kern = bwd_kernel<T, Tg, P>;
   const size_t smem = smem_bwd<P>();
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const dim3 grid = flags ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
+  const dim3 grid = xlist ? dim3((unsigned)(MC * H < kNumSMs ? MC * H : kNumSMs), 1)
                           : dim3((unsigned)MC, H);
   launch_pdl(kern, grid, dim3(NTHR), smem, s, (const T*)q, (const T*)k, (const T*)v, (const Tg*)g, cu, off, N, H, K,
-             V, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, flags, MC);
+             V, scale, states, dstates, (const T*)dout, (T*)dq, (T*)dk, (T*)dv, dg, xlist, MC);
   SSLA_CHECK_LAUNCH("chunk_gla bwd");
   return SSLA_OK;
 }
@@ -788,12 +809,12 @@ inline int pad_of(int64_t K, int64_t V) {
 
 int simt_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
                const int64_t* cu, const longlong2* off, int64_t N, int64_t MC, int64_t H, int64_t K,
-               int64_t V, float scale, const float* states, void* o, const int* flags,
+               int64_t V, float scale, const float* states, void* o, const int* xlist,
                cudaStream_t s) {
   return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
     return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
       return run_fwd_o<T_, Tg, P>(q, k, v, g, cu, off, N, MC, (int)H, (int)K, (int)V, scale,
-                                  states, o, flags, s);
+                                  states, o, xlist, s);
     });
   });
 }
@@ -801,27 +822,40 @@ int simt_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void*
 int simt_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, const void* g,
              const int64_t* cu, const longlong2* off, int64_t N, int64_t MC, int64_t H, int64_t K,
              int64_t V, float scale, const float* states, const float* dstates, const void* dout,
-             void* dq, void* dk, void* dv, float* dg, const int* flags, cudaStream_t s) {
+             void* dq, void* dk, void* dv, float* dg, const int* xlist, cudaStream_t s) {
   return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
     return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
       return run_bwd<T_, Tg, P>(q, k, v, g, cu, off, N, MC, (int)H, (int)K, (int)V, scale, states,
-                                dstates, dout, dq, dk, dv, dg, flags, s);
+                                dstates, dout, dq, dk, dv, dg, xlist, s);
     });
   });
 }
 
 int launch_chunk_offsets(const int64_t* cu, int64_t N, int64_t MC, int64_t* chunk_off,
-                         longlong2* chunk_tab, int* flags, cudaStream_t s) {
-  launch_pdl(chunk_offsets_kernel, dim3(1), dim3(1024), 0, s, cu, N, MC, chunk_off, chunk_tab, flags);
+                         longlong2* chunk_tab, int* xcount, cudaStream_t s) {
+  launch_pdl(chunk_offsets_kernel, dim3(1), dim3(1024), 0, s, cu, N, MC, chunk_off, chunk_tab, xcount);
   SSLA_CHECK_LAUNCH("chunk_gla chunk_offsets");
   return SSLA_OK;
 }
 
+int simt_local(int dtype, int dtype_g, int mode, const void* a_src, const void* b_src, const void* g,
+               const int64_t* cu, const longlong2* chunk_tab, int64_t N, int64_t MC, int64_t H,
+               int64_t K, int64_t V, float scale, float* dS, float* decay, cudaStream_t s) {
+  return SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
+    return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
+      return run_local<T_, Tg, P>(mode, a_src, b_src, g, cu, chunk_tab, N, MC, (int)H, (int)K, (int)V, scale, dS,
+                                  decay, s);
+    });
+  });
+}
+
 int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_off, int64_t N,
-                      int64_t H, int64_t K, int64_t V, const float* init, float* per_chunk,
+                      int64_t H, int64_t K, int64_t V, const float* init, float* h32,
+                      const unsigned char* xflag, void* h16, int dtype16, const float* escale,
                       float* final_state, bool reverse, cudaStream_t s) {
   // 4 consecutive value columns per thread when rows split evenly and the state arrays align
-  const bool v4 = V % 4 == 0 && ((uintptr_t)dS | (uintptr_t)per_chunk | (uintptr_t)init | (uintptr_t)final_state) % 16 == 0;
+  const bool v4 = V % 4 == 0 &&
+                  ((uintptr_t)dS | (uintptr_t)h32 | (uintptr_t)init | (uintptr_t)final_state | (uintptr_t)h16) % 16 == 0;
   const int vec = v4 ? 4 : 1;
   const int64_t threads = N * H * K * V / vec;
   if (threads == 0) return SSLA_OK;
@@ -829,12 +863,20 @@ int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_
   int64_t nseg = (int64_t)kNumSMs * 2048 / threads;
   nseg = nseg < 1 ? 1 : (nseg > SCAN_MAXSEG ? SCAN_MAXSEG : nseg);
   const dim3 grid(ceil_div(threads, SCAN_EL)), block(SCAN_EL * (int)nseg);
-  if (v4)
-    launch_pdl(state_scan_kernel<4>, grid, block, 0, s, dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk,
-               final_state, reverse, (int)nseg);
-  else
-    launch_pdl(state_scan_kernel<1>, grid, block, 0, s, dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, per_chunk,
-               final_state, reverse, (int)nseg);
+  auto go = [&](auto kern, auto* out16) {
+    launch_pdl(kern, grid, block, 0, s, dS, decay, chunk_off, N, (int)H, (int)K, (int)V, init, h32, xflag, out16,
+               escale, final_state, reverse, (int)nseg);
+  };
+  if (!h16) {
+    if (v4) go(state_scan_kernel<4, float>, (float*)nullptr);
+    else go(state_scan_kernel<1, float>, (float*)nullptr);
+  } else if (dtype16 == SSLA_BF16) {
+    if (v4) go(state_scan_kernel<4, __nv_bfloat16>, (__nv_bfloat16*)h16);
+    else go(state_scan_kernel<1, __nv_bfloat16>, (__nv_bfloat16*)h16);
+  } else {
+    if (v4) go(state_scan_kernel<4, __half>, (__half*)h16);
+    else go(state_scan_kernel<1, __half>, (__half*)h16);
+  }
   SSLA_CHECK_LAUNCH("chunk_gla state_scan");
   return SSLA_OK;
 }
@@ -850,7 +892,7 @@ static int check_common(const char* name, int dtype, int dtype_g, int64_t N, int
   SSLA_CHECK_ARG(dtype_ok(dtype), "%s: bad dtype", name);
   SSLA_CHECK_ARG(dtype_g == dtype || dtype_g == SSLA_F32, "%s: g must have q's dtype or fp32", name);
   SSLA_CHECK_ARG(N >= 0 && T >= 0 && H >= 0, "%s: negative size", name);
-  SSLA_CHECK_ARG((K >= 1 && V >= 1 && K <= 64 && V <= 64) || tc_supported(dtype, dtype_g, K, V),
+  SSLA_CHECK_ARG(K >= 1 && V >= 1 && K <= 64 && V <= 64,
                  "%s: K=%lld V=%lld not supported (1 <= K, V <= 64 in this build)", name,
                  (long long)K, (long long)V);
   return SSLA_OK;
@@ -860,65 +902,71 @@ extern "C" int64_t ssla_chunk_gla_max_chunks(int64_t n_seqs, int64_t T) {
   return max_chunks(n_seqs, T);
 }
 
+extern "C" size_t ssla_chunk_gla_states_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
+                                              int dtype, int dtype_g) {
+  return saved_bytes(n_seqs, T, H, K, V, tc_shape(dtype, dtype_g, K, V));
+}
+
 extern "C" size_t ssla_chunk_gla_workspace_bytes(int64_t n_seqs, int64_t T, int64_t H, int64_t K,
-                                                 int64_t V) {
-  return workspace_bytes(n_seqs, T, H, K, V);
+                                                 int64_t V, int dtype, int dtype_g) {
+  return workspace_bytes(n_seqs, T, H, K, V, tc_shape(dtype, dtype_g, K, V));
 }
 
 extern "C" int ssla_chunk_gla_fwd(const void* q, const void* k, const void* v, const void* g,
                                   int dtype, int dtype_g, const int64_t* cu_seqlens,
                                   int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
                                   float scale, const float* h0, void* o, float* ht,
-                                  float* states, void* workspace, size_t workspace_bytes_,
-                                  ssla_stream_t stream) {
+                                  void* states, size_t states_bytes, void* workspace,
+                                  size_t workspace_bytes_, ssla_stream_t stream) {
   int rc = check_common("ssla_chunk_gla_fwd", dtype, dtype_g, n_seqs, T, H, K, V);
   if (rc) return rc;
   if (n_seqs == 0 || H == 0) return SSLA_OK;
   SSLA_CHECK_ARG(cu_seqlens && states && workspace, "ssla_chunk_gla_fwd: null pointer");
   SSLA_CHECK_ARG(T == 0 || (q && k && v && g && o), "ssla_chunk_gla_fwd: null pointer");
-  if (workspace_bytes_ < workspace_bytes(n_seqs, T, H, K, V)) {
+  const bool tc_layout = tc_shape(dtype, dtype_g, K, V);
+  if (states_bytes < saved_bytes(n_seqs, T, H, K, V, tc_layout)) {
+    set_error("ssla_chunk_gla_fwd: states buffer of %zu bytes < %zu needed", states_bytes,
+              saved_bytes(n_seqs, T, H, K, V, tc_layout));
+    return SSLA_ERR_WORKSPACE;
+  }
+  if (workspace_bytes_ < fwd_workspace_bytes(n_seqs, T, H, K, V)) {
     set_error("ssla_chunk_gla_fwd: workspace of %zu bytes < %zu needed", workspace_bytes_,
-              workspace_bytes(n_seqs, T, H, K, V));
+              fwd_workspace_bytes(n_seqs, T, H, K, V));
     return SSLA_ERR_WORKSPACE;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  Workspace w = carve(workspace, n_seqs, T, H, K, V);
+  const Saved sv = carve_saved(states, n_seqs, T, H, K, V, tc_layout);
+  const Workspace w = carve(workspace, n_seqs, T, H, K, V, tc_layout);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, w.flags, s))) return rc;
+  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, sv.chunk_off, sv.chunk_tab, sv.xlist, s))) return rc;
   const void* in[4] = {q, k, v, g};
-  const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 4);
+  const bool tc = tc_layout && tc_aligned(in, 4);
   if (MC > 0) {
-    if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 0, k, v, g, w.chunk_tab, T, MC, H, scale, w.dS, w.decay, s);
-    } else {
-      rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
-        return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-          return run_local<T_, Tg, P>(0, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, (int)H,
-                                      (int)K, (int)V, scale, w.dS, w.decay, s);
-        });
-      });
-    }
+    rc = tc ? tc_local_state(dtype, dtype_g, 0, k, v, g, sv.chunk_tab, T, MC, H, scale, w.dS, w.decay, w.escale,
+                             sv.xflag, sv.xlist, s)
+            : simt_local(dtype, dtype_g, 0, k, v, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, w.dS,
+                         w.decay, s);
     if (rc) return rc;
   }
-  if ((rc = launch_state_scan(w.dS, w.decay, w.chunk_off, n_seqs, H, K, V, h0, states, ht, false, s)))
+  if ((rc = launch_state_scan(w.dS, w.decay, sv.chunk_off, n_seqs, H, K, V, h0, sv.h32, tc ? sv.xflag : nullptr,
+                              tc ? sv.h16 : nullptr, dtype, w.escale, ht, false, s)))
     return rc;
   if (MC == 0) return SSLA_OK;
   if (tc) {
-    if ((rc = tc_fwd_o(dtype, dtype_g, q, k, v, g, w.chunk_tab, T, MC, H, scale, states, o, w.flags, s)))
-      return rc;
-    return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V,
-                      scale, states, o, w.flags, s);
+    if ((rc = tc_fwd_o(dtype, dtype_g, q, k, v, g, sv.chunk_tab, T, MC, H, scale, sv.h16, sv.xflag, o, s))) return rc;
+    return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, sv.h32, o,
+                      sv.xlist, s);
   }
-  return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V,
-                    scale, states, o, nullptr, s);
+  return simt_fwd_o(dtype, dtype_g, q, k, v, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, sv.h32, o,
+                    nullptr, s);
 }
 
 extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, const void* g,
                                   int dtype, int dtype_g, const int64_t* cu_seqlens,
                                   int64_t n_seqs, int64_t T, int64_t H, int64_t K, int64_t V,
-                                  float scale, const float* states, const void* dout,
-                                  const float* dht, void* dq, void* dk, void* dv, float* dg,
-                                  float* dh0, void* workspace, size_t workspace_bytes_,
+                                  float scale, const void* states, size_t states_bytes,
+                                  const void* dout, const float* dht, void* dq, void* dk, void* dv,
+                                  float* dg, float* dh0, void* workspace, size_t workspace_bytes_,
                                   ssla_stream_t stream) {
   int rc = check_common("ssla_chunk_gla_bwd", dtype, dtype_g, n_seqs, T, H, K, V);
   if (rc) return rc;
@@ -926,41 +974,42 @@ extern "C" int ssla_chunk_gla_bwd(const void* q, const void* k, const void* v, c
   SSLA_CHECK_ARG(cu_seqlens && states && workspace, "ssla_chunk_gla_bwd: null pointer");
   SSLA_CHECK_ARG(T == 0 || (q && k && v && g && dout && dq && dk && dv && dg),
                  "ssla_chunk_gla_bwd: null pointer");
-  if (workspace_bytes_ < workspace_bytes(n_seqs, T, H, K, V)) {
+  const bool tc_layout = tc_shape(dtype, dtype_g, K, V);
+  if (states_bytes < saved_bytes(n_seqs, T, H, K, V, tc_layout)) {
+    set_error("ssla_chunk_gla_bwd: states buffer of %zu bytes < %zu needed", states_bytes,
+              saved_bytes(n_seqs, T, H, K, V, tc_layout));
+    return SSLA_ERR_WORKSPACE;
+  }
+  if (workspace_bytes_ < workspace_bytes(n_seqs, T, H, K, V, tc_layout)) {
     set_error("ssla_chunk_gla_bwd: workspace of %zu bytes < %zu needed", workspace_bytes_,
-              workspace_bytes(n_seqs, T, H, K, V));
+              workspace_bytes(n_seqs, T, H, K, V, tc_layout));
     return SSLA_ERR_WORKSPACE;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  Workspace w = carve(workspace, n_seqs, T, H, K, V);
+  // the forward's chunk table, exact-item flags and states (read only)
+  const Saved sv = carve_saved(const_cast<void*>(states), n_seqs, T, H, K, V, tc_layout);
+  const Workspace w = carve(workspace, n_seqs, T, H, K, V, tc_layout);
   const int64_t MC = max_chunks(n_seqs, T);
-  if ((rc = launch_chunk_offsets(cu_seqlens, n_seqs, MC, w.chunk_off, w.chunk_tab, w.flags, s))) return rc;
   const void* in[5] = {q, k, v, g, dout};
-  const bool tc = tc_supported(dtype, dtype_g, K, V) && tc_aligned(in, 5);
+  const bool tc = tc_layout && tc_aligned(in, 5);
   if (MC > 0) {
-    if (tc) {
-      rc = tc_local_state(dtype, dtype_g, 1, q, dout, g, w.chunk_tab, T, MC, H, scale, w.dS, w.decay, s);
-    } else {
-      rc = SSLA_DISPATCH_QG(dtype, dtype_g, T_, Tg, [&] {
-        return SSLA_DISPATCH_PAD(pad_of(K, V), [&] {
-          return run_local<T_, Tg, P>(1, q, dout, g, cu_seqlens, w.chunk_tab, n_seqs, MC, (int)H,
-                                      (int)K, (int)V, scale, w.dS, w.decay, s);
-        });
-      });
-    }
+    rc = tc ? tc_local_state(dtype, dtype_g, 1, q, dout, g, sv.chunk_tab, T, MC, H, scale, w.dS, w.decay, w.escale,
+                             nullptr, nullptr, s)
+            : simt_local(dtype, dtype_g, 1, q, dout, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, w.dS,
+                         w.decay, s);
     if (rc) return rc;
   }
-  if ((rc = launch_state_scan(w.dS, w.decay, w.chunk_off, n_seqs, H, K, V, dht, w.dstates, dh0, true,
-                              s)))
+  if ((rc = launch_state_scan(w.dS, w.decay, sv.chunk_off, n_seqs, H, K, V, dht, w.dh32, tc ? sv.xflag : nullptr,
+                              tc ? w.dh16 : nullptr, dtype, w.escale, dh0, true, s)))
     return rc;
   if (MC == 0) return SSLA_OK;
   if (tc) {
-    if ((rc = tc_bwd(dtype, dtype_g, q, k, v, g, w.chunk_tab, T, MC, H, scale, states, w.dstates, dout, dq, dk,
-                     dv, dg, w.flags, s)))
+    if ((rc = tc_bwd(dtype, dtype_g, q, k, v, g, sv.chunk_tab, T, MC, H, scale, sv.h16, w.dh16, sv.xflag, dout, dq,
+                     dk, dv, dg, s)))
       return rc;
-    return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V, scale,
-                    states, w.dstates, dout, dq, dk, dv, dg, w.flags, s);
+    return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, sv.h32, w.dh32,
+                    dout, dq, dk, dv, dg, sv.xlist, s);
   }
-  return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, w.chunk_tab, n_seqs, MC, H, K, V, scale,
-                  states, w.dstates, dout, dq, dk, dv, dg, nullptr, s);
+  return simt_bwd(dtype, dtype_g, q, k, v, g, cu_seqlens, sv.chunk_tab, n_seqs, MC, H, K, V, scale, sv.h32, w.dh32,
+                  dout, dq, dk, dv, dg, nullptr, s);
 }

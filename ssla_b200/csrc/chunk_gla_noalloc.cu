@@ -8,8 +8,9 @@
 // image instead.
 //
 // The scratch is a file-scope __device__ array of kNoAllocScratchBytes (64 MiB), so every GPU
-// that loads the library holds those 64 MiB until the process exits.  Calls whose workspace
-// need exceeds it are rejected with SSLA_ERR_WORKSPACE.  All calls on one device share the
+// that loads the library holds those 64 MiB until the process exits.  Calls whose scratch
+// need (the forward's states buffer plus its workspace) exceeds it are rejected with
+// SSLA_ERR_WORKSPACE.  All calls on one device share the
 // array: two calls that overlap on the GPU (different streams, or host threads racing) would
 // corrupt each other's intermediates, so serialise them (one stream, or events).  The forward
 // writes every scratch byte it later reads, so nothing has to be cleared between calls.
@@ -31,6 +32,8 @@ void* g_scratch_ptr[kMaxDevices] = {};
 // g_noalloc_scratch is only a stand-in and must never be passed to a kernel; the real
 // address comes from cudaGetSymbolAddress with the device current.  Done once per device,
 // on that device's first call (which therefore should not happen during stream capture).
+// The address is kept for the life of the process: after cudaDeviceReset on a device the
+// cached address is stale, so this entry point must not be used on that device again.
 int scratch_on_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -66,24 +69,37 @@ extern "C" int ssla_chunk_gla_fwd_noalloc(const void* q, const void* k, const vo
                                           const float* h0, void* o, float* ht,
                                           ssla_stream_t stream) {
   using namespace ssla::chunk;
-  if (n_seqs < 0 || T < 0 || H < 0 || K < 0 || V < 0) {
-    ssla::set_error("ssla_chunk_gla_fwd_noalloc: negative size");
+  // the regular entry point's argument checks first, so the size arithmetic below only sees
+  // valid dtypes and 1 <= K, V <= 64
+  if (!ssla::dtype_ok(dtype) || (dtype_g != dtype && dtype_g != SSLA_F32)) {
+    ssla::set_error("ssla_chunk_gla_fwd_noalloc: bad dtype");
     return SSLA_ERR_INVALID_ARG;
   }
-  const size_t ws = workspace_bytes(n_seqs, T, H, K, V);
-  const size_t st = align256(4 * (size_t)(max_chunks(n_seqs, T) > 0 ? max_chunks(n_seqs, T) : 1) * H * K * V);
-  if (ws + st > kNoAllocScratchBytes) {
+  if (n_seqs < 0 || T < 0 || H < 0 || K < 1 || V < 1 || K > 64 || V > 64) {
+    ssla::set_error("ssla_chunk_gla_fwd_noalloc: bad size (N, T, H >= 0 and 1 <= K, V <= 64)");
+    return SSLA_ERR_INVALID_ARG;
+  }
+  // Bound the chunk count by division before multiplying: every (chunk, head) needs at least
+  // K*V*4 bytes of scratch, so more than kNoAllocScratchBytes / (4*K*V) of them cannot fit.
+  // n_seqs and T are bounded first so that max_chunks() cannot overflow.
+  const int64_t lim = (int64_t)kNoAllocScratchBytes;
+  const int64_t MC = (n_seqs > lim || T > lim) ? lim : max_chunks(n_seqs, T);
+  const bool fits = H == 0 || MC == 0 || MC <= lim / (4 * K * V) / H;
+  const bool tc = tc_shape(dtype, dtype_g, K, V);
+  const size_t st = fits ? saved_bytes(n_seqs, T, H, K, V, tc) : 0;
+  const size_t ws = fits ? fwd_workspace_bytes(n_seqs, T, H, K, V) : 0;
+  if (!fits || st + ws > kNoAllocScratchBytes) {
     ssla::set_error(
-        "ssla_chunk_gla_fwd_noalloc: this shape needs %zu bytes of scratch, more than the "
-        "%zu-byte built-in limit; use ssla_chunk_gla_fwd with a caller-allocated workspace",
-        ws + st, kNoAllocScratchBytes);
+        "ssla_chunk_gla_fwd_noalloc: this shape needs more scratch than the %zu-byte built-in "
+        "limit; use ssla_chunk_gla_fwd with caller-allocated buffers",
+        kNoAllocScratchBytes);
     return SSLA_ERR_WORKSPACE;
   }
   void* base = nullptr;
   int rc = scratch_on_current_device(&base);
   if (rc) return rc;
-  float* states = (float*)base;
+  void* states = base;
   void* workspace = (char*)base + st;
   return ssla_chunk_gla_fwd(q, k, v, g, dtype, dtype_g, cu_seqlens, n_seqs, T, H, K, V, scale, h0,
-                            o, ht, states, workspace, ws, stream);
+                            o, ht, states, st, workspace, ws, stream);
 }

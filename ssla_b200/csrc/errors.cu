@@ -17,5 +17,5 @@ const char* get_error() { return g_last_error; }
 
 }  // namespace ssla
 
-extern "C" int ssla_abi_version(void) { return 1; }
+extern "C" int ssla_abi_version(void) { return 2; }
 extern "C" const char* ssla_last_error(void) { return ssla::get_error(); }

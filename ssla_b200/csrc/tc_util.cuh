@@ -169,6 +169,27 @@ __device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, float* v) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16x256b.x4 load without the wait (warp-collective): 16 TMEM lanes x 32 columns.  Thread t
+// receives pairs p = 0..7: v[2p], v[2p+1] = lane (t/4) + 8*(p&1), columns 2*(t%4) + 8*(p>>1)
+// + {0, 1}.  Call tmem_wait_ld() before using the values.
+__device__ __forceinline__ void tmem_ld16x256b_x4_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Ties 16 registers of a tcgen05.ld to this point of the program: placed after
+// tmem_wait_ld(), it keeps the compiler from moving their uses above the wait.
+__device__ __forceinline__ void reg_fence16(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
 // 32x32b.x32 load (warp-collective): thread t receives TMEM lane (address lane + t), 32
 // consecutive columns.  The warp may only address the 32-lane subpartition warp_id % 4.
 __device__ __forceinline__ void tmem_ld32x32b_x32(uint32_t taddr, float* v) {

@@ -33,25 +33,27 @@ def norm_inputs(q, k, v, g):
 
 
 def chunk_gla_fwd(q, k, v, g, scale, initial_state, output_final_state, cu_seqlens):
-    """Returns (o, ht or None, states).  ``states`` [max_chunks, H, K, V] fp32 holds the state at
-    every chunk start and is what the backward consumes."""
+    """Returns (o, ht or None, states).  ``states`` is the opaque device buffer the forward
+    leaves for the backward (the chunk table, which chunks the exact kernels handle, and the
+    state at every chunk start)."""
     T, H, K = q.shape
     V = v.shape[-1]
     N = cu_seqlens.numel() - 1
     L = _lib.load()
-    MC = L.ssla_chunk_gla_max_chunks(N, T)
     dev = q.device
+    dt, dtg = _lib.dtype_code(q), _lib.dtype_code(g)
     o = torch.empty_like(v)
-    states = torch.empty((max(MC, 1), H, K, V), device=dev, dtype=torch.float32)
+    st_bytes = L.ssla_chunk_gla_states_bytes(N, T, H, K, V, dt, dtg)
+    states = torch.empty(max(st_bytes, 1), device=dev, dtype=torch.uint8)
     ht = torch.empty((N, H, K, V), device=dev, dtype=torch.float32) if output_final_state else None
     h0 = initial_state.float().contiguous() if initial_state is not None else None
-    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, T, H, K, V)
+    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, T, H, K, V, dt, dtg)
     ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
     _lib.check(
         L.ssla_chunk_gla_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), _lib.dtype_code(q),
-            _lib.dtype_code(g), cu_seqlens.data_ptr(), N, T, H, K, V, float(scale), _lib.ptr(h0),
-            o.data_ptr(), _lib.ptr(ht), states.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_of(q),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), dt, dtg, cu_seqlens.data_ptr(), N, T, H, K, V,
+            float(scale), _lib.ptr(h0), o.data_ptr(), _lib.ptr(ht), states.data_ptr(), st_bytes, ws.data_ptr(),
+            ws_bytes, _lib.stream_of(q),
         ),
         "chunk_gla forward",
     )
@@ -64,6 +66,7 @@ def chunk_gla_bwd(q, k, v, g, scale, has_h0, states, do, dht, cu_seqlens):
     N = cu_seqlens.numel() - 1
     L = _lib.load()
     dev = q.device
+    dt, dtg = _lib.dtype_code(q), _lib.dtype_code(g)
     do = do.to(q.dtype).contiguous()
     dht = dht.float().contiguous() if dht is not None else None
     dq = torch.empty_like(q)
@@ -71,14 +74,13 @@ def chunk_gla_bwd(q, k, v, g, scale, has_h0, states, do, dht, cu_seqlens):
     dv = torch.empty_like(v)
     dg = torch.empty(g.shape, device=dev, dtype=torch.float32)
     dh0 = torch.empty((N, H, K, V), device=dev, dtype=torch.float32) if has_h0 else None
-    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, T, H, K, V)
+    ws_bytes = L.ssla_chunk_gla_workspace_bytes(N, T, H, K, V, dt, dtg)
     ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
     _lib.check(
         L.ssla_chunk_gla_bwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), _lib.dtype_code(q),
-            _lib.dtype_code(g), cu_seqlens.data_ptr(), N, T, H, K, V, float(scale), states.data_ptr(),
-            do.data_ptr(), _lib.ptr(dht), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
-            _lib.ptr(dh0), ws.data_ptr(), ws_bytes, _lib.stream_of(q),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), dt, dtg, cu_seqlens.data_ptr(), N, T, H, K, V,
+            float(scale), states.data_ptr(), states.numel(), do.data_ptr(), _lib.ptr(dht), dq.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), _lib.ptr(dh0), ws.data_ptr(), ws_bytes, _lib.stream_of(q),
         ),
         "chunk_gla backward",
     )

@@ -156,10 +156,52 @@ def main(ref_root: str):
         print(variant, [g.shape for g in grids], float(grids[0].abs().sum()), head_out.shape)
 
 
+def batch8(ref_root: str):
+    """SSLA-S (MOS_S) forward at batch 8 (BASELINE config 5 with 8 samples, the per-GPU share
+    of the batch of 64 on 8 GPUs): backbone grids and head output of the reference model.
+    Same shims as ``main``; inputs ``event_batch(8, seed=21)``, weights ``seeded_parameters``
+    with seed 2025."""
+    import yaml
+    import ops.common.scan as scan_mod
+    import layers.mos_attention as mos_mod
+    import layers.linear_attention as lin_mod
+
+    scan_mod.scan = lambda u, g, cu_seqlens: og.scan_ref_vectorized(u, g, cu_seqlens)
+    mos_mod.scan = scan_mod.scan
+    lin_mod.scan = scan_mod.scan
+    from model_mos import MosModel
+
+    torch.set_grad_enabled(False)
+    B = 8
+    events, lengths = event_batch(B, seed=21)
+    cfg = yaml.safe_load(open(Path(ref_root) / "configs" / "model" / "MOS_S.yaml"))
+    model = MosModel(cfg, hot_pixel_thres=50, dataset="Gen1").eval()
+    seeded_parameters(model, 2025)
+    x = model.preprocess_inputs(events.clone(), lengths.clone())
+    taps = []
+    for i, layer in enumerate(model.backbone):
+        x = layer(x)
+        if i in model.output_indices:
+            taps.append(x)
+    grids = [model.async_event_to_grid(t, k).float() for k, t in enumerate(taps)]
+    # the head also computes its training losses, so it needs labels: one box per sample
+    labels = torch.tensor([[[60.0 + 20 * b, 50.0 + 15 * b, 40.0, 30.0, float(b % 2)]] for b in range(B)])
+    head_out = model.head(grids, labels)["output"]
+    torch.save(dict(batch=B, seed=21, param_seed=2025, grids=grids, head=head_out), OUT / "model_mos_s_b8.pt")
+    print("S batch 8", [g.shape for g in grids], head_out.shape)
+
+
 if __name__ == "__main__":
     if len(sys.argv) not in (2, 3):
-        sys.exit("usage: make_golden_model.py <path to the ssla sources> [--linear-attention-only]")
-    if len(sys.argv) == 3:
+        sys.exit("usage: make_golden_model.py <path to the ssla sources> [--linear-attention-only | --batch8]")
+    if len(sys.argv) == 3 and sys.argv[2] == "--batch8":
+        install_shims()
+        _sort = torch.sort
+        torch.sort = lambda input, dim=-1, descending=False, stable=True, *, out=None: _sort(
+            input, dim=dim, descending=descending, stable=True)
+        sys.path.insert(0, sys.argv[1])
+        batch8(sys.argv[1])
+    elif len(sys.argv) == 3:
         install_shims()
         _sort = torch.sort
         torch.sort = lambda input, dim=-1, descending=False, stable=True, *, out=None: _sort(

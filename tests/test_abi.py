@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for n in _declared():
         assert hasattr(lib, n), n
     assert set(_declared()) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
-    assert lib.ssla_abi_version() == 1
+    assert lib.ssla_abi_version() == 2
 
 
 def test_size_queries_without_gpu():
@@ -35,7 +35,12 @@ def test_size_queries_without_gpu():
 
     lib = _lib.load()
     assert lib.ssla_chunk_gla_max_chunks(8, 16384) == (16384 + 63 * 8) // 64
-    assert lib.ssla_chunk_gla_workspace_bytes(8, 16384, 4, 64, 64) > 2 * 263 * 4 * 64 * 64 * 4
+    # bf16, K = V = 64: fp32 increments and adjoints plus the 16-bit adjoint copy
+    assert lib.ssla_chunk_gla_workspace_bytes(8, 16384, 4, 64, 64, 1, 1) >= 263 * 4 * 64 * 64 * (4 + 4 + 2)
+    # the states buffer holds fp32 and 16-bit chunk-start states on the tensor-core path only
+    tc = lib.ssla_chunk_gla_states_bytes(8, 16384, 4, 64, 64, 1, 1)
+    simt = lib.ssla_chunk_gla_states_bytes(8, 16384, 4, 64, 64, 0, 0)
+    assert simt >= 263 * 4 * 64 * 64 * 4 and tc - simt >= 263 * 4 * 64 * 64 * 2
 
 
 def test_invalid_args_report_errors():
@@ -46,7 +51,7 @@ def test_invalid_args_report_errors():
     assert rc == -1
     assert b"dtype" in lib.ssla_last_error()
     rc = lib.ssla_chunk_gla_fwd(None, None, None, None, 0, 0, None, 1, 10, 1, 300, 300, 1.0,
-                                None, None, None, None, None, 0, None)
+                                None, None, None, None, 0, None, 0, None)
     assert rc == -1 and b"not supported" in lib.ssla_last_error()
 
 

@@ -5,7 +5,7 @@ import pytest
 import torch
 import yaml
 
-from conftest import GOLDEN, ROOT, rel_err
+from conftest import GOLDEN, ROOT, assert_close, rel_err
 
 pytestmark = pytest.mark.gpu
 FP32_TOL = 1e-5
@@ -115,6 +115,32 @@ def test_full_model_matches_reference(variant, gold_s):
     # the head decode exponentiates box sizes (x up to ~300): 1e-4 relative for the dense head
     assert head.shape == gold["head"].shape
     assert rel_err(head, gold["head"]) < 1e-4
+
+
+def test_full_model_s_batch8_matches_reference():
+    """SSLA-S at batch 8 (the per-GPU share of BASELINE config 5's batch of 64 on 8 GPUs): backbone
+    grids and head output against the reference MosModel on the CPU
+    (tests/golden/make_golden_model.py --batch8: event_batch(8, seed=21), weights seed 2025)."""
+    from ssla_b200.synthetic import event_batch
+
+    gold = torch.load(GOLDEN / "model_mos_s_b8.pt")
+    m = _model("S")
+    ev, ln = event_batch(gold["batch"], seed=gold["seed"])
+    from ssla_b200.model import async_event_to_grid, preprocess_inputs
+
+    with torch.no_grad():
+        x = preprocess_inputs(ev.cuda(), ln.cuda(), m.frame_size, m.hot_pixel_thres)
+        taps = []
+        for i, layer in enumerate(m.backbone):
+            x = layer(x)
+            if i in m.output_indices:
+                taps.append(x)
+        grids = [async_event_to_grid(t, m.grid_sizes[k], m.in_features[k]) for k, t in enumerate(taps)]
+        for i, (a, b) in enumerate(zip(grids, gold["grids"])):
+            assert_close(a, b, FP32_TOL, f"grid {i}")
+        torch.backends.cudnn.allow_tf32 = False
+        head = m.head(grids)
+    assert_close(head, gold["head"], 1e-4, "head")
 
 
 def test_layers_backward_runs():

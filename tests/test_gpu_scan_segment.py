@@ -144,3 +144,33 @@ def test_segment_op_gradients_match_torch():
     seg.gather_rows_ad(a, gi.cuda()).backward(g2.cuda())
     b[gi].backward(g2)
     assert torch.allclose(a.grad.cpu(), b.grad, atol=1e-6)
+
+
+@pytest.mark.parametrize("k", [2, 4])
+def test_c4_pooling_full_size_bit_exact(k):
+    """BASELINE config 4 exactly as specified (16 batches x 2 polarity planes at 240x304, ~5% active
+    pixels half uniform / half in 20 sigma-8 blobs, Poisson(3) events per pixel, int64 flat
+    indices, C=64 bf16): scatter_max values and argmax, scatter_mean and the gather back to the
+    rows, through the torch_scatter interface (expanded index, as layers/sparse_pooling.py:33
+    calls it) and through the sorted-segment path the pooling layer uses; bit-exact against the
+    CPU oracle."""
+    from ssla_b200 import torch_scatter as ts
+    from ssla_b200.ops import segment as seg
+    from ssla_b200.synthetic import pooling_rows
+
+    feats, idx, cells = pooling_rows(seed=0)
+    inv, S = cells[k]
+    R, C = feats.shape
+    assert R > 300_000 and C == 64 and feats.dtype == torch.bfloat16
+    mx_r, arg_r = oseg.scatter_max(feats, inv, S)
+    mean_r = oseg.scatter_mean(feats, inv, S)
+    back_r = mx_r[inv]
+    f, ic = feats.cuda(), inv.cuda()
+    mx, arg = ts.scatter_max(f, ic[:, None].expand(R, C), dim=0, dim_size=S)
+    assert torch.equal(mx.cpu(), mx_r) and torch.equal(arg.cpu(), arg_r)
+    assert torch.equal(ts.scatter_mean(f, ic[:, None].expand(R, C), dim=0, dim_size=S).cpu(), mean_r)
+    off = seg.segment_offsets_sorted(ic, S)
+    mx2, arg2 = seg.segment_reduce(f, off, None, seg.MAX, want_arg=True)
+    mn2, _ = seg.segment_reduce(f, off, None, seg.MEAN)
+    assert torch.equal(mx2.cpu(), mx_r) and torch.equal(arg2.cpu(), arg_r) and torch.equal(mn2.cpu(), mean_r)
+    assert torch.equal(seg.gather_rows(mx2, ic).cpu(), back_r)

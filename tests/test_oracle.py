@@ -74,3 +74,45 @@ def test_segment_oracle_semantics():
     assert torch.equal(s, oseg.scatter_sum_fast(src, idx, 4))
     ref = torch.zeros(4, 2).index_add_(0, idx, src)
     assert torch.equal(oseg.index_add_rows(src, idx, 4), ref)
+
+
+def test_recurrent_step_equals_naive_recurrent():
+    """The vectorised one-token step equals the token recurrence on one-token sequences with a
+    carried state (the streaming use of BASELINE config 3)."""
+    gen = torch.Generator().manual_seed(4)
+    N, H, K, V = 7, 3, 8, 5
+    S = torch.randn(N, H, K, V, generator=gen)
+    for _ in range(3):
+        q, k, g = (torch.randn(N, H, K, generator=gen) for _ in range(3))
+        v = torch.randn(N, H, V, generator=gen)
+        g = torch.nn.functional.logsigmoid(g)
+        o_r, S_r = og.naive_gla_recurrent(q, k, v, g, torch.arange(N + 1), initial_state=S, output_final_state=True)
+        o, S = og.naive_gla_recurrent_step(q, k, v, g, S)
+        assert torch.allclose(o, o_r, rtol=1e-6, atol=1e-6) and torch.allclose(S, S_r, rtol=1e-6, atol=1e-6)
+
+
+def test_segment_oracle_matches_torch_scatter_reduce():
+    """The segment oracle against an independent implementation of the same documented
+    semantics: PyTorch's own CPU scatter_reduce (amax / mean / sum with include_self=False,
+    empty segments left at 0).  torch_scatter itself is not installed anywhere here."""
+    from oracle import segment as oseg
+
+    gen = torch.Generator().manual_seed(9)
+    R, C, S = 5000, 16, 1300  # some segments empty
+    idx = torch.randint(0, S, (R,), generator=gen)
+    src = torch.randn(R, C, generator=gen)
+    src[::5] = src[2]  # ties
+    ex = idx[:, None].expand(R, C)
+    mx, arg = oseg.scatter_max(src, idx, S)
+    ref = torch.zeros(S, C).scatter_reduce_(0, ex, src, reduce="amax", include_self=False)
+    assert torch.equal(mx, ref)
+    # argmax: a row of the segment holding the max, the first such row
+    nonempty = torch.bincount(idx, minlength=S) > 0
+    a = arg[nonempty]
+    assert torch.equal(idx[a], torch.arange(S)[nonempty][:, None].expand_as(a))
+    assert torch.equal(src.gather(0, a), mx[nonempty])
+    assert (arg[~nonempty] == R).all()
+    mean_ref = torch.zeros(S, C).scatter_reduce_(0, ex, src, reduce="mean", include_self=False)
+    assert torch.allclose(oseg.scatter_mean(src, idx, S), mean_ref, rtol=1e-6, atol=1e-7)
+    sum_ref = torch.zeros(S, C).scatter_reduce_(0, ex, src, reduce="sum", include_self=False)
+    assert torch.equal(oseg.scatter_sum_fast(src, idx, S), sum_ref)
