@@ -183,6 +183,103 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# MOS_S scan calls per 2 samples of BASELINE config 5 (T tokens, C channels, N sequences):
+# the shapes the reference's layers/mos_attention.py:115 hands to ops.common.scan.
+SCAN_SHAPES = [(58360, 12, 41371), (519479, 12, 129033), (249056, 24, 36456), (249056, 24, 36456),
+               (91583, 48, 9120), (91583, 48, 9120), (24758, 96, 2280), (24758, 96, 2280)]
+
+
+def scan_inputs(dev, seed=0):
+    """fp32 (u, g in (0, 1), cu_seqlens, dh) per SCAN_SHAPES entry; sequence lengths are a uniform
+    random composition of T into N parts (every sequence non-empty)."""
+    out = []
+    for i, (Tt, C, Nn) in enumerate(SCAN_SHAPES):
+        gen = torch.Generator().manual_seed(seed + i)
+        cuts = torch.randperm(Tt - 1, generator=gen)[: Nn - 1].sort().values + 1
+        cu = torch.cat([torch.zeros(1, dtype=torch.int64), cuts, torch.tensor([Tt])]).to(dev)
+        u = torch.randn(Tt, C, generator=gen).to(dev)
+        g = torch.sigmoid(torch.randn(Tt, C, generator=gen)).to(dev)
+        dh = torch.randn(Tt, C, generator=gen).to(dev)
+        out.append((u, g, cu, dh))
+    return out
+
+
+def time_api(chunk_fn, scan_fn, dev, steps, warmup):
+    """Device time (CUDA events, L2 flushed before each step, inputs resident) of chunk_gla
+    fwd+bwd on config 2 and of the MOS_S scan set fwd+bwd through an implementation's public
+    Python API (autograd).  Returns (chunk ms, scan ms)."""
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    d = {n: t.to(dev) for n, t in make_inputs(1000).items()}
+    sc = scan_inputs(dev)
+
+    def chunk_step():
+        leaves = [d[n].detach().requires_grad_() for n in ("q", "k", "v", "g")]
+        h0 = d["h0"].detach().requires_grad_()
+        o, ht = chunk_fn(*leaves, d["cu"], initial_state=h0, output_final_state=True)
+        torch.autograd.backward([o, ht], [d["do"], d["dht"]])
+
+    def scan_step():
+        for u, g, cu, dh in sc:
+            uu, gg = u.detach().requires_grad_(), g.detach().requires_grad_()
+            scan_fn(uu, gg, cu).backward(dh)
+
+    res = []
+    for fn in (chunk_step, scan_step):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        res.append(1e3 * _event_time(fn, steps, stream, flush) / steps)
+    return res
+
+
+def run_triton_reference(args):
+    """The reference's own Triton chunk_gla (ops/gla/chunk.py:1119-1167) and scan
+    (ops/common/scan.py:140-163), unmodified, imported from the offline install in
+    baseline/_ref, timed on this GPU.  Runs in its own process, which never imports ssla_b200."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "ops" / "gla" / "chunk.py").exists():
+        print(json.dumps({"unavailable": "reference not installed in baseline/_ref (bash baseline/install_ref.sh)"}))
+        return
+    sys.path.insert(0, str(ref))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from ops.common.scan import scan as ref_scan
+    from ops.gla.chunk import chunk_gla as ref_chunk
+
+    with Clocks(0) as clk:
+        chunk_ms, scan_ms = time_api(ref_chunk, ref_scan, dev, args.steps, args.warmup)
+    assert "ssla_b200" not in sys.modules
+    print(json.dumps({"chunk_ms": chunk_ms, "scan_ms": scan_ms, "clocks": clk.summary(),
+                      "triton": __import__("triton").__version__}), flush=True)
+
+
+def triton_reference_line(dev, steps, warmup):
+    """Reference Triton timings (subprocess) next to ours through the same public-API harness."""
+    import subprocess
+
+    from ssla_b200.ops.common.scan import scan as our_scan
+    from ssla_b200.ops.gla.chunk import chunk_gla as our_chunk
+
+    try:
+        r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--leg", "triton-reference", "--steps",
+                            str(steps), "--warmup", str(warmup)], capture_output=True, text=True, timeout=900,
+                           env={**os.environ, "CUDA_VISIBLE_DEVICES": os.environ.get("CUDA_VISIBLE_DEVICES", "0")})
+        lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+        ref = json.loads(lines[-1]) if lines else {"unavailable": (r.stderr or "no output").strip().splitlines()[-1][:300]}
+    except subprocess.TimeoutExpired:
+        ref = {"unavailable": "reference Triton run exceeded 900 s (autotuning)"}
+    ours_chunk, ours_scan = time_api(our_chunk, our_scan, dev, steps, warmup)
+    out = {"what": "device ms per call through each implementation's public API (autograd fwd+bwd), inputs "
+                   "resident, L2 flushed: chunk_gla on BASELINE config 2; scan on the 8 MOS_S scan shapes of 2 "
+                   "samples of config 5 (fp32)",
+           "ours_chunk_ms": ours_chunk, "ours_scan_ms": ours_scan, "reference": ref}
+    if "chunk_ms" in ref:
+        out["chunk_speedup"] = ref["chunk_ms"] / ours_chunk
+        out["scan_speedup"] = ref["scan_ms"] / ours_scan
+    return out
+
+
 def _dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -460,7 +557,12 @@ def main():
                     help="chunk: headline (BASELINE config 2); recurrent: config 3; pool: config 4; "
                          "model: config 5 frames/s")
     ap.add_argument("--no-model", action="store_true", help="skip the SSLA-S frames/s field of the headline")
+    ap.add_argument("--no-triton-reference", action="store_true",
+                    help="skip timing the reference's Triton kernels on this GPU")
+    ap.add_argument("--leg", default=None, choices=["triton-reference"], help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.leg == "triton-reference":
+        return run_triton_reference(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload != "chunk":
@@ -612,6 +714,9 @@ def main():
     e2e_value = world * TOKENS * args.steps / e2e_secs
 
     model_line = None if args.no_model else bench_model(dev, world, rank, dist, steps=3, warmup=2)
+    triton_ref = None
+    if rank == 0 and world == 1 and not args.no_triton_reference:
+        triton_ref = triton_reference_line(dev, steps=10, warmup=3)
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -649,6 +754,7 @@ def main():
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "ssla_s": model_line,
+        "triton_reference": triton_ref,
     }
     print(json.dumps(line), flush=True)
     if dist is not None:

@@ -124,6 +124,25 @@ int ssla_chunk_gla_fwd_noalloc(const void* q, const void* k, const void* v, cons
                                int64_t T, int64_t H, int64_t K, int64_t V, float scale,
                                const float* h0, void* o, float* ht, ssla_stream_t stream);
 
+/* ------------------------------------------------------------------ pixel grouping
+ * group_events (utils/farsecnn_utils.py:130-174, utils/async_utils.py:10-84) followed, with
+ * keep_first, by the hot-pixel truncation of model_mos.py:173-209: events [B,Nmax,C] fp32 rows
+ * <x, y, t, features...> with lengths [B] are grouped by (sample, pixel) in ascending id order,
+ * events of a group in input order, the last max_per_px of each group kept, then the first
+ * keep_first of those (pass INT64_MAX for no truncation).  Two calls with one host read
+ * between: _count fills the workspace and writes totals[3] = {events, groups G, kept K} (int32,
+ * device); _emit writes batch_id,h,w,lengths [G] int64 and time [K] int64, features [K,C-3]
+ * fp32 (with dt_col >= 0 that feature column becomes the pixel delay of model_mos.py:190-200).
+ * Requires B*H*W and B*Nmax below 2^31. */
+size_t ssla_group_events_workspace_bytes(int64_t B, int64_t Nmax, int64_t H, int64_t W);
+int ssla_group_events_count(const float* events, int64_t B, int64_t Nmax, int64_t C, const int64_t* lengths,
+                            int64_t H, int64_t W, int64_t max_per_px, int64_t keep_first, void* workspace,
+                            size_t workspace_bytes, int* totals, ssla_stream_t stream);
+int ssla_group_events_emit(const float* events, int64_t B, int64_t Nmax, int64_t C, int64_t H, int64_t W,
+                           int64_t max_per_px, int64_t keep_first, const void* workspace, int64_t G, int64_t K,
+                           int dt_col, int64_t* batch_id, int64_t* h, int64_t* w, int64_t* lengths, int64_t* time,
+                           float* features, ssla_stream_t stream);
+
 /* ------------------------------------------------------------------ segments
  * Reductions of rows of src [R,C] into out [S,C] by a row->segment index [R] (int64).
  * Semantics of torch_scatter.scatter_max / scatter_mean / scatter_sum (dim=0) as called

@@ -9,6 +9,9 @@ path never calls it.
 Pinning: the restatements are checked against golden vectors produced by the reference's own
 code (``tests/golden/make_golden.py`` imports the reference and runs its naive PyTorch forms
 and its Triton kernels under the Triton CPU interpreter); see ``tests/test_oracle.py``.
+``oracle.routing`` restates the pixel grouping of utils/farsecnn_utils.py:130-174 and the model
+preprocessing of model_mos.py:173-209; it is pinned against the reference model's own grouped
+output (tests/golden/model_mos_s.pt, tests/test_oracle.py).
 ``torch_scatter`` is not installed anywhere in this environment, so the segment-reduction
 oracle (``oracle.segment``) restates its documented semantics: parity unpinned for
 torch_scatter itself.

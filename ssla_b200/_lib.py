@@ -63,6 +63,9 @@ SIGNATURES = {
     "ssla_dat_decode_windows": (i32, [p, p, p, i64, i64, p, p]),
     "ssla_split_tf32": (i32, [p, i64, p, p, p]),
     "ssla_chunk_gla_tc_timeouts": (i32, [i32, p]),
+    "ssla_group_events_workspace_bytes": (sz, [i64, i64, i64, i64]),
+    "ssla_group_events_count": (i32, [p, i64, i64, i64, p, i64, i64, i64, i64, p, sz, p, p]),
+    "ssla_group_events_emit": (i32, [p, i64, i64, i64, i64, i64, i64, i64, p, i64, i64, i32, p, p, p, p, p, p, p]),
     "ssla_gemm_f32_tc": (i32, [p, i64, i64, i64, p, p, i64, i64, p, i64, p, p]),
     "ssla_rows_matmul_f32": (i32, [p, i64, i64, i64, p, i64, p, i64, p]),
 }

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(1024) chunk_offsets_kernel(const int64_t* __re
 // value is written to h32 (fp32; every chunk when xflag is null, else only flagged items) and,
 // for the tensor-core kernels, escale[chunk][k] * value to h16 in the 16-bit operand dtype T16
 // (T16 = float: no 16-bit output).
-constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8, SCAN_U = 8;
+constexpr int SCAN_EL = 32, SCAN_MAXSEG = 8;
 
 // VEC consecutive state elements (one key row, consecutive value columns) per thread.
 template <int VEC> struct SVec;
@@ -159,7 +159,7 @@ template <> struct SVec<4> {
 };
 
 template <int VEC, typename T16>
-__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
+__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
     const float* __restrict__ init, float* __restrict__ h32, const unsigned char* __restrict__ xflag,
@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
   using S = SVec<VEC>;
   using vec = typename S::type;
   constexpr bool kOut16 = !std::is_same<T16, float>::value;
+  constexpr int SCAN_U = VEC == 4 ? 4 : 8;  // chunks whose loads are in flight together
   __shared__ float sA[SCAN_MAXSEG][SCAN_EL];
   __shared__ vec sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
   const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, 4) state_scan_kernel(
     if (valid && fin) S::st(fin + idx, S::fma(A, x, B));
   }
   // 3. re-walk from the start value, writing the state at every chunk
-  auto put = [&](int64_t e, int64_t dd, int64_t f, const vec& val) {
+  auto put = [&](int64_t e, int64_t dd, int64_t f, vec val) {
     if (!xflag || xflag[f]) S::st(h32 + e, val);
     if constexpr (kOut16) S::template st16<T16>(h16 + e, escale[dd], val);
   };

@@ -111,6 +111,10 @@ struct GateSmem {
   float part[NG][D];  // per-group partial sums (gate scan, dgL, dg reverse cumsum)
 };
 
+// Barrier over the NT compute threads (named barrier 1; a producer warp, where a kernel has
+// one, never joins it).
+__device__ __forceinline__ void cbar() { named_barrier(1, NT); }
+
 // Thread t owns row tr = t % 64, 16-byte pieces at columns tc .. tc+7 and tc+32 .. tc+39
 // (tc = 8 * (t / 64)) of every 16-bit tile in the gating and tail-zeroing passes.
 struct Own {
@@ -186,7 +190,7 @@ __device__ __forceinline__ void zero_tail(unsigned char* dst16, int n16, unsigne
 // q = tid / 64) scans rows RG*q .. RG*q+RG-1 of its column serially in registers; the group
 // offsets and ref (gc of row 31, the end of group 31 / RG) come from the group totals.
 template <typename Tg>
-__device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw) {
+__device__ __forceinline__ void gate_prep(float* __restrict__ E, float (*part)[D], const unsigned char* raw) {
   const int tid = threadIdx.x, c = tid & 63, qt = tid >> 6;
   const Tg* gr = reinterpret_cast<const Tg*>(raw);
   float x[RG];
@@ -196,25 +200,25 @@ __device__ __forceinline__ void gate_prep(GateSmem& G, const unsigned char* raw)
     run += ldf(gr + (RG * qt + i) * D + c);
     x[i] = run;
   }
-  G.part[qt][c] = run;
-  __syncthreads();
+  part[qt][c] = run;
+  cbar();
   float off = 0.f, ref = 0.f;
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
-    const float pj = G.part[j][c];
+    const float pj = part[j][c];
     if (j < qt) off += pj;
     if (j <= 31 / RG) ref += pj;
   }
 #pragma unroll
-  for (int i = 0; i < RG; ++i) G.E[(RG * qt + i) * LDG + c] = __expf((x[i] + off) - ref);
-  __syncthreads();
+  for (int i = 0; i < RG; ++i) E[(RG * qt + i) * LDG + c] = __expf((x[i] + off) - ref);
+  cbar();
 }
 
 // Gate the staged q and k chunks of this thread: Q^ = scale q E, K^ = k / E, written to dQ /
 // dK (which may be the source tiles themselves).
 template <typename T>
 __device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned char* sK, unsigned char* dQ,
-                                        unsigned char* dK, const GateSmem& G, const Own& me, float scale) {
+                                        unsigned char* dK, const float* __restrict__ E, const Own& me, float scale) {
 #pragma unroll
   for (int pc = 0; pc < 2; ++pc) {
     const int off = pc ? me.off1 : me.off0;
@@ -222,7 +226,7 @@ __device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned 
     const uint4 uk = *reinterpret_cast<const uint4*>(sK + off);
     const T* xq = reinterpret_cast<const T*>(&uq);
     const T* xk = reinterpret_cast<const T*>(&uk);
-    const float* e = G.E + me.tr * LDG + me.tc + 32 * pc;
+    const float* e = E + me.tr * LDG + me.tc + 32 * pc;
     float yq[8], yk[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -238,7 +242,7 @@ __device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned 
 __device__ __forceinline__ void operands_ready() {
   fence_proxy_async();
   fence_before();
-  __syncthreads();
+  cbar();
   fence_after();
 }
 
@@ -275,6 +279,23 @@ constexpr size_t kAlignSlack = 1024;
 __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
   return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
 }
+
+// Phase timing (built only with -DSSLA_PHASE_PROF, for kernel development): thread 0 of each
+// CTA records clock64() at numbered points of its first kPhaseItems items into g_phase
+// [CTA][item][point]; ssla_chunk_gla_phase_dump copies the table out.
+constexpr int kPhaseItems = 8, kPhasePts = 16, kPhaseCtas = 1024;
+#ifdef SSLA_PHASE_PROF
+__device__ long long g_phase[kPhaseCtas * kPhaseItems * kPhasePts];
+#define PHASE(item, k)                                                                                  \
+  do {                                                                                                  \
+    if (threadIdx.x == 0 && (item) < kPhaseItems && blockIdx.x < kPhaseCtas)                            \
+      g_phase[(blockIdx.x * kPhaseItems + (item)) * kPhasePts + (k)] = clock64();                       \
+  } while (0)
+#else
+#define PHASE(item, k) \
+  do {                 \
+  } while (0)
+#endif
 
 // --------------------------------------------------------------------------- persistent loop
 struct Item {
@@ -508,313 +529,463 @@ __global__ void __launch_bounds__(NT, 4) tc_local_state_kernel(
   epilogue_end(tb, 64);
 }
 
+// --------------------------------------------------------------------------- pipelined kernels
+// tc_fwd_o and tc_bwd run one CTA per SM: NT compute threads plus one producer warp.  The
+// producer fills a ring of NS shared-memory stages by TMA, each once the consumer released it
+// (the `empty` barrier: the tensor core's completion of the last MMA batch that reads the
+// stage, or an arrive for items left to the exact kernels).  The compute threads run a
+// two-item software pipeline: item i's gating and first MMA batch are issued before item
+// i-1's last batch is waited for and its epilogue written, so the tensor core works on one
+// item while the CUDA cores work on the other; TMEM regions, gated operand tiles and gate
+// factors are double-buffered between the two items in flight.  Outputs of whole chunks are
+// staged in shared memory as swizzled tiles and written by TMA stores; rows of a partial chunk
+// (the next sequence's tokens follow them) are stored directly.
+
+// Producer: for the CTA's j-th item, wait until stage j % NS is released by item j - NS, then
+// issue the item's copies on full[j % NS].
+template <int NS, class Issue>
+__device__ __forceinline__ void producer_loop(int MC, int H, const longlong2* __restrict__ tab, uint64_t* full,
+                                              uint64_t* empty, volatile int* bad, Issue issue) {
+  const int G = gridDim.x, gq = G / H, gr = G % H;
+  Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
+  Item x;
+  for (int j = 0; decode_item(c, item_entry(c, MC, tab), x); ++j, c.advance(gq, gr, H)) {
+    const int s = j % NS;
+    if (j >= NS && !mbar_wait(&empty[s], (uint32_t)(((j - NS) / NS) & 1))) {
+      if ((threadIdx.x & 31) == 0) atomicAdd(&g_wait_timeouts, 1u);
+      *bad = 1;
+      break;
+    }
+    issue(x, s);
+  }
+}
+
+// Consumer item walk: calls body(item, stage, parity) for the CTA's items in order.
+template <int NS, class Body>
+__device__ __forceinline__ void consumer_loop(int MC, int H, const longlong2* __restrict__ tab, Body body) {
+  const int G = gridDim.x, gq = G / H, gr = G % H;
+  Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
+  Item x;
+  for (int i = 0; decode_item(c, item_entry(c, MC, tab), x); ++i, c.advance(gq, gr, H))
+    body(x, i % NS, (uint32_t)((i / NS) & 1));
+}
+
+// End of a producer/consumer kernel: every thread (producer included) meets; the TMA stores of
+// the last epilogue are waited for; TMEM is released.
+__device__ __forceinline__ void pipeline_end(uint32_t tb, uint32_t ncols) {
+  if (threadIdx.x == 0) bulk_wait_all();
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if ((threadIdx.x >> 5) == 0) tmem_dealloc(tb, ncols);
+}
+
 // --------------------------------------------------------------------------- forward output
 // stage: q | k | v | H' tiles | raw gate.  Q^ and K^ are gated in place.
 template <typename Tg> __host__ __device__ constexpr int fo_stage_bytes() { return 4 * TILE + gate_bytes<Tg>(); }
+constexpr int FO_NS = 3;
 
-template <typename T, typename Tg, int NS>
-__global__ void __launch_bounds__(NT, NS == 1 ? 3 : 2) tc_fwd_o_kernel(
+template <typename T, typename Tg>
+__global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mg,
-    const __grid_constant__ CUtensorMap mh, const longlong2* __restrict__ chunk_tab, int MC, int H, float scale,
-    const unsigned char* __restrict__ xflag, T* __restrict__ o) {
+    const __grid_constant__ CUtensorMap mh, const __grid_constant__ CUtensorMap mo,
+    const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, const unsigned char* __restrict__ xflag,
+    T* __restrict__ o) {
+  constexpr int NS = FO_NS;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = fo_stage_bytes<Tg>();
   unsigned char* sA = smem + NS * STAGE;
-  GateSmem& G = *reinterpret_cast<GateSmem*>(sA + TILE);
-  __shared__ uint64_t bars[3];  // MMA, full[0], full[1]
-  __shared__ uint32_t tbase_s;
-  __shared__ int s_bad;
-  volatile int* bad = &s_bad;
-  uint64_t* full = bars + 1;
-  const int tid = threadIdx.x;
-  prologue<3>(&tbase_s, 128, bars, bad);
-  const uint32_t tb = tbase_s;
-  uint32_t phase = 0;
-  const Epi ep;
-  const Own me;
-  const CUtensorMap* m16[3] = {&mq, &mk, &mv};
-  if (tid == 0)
-    for (const CUtensorMap* m : {&mq, &mk, &mv, &mg, &mh}) prefetch_tensormap(m);
-  constexpr uint32_t F = Fmt<T>::v;
-  griddep_wait();
-  auto poison = [&](const Item& x) {
-    T* ob = o + (x.t0 * H + x.head) * D;
-    for (int e = tid; e < x.len * D; e += NT) stf(ob + (int64_t)(e / D) * H * D + (e % D), kNaN);
-  };
-  persistent_loop<NS>(
-      MC, H, chunk_tab, full, bad,
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        unsigned char* sd[1] = {b + 3 * TILE};
-        const CUtensorMap* ms[1] = {&mh};
-        issue_loads(b, m16, 3, b + 4 * TILE, &mg, gate_bytes<Tg>(), sd, ms, 1, (int)(x.id(H) * D), x.t0, x.head,
-                    &full[st]);
-      },
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        zero_tail<Tg>(b, 3, b + 4 * TILE, x.len, me);
-      },
-      [&](const Item& x, int st, auto& next) {
-        next();  // short items: the next item's copies start right away
-        if (xflag[x.id(H)]) return;  // left to the exact kernel
-        unsigned char* sQ = smem + st * STAGE;
-        unsigned char* sK = sQ + TILE;
-        unsigned char* sV = sK + TILE;
-        unsigned char* sH = sV + TILE;
-        gate_prep<Tg>(G, sH + TILE);
-        gate_qk<T>(sQ, sK, sQ, sK, G, me, scale);
-        operands_ready();
-        if (tid == 0) {
-          mma64(tb, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);       // A = Q^ K^^T
-          mma64(tb + 64, sQ, 0, sH, 1, idesc_f16(64, 64, F, 0, 1), false);  // O = Q^ H'
-          commit(&bars[0]);
-        }
-        wait_mma(&bars[0], phase, bad);
-        {
-          float a[1][16];
-          ld_acc<1>(ep, {tb}, a);
-#pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const int r = ep.row(p), c = ep.col(p);
-            st2_tile<T>(sA, r, c, c > r ? 0.f : a[0][2 * p], c + 1 > r ? 0.f : a[0][2 * p + 1]);
-          }
-        }
-        operands_ready();
-        if (tid == 0) {
-          mma64(tb + 64, sA, 0, sV, 1, idesc_f16(64, 64, F, 0, 1), true);  // O += A V
-          commit(&bars[0]);
-        }
-        wait_mma(&bars[0], phase, bad);
-        {
-          float y[1][16];
-          ld_acc<1>(ep, {tb + 64}, y);
-          const bool poisoned = *bad;
-          T* ob = o + (x.t0 * H + x.head) * D;
-#pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const int r = ep.row(p);
-            if (r < x.len)
-              st2_global<T>(ob + (int64_t)r * H * D + ep.col(p), poisoned ? kNaN : y[0][2 * p],
-                            poisoned ? kNaN : y[0][2 * p + 1]);
-          }
-        }
-        fence_before();
-      },
-      poison);
-  epilogue_end(tb, 128);
-}
-
-// --------------------------------------------------------------------------- backward
-// stage: q | k | v | do | H' | dH' tiles | raw gate.  Gated Q^, K^ and the score tiles A, dA
-// are working tiles outside the stages; the raw q and k stay in the stage for dg.
-template <typename Tg> __host__ __device__ constexpr int bw_stage_bytes() { return 6 * TILE + gate_bytes<Tg>(); }
-
-struct BwSmem {
-  GateSmem G;
-  float hd[NG][D];  // per-piece-group partial sums of H'.dH' per key row
-  float dgl[D];     // dgL per key index
-};
-
-template <typename T, typename Tg, int NS>
-__global__ void __launch_bounds__(NT, NS == 1 ? 2 : 1) tc_bwd_kernel(
-    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
-    const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mh,
-    const __grid_constant__ CUtensorMap mdh, const longlong2* __restrict__ chunk_tab, int MC, int H,
-    float scale, const unsigned char* __restrict__ xflag, T* __restrict__ dq, T* __restrict__ dk,
-    T* __restrict__ dv, float* __restrict__ dg) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  constexpr int STAGE = bw_stage_bytes<Tg>();
-  unsigned char* sQg = smem + NS * STAGE;
-  unsigned char* sKg = sQg + TILE;
-  unsigned char* sA = sKg + TILE;
-  unsigned char* sdA = sA + TILE;
-  BwSmem& W = *reinterpret_cast<BwSmem*>(sdA + TILE);
-  GateSmem& G = W.G;
-  __shared__ uint64_t bars[4];  // score batch then dq / dk, dv, full[0], full[1]
+  unsigned char* sOut = sA + TILE;
+  GateSmem& G = *reinterpret_cast<GateSmem*>(sOut + TILE);
+  __shared__ uint64_t bars[2 + 2 * NS];  // batch 1, batch 2, full[NS], empty[NS]
   __shared__ uint32_t tbase_s;
   __shared__ int s_bad;
   volatile int* bad = &s_bad;
   uint64_t* full = bars + 2;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  prologue<4>(&tbase_s, 256, bars, bad);
+  uint64_t* empty = bars + 2 + NS;
+  const int tid = threadIdx.x;
+  prologue<2 + 2 * NS>(&tbase_s, 256, bars, bad);
   const uint32_t tb = tbase_s;
-  uint32_t phase = 0, phase_dv = 0;
-  const Epi ep;
-  const Own me;
-  const CUtensorMap* m16[4] = {&mq, &mk, &mv, &mdo};
   if (tid == 0)
-    for (const CUtensorMap* m : {&mq, &mk, &mv, &mdo, &mg, &mh, &mdh}) prefetch_tensormap(m);
+    for (const CUtensorMap* m : {&mq, &mk, &mv, &mg, &mh, &mo}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
   griddep_wait();
-  auto poison = [&](const Item& x) {
-    const int64_t base = (x.t0 * H + x.head) * D;
-    for (int e = tid; e < x.len * D; e += NT) {
-      const int64_t off = base + (int64_t)(e / D) * H * D + (e % D);
-      stf(dq + off, kNaN);
-      stf(dk + off, kNaN);
-      stf(dv + off, kNaN);
-      dg[off] = kNaN;
-    }
-  };
-  persistent_loop<NS>(
-      MC, H, chunk_tab, full, bad,
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        unsigned char* sd[2] = {b + 4 * TILE, b + 5 * TILE};
-        const CUtensorMap* ms[2] = {&mh, &mdh};
-        issue_loads(b, m16, 4, b + 6 * TILE, &mg, gate_bytes<Tg>(), sd, ms, 2, (int)(x.id(H) * D), x.t0, x.head,
-                    &full[st]);
-      },
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        zero_tail<Tg>(b, 4, b + 6 * TILE, x.len, me);
-      },
-      [&](const Item& x, int st, auto& next) {
-        if (xflag[x.id(H)]) return;  // left to the exact kernel
-        unsigned char* rQ = smem + st * STAGE;
-        unsigned char* rK = rQ + TILE;
-        unsigned char* sV = rK + TILE;
-        unsigned char* sDO = sV + TILE;
-        unsigned char* sH = sDO + TILE;
-        unsigned char* sDH = sH + TILE;
-        gate_prep<Tg>(G, sDH + TILE);
-        gate_qk<T>(rQ, rK, sQg, sKg, G, me, scale);
-        operands_ready();
+  if (tid >= NT) {  // producer warp
+    const CUtensorMap* m16[3] = {&mq, &mk, &mv};
+    producer_loop<NS>(MC, H, chunk_tab, full, empty, bad, [&](const Item& x, int st) {
+      unsigned char* b = smem + st * STAGE;
+      unsigned char* sd[1] = {b + 3 * TILE};
+      const CUtensorMap* ms[1] = {&mh};
+      issue_loads(b, m16, 3, b + 4 * TILE, &mg, gate_bytes<Tg>(), sd, ms, 1, (int)(x.id(H) * D), x.t0, x.head,
+                  &full[st]);
+    });
+  } else {
+    const Epi ep;
+    const Own me;
+    uint32_t ph1 = 0, ph2 = 0;
+    int ci = 0;             // items computed so far (TMEM region parity)
+    bool pending = false;   // an item whose last batch is issued and epilogue not yet written
+    Item prev{};
+    int prev_b = 0;
+    // epilogue of the pending item: O from TMEM region pb -> staged tile + TMA store (whole
+    // chunks) or direct stores (partial chunks)
+    auto finish = [&](const Item& x, int pb) {
+      wait_mma(&bars[1], ph2, bad);
+      float y[1][16];
+      ld_acc<1>(ep, {tb + 128 * pb + 64}, y);
+      const bool poisoned = *bad;
+      if (x.len == BT) {
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          st2_tile<T>(sOut, ep.row(p), ep.col(p), poisoned ? kNaN : y[0][2 * p], poisoned ? kNaN : y[0][2 * p + 1]);
+        fence_proxy_async();
+        cbar();
         if (tid == 0) {
-          mma64(tb, sQg, 0, sKg, 0, idesc_f16(64, 64, F, 0, 0), false);       // A  = Q^ K^^T
-          mma64(tb + 64, sDO, 0, sV, 0, idesc_f16(64, 64, F, 0, 0), false);   // dA = do v^T
-          mma64(tb + 128, sKg, 1, sV, 1, idesc_f16(64, 64, F, 1, 1), false);  // S  = K^^T v
-          commit(&bars[0]);
+          tma_store_3d(&mo, sOut, 0, x.head, (int)x.t0);
+          bulk_commit_group();
         }
-        // H'.dH' per key row (this thread's 16 elements) while the score batch runs
-        {
-          float hd = 0.f;
+      } else {
+        T* ob = o + (x.t0 * H + x.head) * D;
 #pragma unroll
-          for (int pc = 0; pc < 2; ++pc) {
-            const int off = pc ? me.off1 : me.off0;
-            const uint4 uh = *reinterpret_cast<const uint4*>(sH + off);
-            const uint4 ud = *reinterpret_cast<const uint4*>(sDH + off);
-            const T* xh = reinterpret_cast<const T*>(&uh);
-            const T* xd = reinterpret_cast<const T*>(&ud);
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p);
+          if (r < x.len)
+            st2_global<T>(ob + (int64_t)r * H * D + ep.col(p), poisoned ? kNaN : y[0][2 * p],
+                          poisoned ? kNaN : y[0][2 * p + 1]);
+        }
+      }
+    };
+    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+      counted_wait(&full[st], par, bad);
+      unsigned char* sQ = smem + st * STAGE;
+      unsigned char* sK = sQ + TILE;
+      unsigned char* sV = sK + TILE;
+      unsigned char* sH = sV + TILE;
+      if (x.len < BT) {
+        zero_tail<Tg>(sQ, 3, sH + TILE, x.len, me);
+        cbar();
+      }
+      if (xflag[x.id(H)] || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
+        if (pending) finish(prev, prev_b);
+        pending = false;
+        if (*bad) {
+          T* ob = o + (x.t0 * H + x.head) * D;
+          for (int e = tid; e < x.len * D; e += NT) stf(ob + (int64_t)(e / D) * H * D + (e % D), kNaN);
+        }
+        cbar();
+        if (tid == 0) mbar_arrive(&empty[st]);
+        return;
+      }
+      const int b = ci & 1;
+      const uint32_t tA = tb + 128 * b, tO = tA + 64;
+      gate_prep<Tg>(G.E, G.part, sH + TILE);
+      gate_qk<T>(sQ, sK, sQ, sK, G.E, me, scale);
+      operands_ready();
+      if (tid == 0) {
+        mma64(tA, sQ, 0, sK, 0, idesc_f16(64, 64, F, 0, 0), false);  // A = Q^ K^^T
+        mma64(tO, sQ, 0, sH, 1, idesc_f16(64, 64, F, 0, 1), false);  // O = Q^ H'
+        commit(&bars[0]);
+      }
+      if (pending) finish(prev, prev_b);
+      wait_mma(&bars[0], ph1, bad);
+      {
+        float a[1][16];
+        ld_acc<1>(ep, {tA}, a);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) hd = fmaf(ldf(xh + i), ldf(xd + i), hd);
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p), c = ep.col(p);
+          st2_tile<T>(sA, r, c, c > r ? 0.f : a[0][2 * p], c + 1 > r ? 0.f : a[0][2 * p + 1]);
+        }
+      }
+      if (tid == 0) bulk_wait_read_all();  // the staged output tile is free again
+      operands_ready();
+      if (tid == 0) {
+        mma64(tO, sA, 0, sV, 1, idesc_f16(64, 64, F, 0, 1), true);  // O += A V
+        commit(&bars[1]);
+        commit(&empty[st]);  // the stage is free once this batch has read it
+      }
+      ++ci;
+      pending = true;
+      prev = x;
+      prev_b = b;
+    });
+    if (pending) finish(prev, prev_b);
+  }
+  pipeline_end(tb, 256);
+}
+
+// --------------------------------------------------------------------------- backward
+// stage: q | k | v | do | H' | dH' tiles | raw gate.  Double-buffered work tiles: gated Q^, K^
+// (which become the staged dq, dk tiles of the item's epilogue), gate factors E (then dgc);
+// single: the score tiles A, dA and the staged dv tile.
+template <typename Tg> __host__ __device__ constexpr int bw_stage_bytes() { return 6 * TILE + gate_bytes<Tg>(); }
+constexpr int BW_NS = 2;
+
+struct BwSmem {
+  float E[2][BT * LDG];  // exp(gc - ref) per buffer; dgc scratch in the epilogue
+  float part[NG][D];     // gate-scan group sums
+  float dpart[NG][D];    // dg reverse-cumsum group sums
+  float hd[NG][D];       // H'.dH' partial sums per key row
+  float gp[2][D];        // dH'.S partial sums per key row, per column half
+  float dgl[2][D];       // dgL per key index, per buffer
+};
+
+template <typename T, typename Tg>
+__global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
+    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+    const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mh,
+    const __grid_constant__ CUtensorMap mdh, const __grid_constant__ CUtensorMap mdq,
+    const __grid_constant__ CUtensorMap mdk, const __grid_constant__ CUtensorMap mdv,
+    const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, const unsigned char* __restrict__ xflag,
+    T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dg) {
+  constexpr int NS = BW_NS;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  constexpr int STAGE = bw_stage_bytes<Tg>();
+  unsigned char* sQg = smem + NS * STAGE;  // [2] tiles
+  unsigned char* sKg = sQg + 2 * TILE;     // [2] tiles
+  unsigned char* sA = sKg + 2 * TILE;
+  unsigned char* sdA = sA + TILE;
+  unsigned char* sOut = sdA + TILE;
+  BwSmem& W = *reinterpret_cast<BwSmem*>(sOut + TILE);
+  __shared__ uint64_t bars[2 + 2 * NS];  // batch 1, batch 2, full[NS], empty[NS]
+  __shared__ uint32_t tbase_s;
+  __shared__ int s_bad;
+  volatile int* bad = &s_bad;
+  uint64_t* full = bars + 2;
+  uint64_t* empty = bars + 2 + NS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  prologue<2 + 2 * NS>(&tbase_s, 512, bars, bad);
+  const uint32_t tb = tbase_s;
+  if (tid == 0)
+    for (const CUtensorMap* m : {&mq, &mk, &mv, &mdo, &mg, &mh, &mdh, &mdq, &mdk, &mdv}) prefetch_tensormap(m);
+  constexpr uint32_t F = Fmt<T>::v;
+  // TMEM: batch 1 (A, dA, S) at columns 0..191, batch 2 (dq~, dk~, dv) at 256..447
+  const uint32_t tA = tb, tdA = tb + 64, tS = tb + 128, tQ = tb + 256, tK = tb + 320, tV = tb + 384;
+  griddep_wait();
+  if (tid >= NT) {  // producer warp
+    const CUtensorMap* m16[4] = {&mq, &mk, &mv, &mdo};
+    producer_loop<NS>(MC, H, chunk_tab, full, empty, bad, [&](const Item& x, int st) {
+      unsigned char* b = smem + st * STAGE;
+      unsigned char* sd[2] = {b + 4 * TILE, b + 5 * TILE};
+      const CUtensorMap* ms[2] = {&mh, &mdh};
+      issue_loads(b, m16, 4, b + 6 * TILE, &mg, gate_bytes<Tg>(), sd, ms, 2, (int)(x.id(H) * D), x.t0, x.head,
+                  &full[st]);
+    });
+  } else {
+    const Epi ep;
+    const Own me;
+    uint32_t ph1 = 0, ph2 = 0;
+    int ci = 0;
+    bool pending = false;
+    Item prev{};
+    int prev_b = 0;
+    auto poison_rows = [&](const Item& x) {
+      const int64_t base = (x.t0 * H + x.head) * D;
+      for (int e = tid; e < x.len * D; e += NT) {
+        const int64_t off = base + (int64_t)(e / D) * H * D + (e % D);
+        stf(dq + off, kNaN);
+        stf(dk + off, kNaN);
+        stf(dv + off, kNaN);
+        dg[off] = kNaN;
+      }
+    };
+    // epilogue of the pending item (buffer pb): dv, dq, dk and dg
+    auto finish = [&](const Item& x, int pb) {
+      PHASE(ci - 1, 10);
+      wait_mma(&bars[1], ph2, bad);
+      PHASE(ci - 1, 11);
+      const bool poisoned = *bad;
+      const bool whole = x.len == BT;
+      const int64_t base = (x.t0 * H + x.head) * D;
+      unsigned char* gQ = sQg + pb * TILE;
+      unsigned char* gK = sKg + pb * TILE;
+      float* E = W.E[pb];
+      {
+        float z[1][16];
+        ld_acc<1>(ep, {tV}, z);
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p), c = ep.col(p);
+          const float z0 = poisoned ? kNaN : z[0][2 * p], z1 = poisoned ? kNaN : z[0][2 * p + 1];
+          if (whole) st2_tile<T>(sOut, r, c, z0, z1);
+          else if (r < x.len) st2_global<T>(dv + base + (int64_t)r * H * D + c, z0, z1);
+        }
+      }
+      {
+        float acc[2][16];
+        ld_acc<2>(ep, {tQ, tK}, acc);
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p), c = ep.col(p);
+          float* e = E + r * LDG + c;
+          const float e0 = e[0], e1 = e[1];
+          float q0 = acc[0][2 * p] * (scale * e0), q1 = acc[0][2 * p + 1] * (scale * e1);
+          float k0 = __fdividef(acc[1][2 * p], e0), k1 = __fdividef(acc[1][2 * p + 1], e1);
+          if (poisoned) q0 = q1 = k0 = k1 = kNaN;
+          // dgc = q dq - k dk = Q^ dq~ - K^ dk~ (the gated tiles of this item)
+          float gq0, gq1, gk0, gk1;
+          ld2_tile<T>(gQ, r, c, gq0, gq1);
+          ld2_tile<T>(gK, r, c, gk0, gk1);
+          e[0] = gq0 * acc[0][2 * p] - gk0 * acc[1][2 * p];
+          e[1] = gq1 * acc[0][2 * p + 1] - gk1 * acc[1][2 * p + 1];
+          if (whole) {  // this thread's own elements: the gated tiles become the staged outputs
+            st2_tile<T>(gQ, r, c, q0, q1);
+            st2_tile<T>(gK, r, c, k0, k1);
+          } else if (r < x.len) {
+            const int64_t off = base + (int64_t)r * H * D + c;
+            st2_global<T>(dq + off, q0, q1);
+            st2_global<T>(dk + off, k0, k1);
           }
-          W.hd[me.tc >> 3][me.tr] = hd;
         }
-        wait_mma(&bars[0], phase, bad);
-        {
-          float acc[3][16];
-          ld_acc<3>(ep, {tb, tb + 64, tb + 128}, acc);
-          float dgl0 = 0.f, dgl1 = 0.f;  // rows r0, r0 + 8
+      }
+      fence_proxy_async();
+      fence_before();
+      cbar();
+      PHASE(ci - 1, 12);
+      if (whole && tid == 0) {
+        tma_store_3d(&mdv, sOut, 0, x.head, (int)x.t0);
+        tma_store_3d(&mdq, gQ, 0, x.head, (int)x.t0);
+        tma_store_3d(&mdk, gK, 0, x.head, (int)x.t0);
+        bulk_commit_group();
+      }
+      // dg = reverse cumulative sum over rows of dgc (+ dgL at every row): NG groups of RG rows
+      {
+        const int c = tid & 63, qt = tid >> 6;
+        float y[RG];
+        float run = 0.f;
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const int r = ep.row(p), c = ep.col(p);
-            const bool m0 = c > r, m1 = c + 1 > r;
-            st2_tile<T>(sA, r, c, m0 ? 0.f : acc[0][2 * p], m1 ? 0.f : acc[0][2 * p + 1]);
-            st2_tile<T>(sdA, r, c, m0 ? 0.f : acc[1][2 * p], m1 ? 0.f : acc[1][2 * p + 1]);
-            // row r of S is key index r: dH'[r, :] . S[r, :]
-            float d0, d1;
-            ld2_tile<T>(sDH, r, c, d0, d1);
-            const float t = fmaf(d0, acc[2][2 * p], d1 * acc[2][2 * p + 1]);
-            if (p & 1) dgl1 += t; else dgl0 += t;
-          }
-          dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 1);
-          dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 2);
-          dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 1);
-          dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 2);
-          if ((lane & 3) == 0) {
-            G.part[warp >> 2][ep.r0] = dgl0;
-            G.part[warp >> 2][ep.r0 + 8] = dgl1;
-          }
+        for (int i = RG - 1; i >= 0; --i) {
+          run += E[(RG * qt + i) * LDG + c];
+          y[i] = run;
         }
-        operands_ready();
-        if (tid == 0) {
-          mma64(tb + 192, sA, 1, sDO, 1, idesc_f16(64, 64, F, 1, 1), false);  // dv  = A^T do
-          mma64(tb + 192, sKg, 0, sDH, 1, idesc_f16(64, 64, F, 0, 1), true);  //     + K^ dH'
-          commit(&bars[1]);
-          mma64(tb, sDO, 0, sH, 0, idesc_f16(64, 64, F, 0, 0), false);        // dq~ = do H'^T
-          mma64(tb, sdA, 0, sKg, 1, idesc_f16(64, 64, F, 0, 1), true);        //     + dA K^
-          mma64(tb + 64, sV, 0, sDH, 0, idesc_f16(64, 64, F, 0, 0), false);   // dk~ = v dH'^T
-          mma64(tb + 64, sdA, 1, sQg, 1, idesc_f16(64, 64, F, 1, 1), true);   //     + dA^T Q^
-          commit(&bars[0]);
+        W.dpart[qt][c] = run;
+        cbar();
+        float after = W.dgl[pb][c];
+#pragma unroll
+        for (int j = 0; j < NG; ++j)
+          if (j > qt) after += W.dpart[j][c];
+        float* dst = dg + base + (int64_t)RG * qt * H * D + c;
+#pragma unroll
+        for (int i = 0; i < RG; ++i)
+          if (RG * qt + i < x.len) dst[(int64_t)i * H * D] = poisoned ? kNaN : y[i] + after;
+      }
+      PHASE(ci - 1, 13);
+    };
+    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+      PHASE(ci, 0);
+      counted_wait(&full[st], par, bad);
+      PHASE(ci, 1);
+      unsigned char* rQ = smem + st * STAGE;
+      unsigned char* rK = rQ + TILE;
+      unsigned char* sV = rK + TILE;
+      unsigned char* sDO = sV + TILE;
+      unsigned char* sH = sDO + TILE;
+      unsigned char* sDH = sH + TILE;
+      if (x.len < BT) {
+        zero_tail<Tg>(rQ, 4, sDH + TILE, x.len, me);
+        cbar();
+      }
+      if (xflag[x.id(H)] || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
+        if (pending) finish(prev, prev_b);
+        pending = false;
+        if (*bad) poison_rows(x);
+        cbar();
+        if (tid == 0) mbar_arrive(&empty[st]);
+        return;
+      }
+      const int b = ci & 1;
+      unsigned char* gQ = sQg + b * TILE;
+      unsigned char* gK = sKg + b * TILE;
+      gate_prep<Tg>(W.E[b], W.part, sDH + TILE);
+      PHASE(ci, 2);
+      gate_qk<T>(rQ, rK, gQ, gK, W.E[b], me, scale);
+      operands_ready();
+      PHASE(ci, 3);
+      if (tid == 0) {
+        mma64(tA, gQ, 0, gK, 0, idesc_f16(64, 64, F, 0, 0), false);    // A  = Q^ K^^T
+        mma64(tdA, sDO, 0, sV, 0, idesc_f16(64, 64, F, 0, 0), false);  // dA = do v^T
+        mma64(tS, gK, 1, sV, 1, idesc_f16(64, 64, F, 1, 1), false);    // S  = K^^T v
+        commit(&bars[0]);
+      }
+      // H'.dH' per key row (this thread's 16 elements) while the batch runs
+      {
+        float hd = 0.f;
+#pragma unroll
+        for (int pc = 0; pc < 2; ++pc) {
+          const int off = pc ? me.off1 : me.off0;
+          const uint4 uh = *reinterpret_cast<const uint4*>(sH + off);
+          const uint4 ud = *reinterpret_cast<const uint4*>(sDH + off);
+          const T* xh = reinterpret_cast<const T*>(&uh);
+          const T* xd = reinterpret_cast<const T*>(&ud);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hd = fmaf(ldf(xh + i), ldf(xd + i), hd);
         }
-        next();
-        // dgL per key index: H'.dH' + dH'.(K^^T v)
-        if (tid < D) {
-          float s = G.part[0][tid] + G.part[1][tid];
+        W.hd[me.tc >> 3][me.tr] = hd;
+      }
+      PHASE(ci, 4);
+      if (pending) finish(prev, prev_b);
+      PHASE(ci, 5);
+      wait_mma(&bars[0], ph1, bad);
+      PHASE(ci, 6);
+      {
+        float acc[3][16];
+        ld_acc<3>(ep, {tA, tdA, tS}, acc);
+        float dgl0 = 0.f, dgl1 = 0.f;  // rows r0, r0 + 8
 #pragma unroll
-          for (int j = 0; j < NG; ++j) s += W.hd[j][tid];
-          W.dgl[tid] = s;
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p), c = ep.col(p);
+          const bool m0 = c > r, m1 = c + 1 > r;
+          st2_tile<T>(sA, r, c, m0 ? 0.f : acc[0][2 * p], m1 ? 0.f : acc[0][2 * p + 1]);
+          st2_tile<T>(sdA, r, c, m0 ? 0.f : acc[1][2 * p], m1 ? 0.f : acc[1][2 * p + 1]);
+          // row r of S is key index r: dH'[r, :] . S[r, :]
+          float d0, d1;
+          ld2_tile<T>(sDH, r, c, d0, d1);
+          const float t = fmaf(d0, acc[2][2 * p], d1 * acc[2][2 * p + 1]);
+          if (p & 1) dgl1 += t; else dgl0 += t;
         }
-        const int64_t base = (x.t0 * H + x.head) * D;
-        wait_mma(&bars[1], phase_dv, bad);
-        {
-          float z[1][16];
-          ld_acc<1>(ep, {tb + 192}, z);
-          const bool poisoned = *bad;
-#pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const int r = ep.row(p);
-            if (r < x.len)
-              st2_global<T>(dv + base + (int64_t)r * H * D + ep.col(p), poisoned ? kNaN : z[0][2 * p],
-                            poisoned ? kNaN : z[0][2 * p + 1]);
-          }
+        dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 1);
+        dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 2);
+        dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 1);
+        dgl1 += __shfl_xor_sync(0xffffffffu, dgl1, 2);
+        if ((lane & 3) == 0) {
+          W.gp[warp >> 2][ep.r0] = dgl0;
+          W.gp[warp >> 2][ep.r0 + 8] = dgl1;
         }
-        wait_mma(&bars[0], phase, bad);
-        {
-          float acc[2][16];
-          ld_acc<2>(ep, {tb, tb + 64}, acc);
-          const bool poisoned = *bad;
+      }
+      PHASE(ci, 7);
+      if (tid == 0) bulk_wait_read_all();  // the staged output tiles are free again
+      operands_ready();
+      if (tid == 0) {
+        mma64(tV, sA, 1, sDO, 1, idesc_f16(64, 64, F, 1, 1), false);  // dv  = A^T do
+        mma64(tV, gK, 0, sDH, 1, idesc_f16(64, 64, F, 0, 1), true);   //     + K^ dH'
+        mma64(tQ, sDO, 0, sH, 0, idesc_f16(64, 64, F, 0, 0), false);  // dq~ = do H'^T
+        mma64(tQ, sdA, 0, gK, 1, idesc_f16(64, 64, F, 0, 1), true);   //     + dA K^
+        mma64(tK, sV, 0, sDH, 0, idesc_f16(64, 64, F, 0, 0), false);  // dk~ = v dH'^T
+        mma64(tK, sdA, 1, gQ, 1, idesc_f16(64, 64, F, 1, 1), true);   //     + dA^T Q^
+        commit(&bars[1]);
+        commit(&empty[st]);  // the stage is free once this batch has read it
+      }
+      PHASE(ci, 8);
+      // dgL per key index: H'.dH' + dH'.(K^^T v)
+      if (tid < D) {
+        float s2 = W.gp[0][tid] + W.gp[1][tid];
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const int r = ep.row(p), c = ep.col(p);
-            float* e = G.E + r * LDG + c;
-            const float e0 = e[0], e1 = e[1];
-            float q0 = acc[0][2 * p] * (scale * e0), q1 = acc[0][2 * p + 1] * (scale * e1);
-            float k0 = __fdividef(acc[1][2 * p], e0), k1 = __fdividef(acc[1][2 * p + 1], e1);
-            if (poisoned) q0 = q1 = k0 = k1 = kNaN;
-            float rq0, rq1, rk0, rk1;
-            ld2_tile<T>(rQ, r, c, rq0, rq1);
-            ld2_tile<T>(rK, r, c, rk0, rk1);
-            e[0] = rq0 * q0 - rk0 * k0;  // dgc
-            e[1] = rq1 * q1 - rk1 * k1;
-            if (r < x.len) {
-              const int64_t off = base + (int64_t)r * H * D + c;
-              st2_global<T>(dq + off, q0, q1);
-              st2_global<T>(dk + off, k0, k1);
-            }
-          }
-        }
-        fence_before();
-        __syncthreads();
-        // dg = reverse cumulative sum over rows of dgc (+ dgL at every row): NG groups of RG rows
-        {
-          const int c = tid & 63, qt = tid >> 6;
-          float y[RG];
-          float run = 0.f;
-#pragma unroll
-          for (int i = RG - 1; i >= 0; --i) {
-            run += G.E[(RG * qt + i) * LDG + c];
-            y[i] = run;
-          }
-          G.part[qt][c] = run;
-          __syncthreads();
-          float after = W.dgl[c];
-#pragma unroll
-          for (int j = 0; j < NG; ++j)
-            if (j > qt) after += G.part[j][c];
-          float* dst = dg + base + (int64_t)RG * qt * H * D + c;
-#pragma unroll
-          for (int i = 0; i < RG; ++i)
-            if (RG * qt + i < x.len) dst[(int64_t)i * H * D] = y[i] + after;
-        }
-      },
-      poison);
-  epilogue_end(tb, 256);
+        for (int j = 0; j < NG; ++j) s2 += W.hd[j][tid];
+        W.dgl[b][tid] = s2;
+      }
+      PHASE(ci, 9);
+      ++ci;
+      pending = true;
+      prev = x;
+      prev_b = b;
+    });
+    if (pending) finish(prev, prev_b);
+  }
+  pipeline_end(tb, 512);
 }
 
 template <typename K_>
@@ -830,7 +1001,7 @@ int prepare(K_ kern, size_t smem) {
 // Grid: as many CTAs as fit on the device at once (shared memory, registers and TMEM columns
 // permitting), capped by the number of items.
 template <typename K_>
-int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned& grid) {
+int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned& grid, int nthreads = NT) {
   int rc = prepare(kern, smem);
   if (rc) return rc;
   // CTAs per SM from the kernel's own resources (the occupancy query can report the pre-launch
@@ -846,9 +1017,9 @@ int persistent_grid(K_ kern, size_t smem, int tmem_cols, int64_t items, unsigned
     return SSLA_ERR_CUDA;
   }
   const int by_smem = (int)((228 * 1024) / (smem + fa.sharedSizeBytes + 1024));
-  const int by_regs = 65536 / (((fa.numRegs + 7) / 8) * 8 * NT);
+  const int by_regs = 65536 / (((fa.numRegs + 7) / 8) * 8 * nthreads);
   int per_sm = by_smem < by_regs ? by_smem : by_regs;
-  if (per_sm > 2048 / NT) per_sm = 2048 / NT;
+  if (per_sm > 2048 / nthreads) per_sm = 2048 / nthreads;
   if (per_sm * tmem_cols > 512) per_sm = 512 / tmem_cols;
   if (per_sm < 1) {
     set_error("chunk_gla tensor-core kernel: %zu bytes of shared memory do not fit an SM", smem);
@@ -915,16 +1086,6 @@ int check_sizes(int64_t T, int64_t MC, int64_t H) {
   return SSLA_OK;
 }
 
-// Shared-memory stages per CTA (1: several CTAs per SM; 2: copies of the next item overlap
-// the current one inside the CTA).  SSLA_TC_STAGES=1|2 overrides the per-kernel default.
-int stages(int dflt) {
-  static const int env = [] {
-    const char* e = getenv("SSLA_TC_STAGES");
-    return e ? atoi(e) : 0;
-  }();
-  return env == 1 || env == 2 ? env : dflt;
-}
-
 }  // namespace
 
 int tc_aligned(const void* const* ptrs, int n) {
@@ -961,24 +1122,22 @@ int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v
              const unsigned char* xflag, void* o, cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
   if (int rc = check_sizes(T, MC, H)) return rc;
-  CUtensorMap mq, mk, mv, mg, mh;
+  CUtensorMap mq, mk, mv, mg, mh, mo;
   int rc;
   if ((rc = make_map(&mq, q, dtype, T, H, true)) || (rc = make_map(&mk, k, dtype, T, H, true)) ||
       (rc = make_map(&mv, v, dtype, T, H, true)) || (rc = make_map(&mg, g, dtype_g, T, H, false)) ||
-      (rc = make_state_map(&mh, h16, dtype, MC * H * D)))
+      (rc = make_state_map(&mh, h16, dtype, MC * H * D)) || (rc = make_map(&mo, o, dtype, T, H, true)))
     return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
-    auto run = [&](auto kern, int ns) -> int {
-      const size_t smem = ns * fo_stage_bytes<Tg>() + TILE + sizeof(GateSmem) + kAlignSlack;
-      unsigned grid = 0;
-      int rc2 = persistent_grid(kern, smem, 128, MC * H, grid);
-      if (rc2) return rc2;
-      launch_pdl(kern, dim3(grid), dim3(NT), smem, s, mq, mk, mv, mg, mh, chunk_tab, (int)MC, (int)H, scale, xflag,
-                 (T_*)o);
-      SSLA_CHECK_LAUNCH("chunk_gla tc_fwd_o");
-      return SSLA_OK;
-    };
-    return stages(1) == 1 ? run(tc_fwd_o_kernel<T_, Tg, 1>, 1) : run(tc_fwd_o_kernel<T_, Tg, 2>, 2);
+    auto kern = tc_fwd_o_kernel<T_, Tg>;
+    const size_t smem = FO_NS * fo_stage_bytes<Tg>() + 2 * TILE + sizeof(GateSmem) + kAlignSlack;
+    unsigned grid = 0;
+    int rc2 = persistent_grid(kern, smem, 256, MC * H, grid, NT + 32);
+    if (rc2) return rc2;
+    launch_pdl(kern, dim3(grid), dim3(NT + 32), smem, s, mq, mk, mv, mg, mh, mo, chunk_tab, (int)MC, (int)H, scale,
+               xflag, (T_*)o);
+    SSLA_CHECK_LAUNCH("chunk_gla tc_fwd_o");
+    return SSLA_OK;
   });
 }
 
@@ -988,25 +1147,24 @@ int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, 
            float* dg, cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
   if (int rc = check_sizes(T, MC, H)) return rc;
-  CUtensorMap mq, mk, mv, mdo, mg, mh, mdh;
+  CUtensorMap mq, mk, mv, mdo, mg, mh, mdh, mdq, mdk, mdv;
   int rc;
   if ((rc = make_map(&mq, q, dtype, T, H, true)) || (rc = make_map(&mk, k, dtype, T, H, true)) ||
       (rc = make_map(&mv, v, dtype, T, H, true)) || (rc = make_map(&mdo, dout, dtype, T, H, true)) ||
       (rc = make_map(&mg, g, dtype_g, T, H, false)) || (rc = make_state_map(&mh, h16, dtype, MC * H * D)) ||
-      (rc = make_state_map(&mdh, dh16, dtype, MC * H * D)))
+      (rc = make_state_map(&mdh, dh16, dtype, MC * H * D)) || (rc = make_map(&mdq, dq, dtype, T, H, true)) ||
+      (rc = make_map(&mdk, dk, dtype, T, H, true)) || (rc = make_map(&mdv, dv, dtype, T, H, true)))
     return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
-    auto run = [&](auto kern, int ns) -> int {
-      const size_t smem = ns * bw_stage_bytes<Tg>() + 4 * TILE + sizeof(BwSmem) + kAlignSlack;
-      unsigned grid = 0;
-      int rc2 = persistent_grid(kern, smem, 256, MC * H, grid);
-      if (rc2) return rc2;
-      launch_pdl(kern, dim3(grid), dim3(NT), smem, s, mq, mk, mv, mdo, mg, mh, mdh, chunk_tab, (int)MC, (int)H, scale,
-                 xflag, (T_*)dq, (T_*)dk, (T_*)dv, dg);
-      SSLA_CHECK_LAUNCH("chunk_gla tc_bwd");
-      return SSLA_OK;
-    };
-    return stages(1) == 1 ? run(tc_bwd_kernel<T_, Tg, 1>, 1) : run(tc_bwd_kernel<T_, Tg, 2>, 2);
+    auto kern = tc_bwd_kernel<T_, Tg>;
+    const size_t smem = BW_NS * bw_stage_bytes<Tg>() + 7 * TILE + sizeof(BwSmem) + kAlignSlack;
+    unsigned grid = 0;
+    int rc2 = persistent_grid(kern, smem, 512, MC * H, grid, NT + 32);
+    if (rc2) return rc2;
+    launch_pdl(kern, dim3(grid), dim3(NT + 32), smem, s, mq, mk, mv, mdo, mg, mh, mdh, mdq, mdk, mdv, chunk_tab,
+               (int)MC, (int)H, scale, xflag, (T_*)dq, (T_*)dk, (T_*)dv, dg);
+    SSLA_CHECK_LAUNCH("chunk_gla tc_bwd");
+    return SSLA_OK;
   });
 }
 
@@ -1029,3 +1187,14 @@ int tc_timeouts(int reset, unsigned* count) {
 }  // namespace ssla
 
 extern "C" int ssla_chunk_gla_tc_timeouts(int reset, unsigned* count) { return ssla::chunk::tc_timeouts(reset, count); }
+
+#ifdef SSLA_PHASE_PROF
+// Development build only: copy (and clear) the phase-timing table; `out` holds
+// kPhaseCtas * kPhaseItems * kPhasePts int64.
+extern "C" int ssla_chunk_gla_phase_dump(long long* out) {
+  using namespace ssla::chunk;
+  if (cudaMemcpyFromSymbol(out, g_phase, sizeof(g_phase)) != cudaSuccess) return SSLA_ERR_CUDA;
+  static long long zero[kPhaseCtas * kPhaseItems * kPhasePts];
+  return cudaMemcpyToSymbol(g_phase, zero, sizeof(g_phase)) == cudaSuccess ? SSLA_OK : SSLA_ERR_CUDA;
+}
+#endif

@@ -135,6 +135,13 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                "r"(y), "r"(smem_u32(src))
                : "memory");
 }
+// TMA tiled store of a 3-D box from shared memory (bulk-group completion); elements outside
+// the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tmap), "r"(x),
+               "r"(y), "r"(z), "r"(smem_u32(src))
+               : "memory");
+}
 // Barrier `id` (1..15) over `n` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

@@ -20,6 +20,7 @@ from .layers import (LinearAttention, MosAttention, SparseAdaptiveAvgPool, Spars
                      SparseMaxPool, TemporalDropout)
 from . import _lib
 from .ops import segment as _seg
+from .ops.mos import check_tc_errors
 from .utils.farsecnn_utils import group_events
 
 FRAME_SIZES = {"Gen1": ((240, 304), 2), "NCaltech101": ((180, 240), 101)}
@@ -80,21 +81,8 @@ def preprocess_inputs(events: torch.Tensor, lengths: torch.Tensor, frame_size, h
     events, so truncating during the grouping gives the same dt)."""
     with torch.no_grad():
         x = torch.cat([events[..., :3], events[..., 2:3], events[..., 3:]], dim=-1)
-        grouped = group_events((x, lengths), frame_size,
-                               keep_first=hot_pixel_thres if hot_pixel_thres > 0 else None)
-        feats = grouped["events"].clone()
-        t = feats[:, 0]
-        dt = torch.empty_like(t)
-        dt[0:1] = t[0:1]
-        dt[1:] = t[1:] - t[:-1]
-        # tensor / tensor: IEEE division on every device (a scalar divisor may become a
-        # multiplication by its reciprocal)
-        dt = torch.clamp(dt / torch.full_like(dt, 1e5), max=1)
-        first = torch.cumsum(grouped["lengths"], 0) - grouped["lengths"]
-        dt[first] = 1
-        feats[:, 0] = dt
-        grouped["events"] = feats
-    return grouped
+        return group_events((x, lengths), frame_size, keep_first=hot_pixel_thres if hot_pixel_thres > 0 else None,
+                            delay_col=0)
 
 
 def async_event_to_grid(x, grid_size, channels: int) -> torch.Tensor:
@@ -206,8 +194,14 @@ class MosDetector(nn.Module):
                 taps.append(x)
         return [async_event_to_grid(t, self.grid_sizes[k], self.in_features[k]) for k, t in enumerate(taps)]
 
-    def forward(self, events: torch.Tensor, lengths: torch.Tensor) -> torch.Tensor:
-        return self.head(self.backbone_grids(events, lengths))
+    def forward(self, events: torch.Tensor, lengths: torch.Tensor, check_errors: bool = True) -> torch.Tensor:
+        """Head output (B, anchors, 4 + 1 + num_classes).  With ``check_errors`` the device flag of
+        the tensor-core GEMMs' bounded waits is read once at the end (one host synchronisation)
+        and a timeout raises instead of returning untrustworthy detections."""
+        out = self.head(self.backbone_grids(events, lengths))
+        if check_errors:
+            check_tc_errors(out.device)
+        return out
 
     def postprocess_with_nms(self, preds: torch.Tensor, conf_thres: float = 0.001, iou_thres: float = 0.65,
                              filtering: bool = True, max_det: int = 100) -> List[Dict]:

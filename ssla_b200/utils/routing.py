@@ -61,66 +61,49 @@ def receptive_field_lut(frame_size, kernel_size, stride) -> Tuple[torch.Tensor, 
     return lut.to(torch.int64), outcoord.reshape(oh * ow, 2).to(torch.int64)
 
 
-def group_events(inputs, frame_size, max_events_per_px: int = 512, keep_first=None) -> Dict[str, torch.Tensor]:
+def group_events(inputs, frame_size, max_events_per_px: int = 512, keep_first=None,
+                 delay_col=None) -> Dict[str, torch.Tensor]:
     """Group events [B, N, C] (rows <x, y, t, features...>, per-sample lengths) by pixel
-    (utils/farsecnn_utils.py:130-174, utils/async_utils.py:10-84): stable order by
-    (sample, pixel), at most the last `max_events_per_px` events of a pixel kept.  With
-    ``keep_first`` only the first ``keep_first`` of those are kept, which is the grouping
-    followed by ``truncate_packed_sequence`` (model_mos.py:173-209) in one pass.
+    (utils/farsecnn_utils.py:130-174, utils/async_utils.py:10-84): groups in ascending
+    (sample, pixel) order, a group's events in input order, at most the last
+    ``max_events_per_px`` events of a pixel kept.  With ``keep_first`` only the first
+    ``keep_first`` of those are kept, which is the grouping followed by
+    ``truncate_packed_sequence`` (model_mos.py:173-209) in one pass; with ``delay_col`` that
+    feature column is replaced by the per-pixel delay min((t - t_prev) / 1e5, 1), 1 for a
+    group's first event (model_mos.py:190-200).
 
-    Works on the padded [B * N] rows directly (padding sorts after every pixel) and reads the
-    device once, for the group and kept-event counts."""
+    Runs the grouping kernels of ``csrc/group.cu`` (counts, scans, placement, per-pixel
+    ordering; no sort) and reads the device once, for the group and kept-event counts."""
     events, lengths = inputs
-    events = events.float()
     B, Nmax, C = events.shape
     H, W = int(frame_size[0]), int(frame_size[1])
+    _lib.require_cuda(events, what="group_events")
     dev = events.device
-    lengths = lengths.to(dev).to(torch.int64)
-    N = B * Nmax
-    rows = events.reshape(N, C)
-    row = torch.arange(N, device=dev)
-    valid = (torch.arange(Nmax, device=dev).unsqueeze(0) < lengths.unsqueeze(1)).reshape(N)
-    batch_of_row = row // max(Nmax, 1)
-    pid = batch_of_row * (H * W) + rows[:, 1].to(torch.int64) * W + rows[:, 0].to(torch.int64)
-    pid = torch.where(valid, pid, B * H * W)
-    order = torch.sort(pid, stable=True)[1]
-    spid = pid[order]
-    svalid = valid[order]  # valid rows first
-    bound = torch.ones(N, dtype=torch.bool, device=dev)  # a group (or the padding) starts here
-    if N:
-        bound[1:] = spid[1:] != spid[:-1]
-    opens = bound & svalid
-    # start row of every group (the padding counts as one): a scatter to the running count of
-    # boundaries; slots past the last group hold N, slot N + 1 takes the non-boundary rows
-    gidx = torch.cumsum(bound, 0) - 1
-    bstart = torch.full((N + 2,), N, dtype=torch.int64, device=dev)
-    bstart.scatter_(0, torch.where(bound, gidx, N + 1), row)
-    gstart = bstart[gidx]
-    gend = bstart[gidx + 1]
-    cnt = gend - gstart
-    rank = row - gstart
-    skip = cnt - cnt.clamp(max=max_events_per_px)
-    keep = svalid & (rank >= skip)
-    if keep_first is not None:
-        keep &= rank - skip < keep_first
-    n_kept = torch.cumsum(keep, 0)
-    G, K = (torch.stack([opens.sum(), n_kept[-1]]).tolist() if N else (0, 0))
-    first = bstart[:G]  # valid groups precede the padding
-    kept_row = torch.empty(K + 1, dtype=torch.int64, device=dev)
-    kept_row.scatter_(0, torch.where(keep, n_kept - 1, K), row)
-    kept_row = kept_row[:K]
-    gr_lengths = cnt[first].clamp(max=max_events_per_px)
-    if keep_first is not None:
-        gr_lengths = gr_lengths.clamp(max=keep_first)
-    kept = rows[order[kept_row]]
-    rep = rows[order[first]]
+    ev = events.float().contiguous()
+    ln = lengths.to(device=dev, dtype=torch.int64).contiguous()
+    L, st = _lib.load(), _lib.stream_of(ev)
+    big = (1 << 62)
+    kf = big if keep_first is None else int(keep_first)
+    nb = L.ssla_group_events_workspace_bytes(B, Nmax, H, W)
+    ws = torch.empty(max(nb, 1), device=dev, dtype=torch.uint8)
+    totals = torch.empty(3, device=dev, dtype=torch.int32)
+    _lib.check(L.ssla_group_events_count(ev.data_ptr(), B, Nmax, C, ln.data_ptr(), H, W, int(max_events_per_px), kf,
+                                         ws.data_ptr(), nb, totals.data_ptr(), st), "group_events")
+    _, G, K = totals.tolist()
+    i64 = lambda n: torch.empty(n, device=dev, dtype=torch.int64)
+    batch_id, gh, gw, glen, time = i64(G), i64(G), i64(G), i64(G), i64(K)
+    feats = torch.empty((K, C - 3), device=dev, dtype=torch.float32)
+    _lib.check(L.ssla_group_events_emit(ev.data_ptr(), B, Nmax, C, H, W, int(max_events_per_px), kf, ws.data_ptr(),
+                                        G, K, -1 if delay_col is None else int(delay_col), batch_id.data_ptr(),
+                                        gh.data_ptr(), gw.data_ptr(), glen.data_ptr(), time.data_ptr(),
+                                        feats.data_ptr(), st), "group_events")
     return {
-        "events": kept[:, 3:],
-        "time": kept[:, 2].to(torch.int64),
-        "batch_id": batch_of_row[order[first]],
-        "h": rep[:, 1].to(torch.int64),
-        "w": rep[:, 0].to(torch.int64),
-        "lengths": gr_lengths,
+        "events": feats,
+        "time": time,
+        "batch_id": batch_id,
+        "h": gh,
+        "w": gw,
+        "lengths": glen,
         "batch_size": B,
     }
 

@@ -338,3 +338,48 @@ def test_batched_nms_matches_torchvision(N, filtering, max_det):
         assert torch.equal(g["labels"], rl)
         assert torch.equal(g["scores"], rs)
         assert torch.equal(g["boxes"], rb)
+
+
+@pytest.mark.parametrize("maxpp,keep", [(512, 50), (512, None), (3, None), (100, 7)])
+def test_group_events_kernels_exact(maxpp, keep):
+    """Native pixel grouping (csrc/group.cu) against the CPU restatement of the reference's
+    stable-sort grouping (oracle.routing), on batches with hot pixels: one pixel with 40 events
+    (the per-thread ranking path), one with 700 (shared-memory sort) and one with 5000 (radix
+    selection of the kept ranks), plus an empty sample and duplicate timestamps."""
+    from oracle import routing as orr
+    from ssla_b200.synthetic import event_batch
+    from ssla_b200.utils.routing import group_events
+
+    ev, ln = event_batch(3, seed=5)
+    ev, ln = ev.clone(), ln.clone()
+    ln[1] = 0
+    gen = torch.Generator().manual_seed(1)
+    for cnt, (x, y) in ((40, (10, 20)), (700, (100, 50)), (5000, (303, 239))):
+        idx = torch.randperm(int(ln[0]), generator=gen)[:cnt]
+        ev[0, idx, 0], ev[0, idx, 1] = float(x), float(y)
+    ev[2, 100:110, 2] = ev[2, 100, 2]  # equal timestamps
+    x = torch.cat([ev[..., :3], ev[..., 2:3], ev[..., 3:]], dim=-1)
+    ref = orr.group_events(x, ln, (240, 304), maxpp)
+    if keep is not None:
+        st = torch.cumsum(ref["lengths"], 0) - ref["lengths"]
+        pos = torch.arange(ref["events"].shape[0]) - torch.repeat_interleave(st, ref["lengths"])
+        k = pos < keep
+        ref["events"], ref["time"] = ref["events"][k], ref["time"][k]
+        ref["lengths"] = ref["lengths"].clamp(max=keep)
+    got = group_events((x.cuda(), ln.cuda()), (240, 304), maxpp, keep_first=keep)
+    for key in ("events", "time", "batch_id", "h", "w", "lengths"):
+        assert torch.equal(got[key].cpu(), ref[key]), key
+
+
+def test_preprocess_delay_matches_oracle():
+    """Grouping + hot-pixel truncation + per-pixel delay in one pass (model.preprocess_inputs)
+    against the reference's three-step preprocessing restated in oracle.routing.preprocess."""
+    from oracle import routing as orr
+    from ssla_b200.model import preprocess_inputs
+    from ssla_b200.synthetic import event_batch
+
+    ev, ln = event_batch(4, seed=9)
+    ref = orr.preprocess(ev, ln, (240, 304), 50)
+    got = preprocess_inputs(ev.cuda(), ln.cuda(), (240, 304), 50)
+    for key in ("events", "time", "batch_id", "h", "w", "lengths"):
+        assert torch.equal(got[key].cpu(), ref[key]), key

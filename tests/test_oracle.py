@@ -116,3 +116,16 @@ def test_segment_oracle_matches_torch_scatter_reduce():
     assert torch.allclose(oseg.scatter_mean(src, idx, S), mean_ref, rtol=1e-6, atol=1e-7)
     sum_ref = torch.zeros(S, C).scatter_reduce_(0, ex, src, reduce="sum", include_self=False)
     assert torch.equal(oseg.scatter_sum_fast(src, idx, S), sum_ref)
+
+
+def test_routing_oracle_matches_reference_preprocessing():
+    """oracle.routing.preprocess against the grouped input the reference model produced
+    (MosModel.preprocess_inputs on event_batch(2, seed=7), tests/golden/make_golden_model.py)."""
+    from oracle import routing as orr
+    from ssla_b200.synthetic import event_batch
+
+    gold = torch.load(GOLDEN / "model_mos_s.pt")
+    ev, ln = event_batch(gold["batch"], seed=gold["seed"])
+    g = orr.preprocess(ev, ln, (240, 304), 50)
+    for k, v in gold["grouped"].items():
+        assert torch.equal(g[k].to(v.dtype), v), k
