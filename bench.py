@@ -263,12 +263,12 @@ def triton_reference_line(dev, steps, warmup):
 
     try:
         r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--leg", "triton-reference", "--steps",
-                            str(steps), "--warmup", str(warmup)], capture_output=True, text=True, timeout=900,
+                            str(steps), "--warmup", str(warmup)], capture_output=True, text=True, timeout=2400,
                            env={**os.environ, "CUDA_VISIBLE_DEVICES": os.environ.get("CUDA_VISIBLE_DEVICES", "0")})
         lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
         ref = json.loads(lines[-1]) if lines else {"unavailable": (r.stderr or "no output").strip().splitlines()[-1][:300]}
     except subprocess.TimeoutExpired:
-        ref = {"unavailable": "reference Triton run exceeded 900 s (autotuning)"}
+        ref = {"unavailable": "reference Triton run exceeded 2400 s (autotuning)"}
     ours_chunk, ours_scan = time_api(our_chunk, our_scan, dev, steps, warmup)
     out = {"what": "device ms per call through each implementation's public API (autograd fwd+bwd), inputs "
                    "resident, L2 flushed: chunk_gla on BASELINE config 2; scan on the 8 MOS_S scan shapes of 2 "
@@ -444,9 +444,10 @@ def run_other(args):
             holder = {}
 
             def step():
-                off = seg.segment_offsets_sorted(inv, S)
-                mx, _ = seg.segment_reduce(feats, off, None, seg.MAX)
-                mn, _ = seg.segment_reduce(feats, off, None, seg.MEAN)
+                # cell ids of pixel-ordered rows are not monotonic: CSR (counting sort) each step
+                off, rows = seg.segment_csr(inv, S)
+                mx, _ = seg.segment_reduce(feats, off, rows, seg.MAX)
+                mn, _ = seg.segment_reduce(feats, off, rows, seg.MEAN)
                 holder["back"] = seg.gather_rows(mx, inv)
                 holder["mean"] = mn
 
@@ -557,8 +558,9 @@ def main():
                     help="chunk: headline (BASELINE config 2); recurrent: config 3; pool: config 4; "
                          "model: config 5 frames/s")
     ap.add_argument("--no-model", action="store_true", help="skip the SSLA-S frames/s field of the headline")
-    ap.add_argument("--no-triton-reference", action="store_true",
-                    help="skip timing the reference's Triton kernels on this GPU")
+    ap.add_argument("--triton-reference", action="store_true",
+                    help="also time the reference's own Triton chunk_gla / scan on this GPU (its autotuner "
+                         "compiles every configuration: about 15 minutes on a fresh box)")
     ap.add_argument("--leg", default=None, choices=["triton-reference"], help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.leg == "triton-reference":
@@ -715,7 +717,7 @@ def main():
 
     model_line = None if args.no_model else bench_model(dev, world, rank, dist, steps=3, warmup=2)
     triton_ref = None
-    if rank == 0 and world == 1 and not args.no_triton_reference:
+    if rank == 0 and world == 1 and args.triton_reference:
         triton_ref = triton_reference_line(dev, steps=10, warmup=3)
     if rank != 0:
         if dist is not None:

@@ -152,8 +152,10 @@ def test_c4_pooling_full_size_bit_exact(k):
     pixels half uniform / half in 20 sigma-8 blobs, Poisson(3) events per pixel, int64 flat
     indices, C=64 bf16): scatter_max values and argmax, scatter_mean and the gather back to the
     rows, through the torch_scatter interface (expanded index, as layers/sparse_pooling.py:33
-    calls it) and through the sorted-segment path the pooling layer uses; bit-exact against the
-    CPU oracle."""
+    calls it) and through the explicit CSR + segment-reduce path; bit-exact against the CPU
+    oracle.  The cell ids of rows ordered by pixel are not monotonic (pixel rows wrap inside a
+    cell row), so the unsorted (CSR) path is the one that applies; the sorted-segment path is
+    checked on the rows stably re-ordered by cell."""
     from ssla_b200 import torch_scatter as ts
     from ssla_b200.ops import segment as seg
     from ssla_b200.synthetic import pooling_rows
@@ -169,8 +171,18 @@ def test_c4_pooling_full_size_bit_exact(k):
     mx, arg = ts.scatter_max(f, ic[:, None].expand(R, C), dim=0, dim_size=S)
     assert torch.equal(mx.cpu(), mx_r) and torch.equal(arg.cpu(), arg_r)
     assert torch.equal(ts.scatter_mean(f, ic[:, None].expand(R, C), dim=0, dim_size=S).cpu(), mean_r)
-    off = seg.segment_offsets_sorted(ic, S)
-    mx2, arg2 = seg.segment_reduce(f, off, None, seg.MAX, want_arg=True)
-    mn2, _ = seg.segment_reduce(f, off, None, seg.MEAN)
+    assert not bool((inv[1:] >= inv[:-1]).all())
+    off, rows = seg.segment_csr(ic, S)
+    mx2, arg2 = seg.segment_reduce(f, off, rows, seg.MAX, want_arg=True)
+    mn2, _ = seg.segment_reduce(f, off, rows, seg.MEAN)
     assert torch.equal(mx2.cpu(), mx_r) and torch.equal(arg2.cpu(), arg_r) and torch.equal(mn2.cpu(), mean_r)
     assert torch.equal(seg.gather_rows(mx2, ic).cpu(), back_r)
+    # sorted-segment path on the rows re-ordered by cell (stable): same values, argmax mapped back
+    perm = torch.sort(inv, stable=True)[1]
+    ps = perm.cuda()
+    off3 = seg.segment_offsets_sorted(ic[ps], S)
+    mx3, arg3 = seg.segment_reduce(f[ps].contiguous(), off3, None, seg.MAX, want_arg=True)
+    mn3, _ = seg.segment_reduce(f[ps].contiguous(), off3, None, seg.MEAN)
+    assert torch.equal(mx3.cpu(), mx_r) and torch.equal(mn3.cpu(), mean_r)
+    a3 = arg3.cpu()
+    assert torch.equal(torch.where(a3 < R, perm[a3.clamp(max=R - 1)], a3), arg_r)
