@@ -138,7 +138,11 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline_sample(threads: int, seq_len: int = 2048, n_seqs: int = 4):
+# one CPU sample for both the headline's cpu_baseline and the --impl reference arm
+CPU_SEQ_LEN, CPU_SEQS = 512, 2
+
+
+def cpu_baseline_sample(threads: int, seq_len: int = CPU_SEQ_LEN, n_seqs: int = CPU_SEQS):
     """Reference CPU path (naive recurrence + autograd) on one bounded sample: ``n_seqs``
     sequences of ``seq_len`` tokens with the workload's H, K, V.  Returns tokens/s."""
     from oracle.gla import naive_gla_recurrent
@@ -166,9 +170,9 @@ def run_reference(args):
         return
     threads = os.cpu_count() or 1
     times = []
-    n_tok = 512
+    n_tok = CPU_SEQ_LEN * CPU_SEQS
     for i in range(args.warmup + args.steps):
-        tps, sample = cpu_baseline_sample(threads, seq_len=n_tok, n_seqs=1)
+        tps, sample = cpu_baseline_sample(threads)
         if i >= args.warmup:
             times.append(n_tok / tps)
     v = n_tok * len(times) / sum(times)
@@ -365,6 +369,140 @@ def bench_model(dev, world, rank, dist, steps=3, warmup=2, variant="S"):
             "data": "synthetic 20 bins x 5 ms, 2% occupancy, uniform + 20 Gaussian blobs"}
 
 
+def recurrent_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
+    """fused_recurrent_gla streaming, 65,536 sequences x H=4, K=V=32, one token
+    per call with the fp32 state carried (ping-pong buffers), through the C ABI."""
+    from ssla_b200 import _lib
+
+    stream = torch.cuda.current_stream(dev)
+    hbm, which = peaks()
+    L = _lib.load()
+    N, Hh, Kk, Vv, Tt = 65536, 4, 32, 32, 20
+    gen = torch.Generator().manual_seed(3 + rank)
+    mk = lambda d: torch.randn(Tt, N, Hh, d, generator=gen).to(torch.bfloat16).to(dev)
+    q, k, v = mk(Kk), mk(Kk), mk(Vv)
+    g = (F.logsigmoid(torch.randn(Tt, N, Hh, Kk, generator=gen)) / 16).to(torch.bfloat16).to(dev)
+    o = torch.empty(Tt, N, Hh, Vv, device=dev, dtype=torch.bfloat16)
+    st = [torch.zeros(N, Hh, Kk, Vv, device=dev), torch.empty(N, Hh, Kk, Vv, device=dev)]
+    cu = torch.arange(N + 1, device=dev)
+    sp = stream.cuda_stream
+    it = [0]
+
+    def step():
+        t = it[0] % Tt
+        src, dst = st[it[0] % 2], st[(it[0] + 1) % 2]
+        _lib.check(L.ssla_recurrent_gla_fwd(q[t].data_ptr(), k[t].data_ptr(), v[t].data_ptr(), g[t].data_ptr(),
+                                            _lib.BF16, _lib.BF16, cu.data_ptr(), N, N, Hh, Kk, Vv, Kk ** -0.5,
+                                            src.data_ptr(), o[t].data_ptr(), dst.data_ptr(), sp), "recurrent")
+        it[0] += 1
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    with Clocks(local) as clk:
+        secs = _max_over_ranks(_event_time(step, steps, stream), dist, dev)
+    bytes_step = 2 * N * Hh * Kk * Vv * 4 + N * Hh * (3 * Kk + 2 * Vv) * 2
+    if rank != 0:
+        return None
+    gbs = bytes_step * steps / secs / 1e9
+    cpu = None
+    if want_cpu and world == 1:
+        from oracle.gla import naive_gla_recurrent
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        n_s = 4096
+        qs, ks, vs, gs = (x[0, :n_s].float().cpu() for x in (q, k, v, g))
+        t0 = time.perf_counter()
+        naive_gla_recurrent(qs, ks, vs, gs, torch.arange(n_s + 1), initial_state=torch.zeros(n_s, Hh, Kk, Vv),
+                            output_final_state=True)
+        cpu = {"value": n_s / (time.perf_counter() - t0), "unit": "tokens/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": f"one streaming step of {n_s} sequences (naive recurrence)"}
+    return {
+        "metric": "fused_recurrent_gla streaming tokens/s", "value": world * N * steps / secs,
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": 1e3 * secs / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 3: 65536 sequences x H=4, K=V=32, one token per call, "
+                               "fp32 state carried (ping-pong buffers), T=20 steps cycled",
+                   "l2": "state 1 GiB per buffer > L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_source": which, "alg_bytes_per_step": bytes_step, "traffic": None},
+        "gpu_launches": steps, "cpu_baseline": cpu, "clocks": clk.summary()}
+
+
+def pool_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
+    """scatter max + mean into 2x2 / 4x4 cells and gather back, through the
+    torch_scatter-equivalent CSR path (cell ids of pixel-ordered rows are not monotonic, so each
+    step builds the row lists by a counting sort).  The CPU leg also checks the k=2 results."""
+    from ssla_b200.ops import segment as seg
+    from ssla_b200.synthetic import pooling_rows
+
+    stream = torch.cuda.current_stream(dev)
+    hbm, which = peaks()
+    feats, idx, cells = pooling_rows(seed=rank)
+    feats = feats.to(dev)
+    R, C = feats.shape
+    lines, out = {}, {}
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    with Clocks(local) as clk:
+        for kk in (2, 4):
+            inv, S = cells[kk]
+            inv = inv.to(dev)
+            holder = {}
+
+            def step():
+                off, rows = seg.segment_csr(inv, S)
+                mx, _ = seg.segment_reduce(feats, off, rows, seg.MAX)
+                mn, _ = seg.segment_reduce(feats, off, rows, seg.MEAN)
+                holder["back"] = seg.gather_rows(mx, inv)
+                holder["max"], holder["mean"] = mx, mn
+
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize(dev)
+            secs = _max_over_ranks(_event_time(step, steps, stream, flush), dist, dev)
+            out[kk] = holder
+            b_scatter = R * C * 2 + R * 8 + S * C * 2
+            b_gather = S * C * 2 + R * 8 + R * C * 2
+            alg = 2 * b_scatter + b_gather
+            gbs = alg * steps / secs / 1e9
+            lines[f"k{kk}"] = {"rows": R, "cells": S, "ms_per_step": 1e3 * secs / steps,
+                               "rows_per_s": world * R * steps / secs, "achieved_gbs": gbs, "frac": gbs / hbm,
+                               "alg_bytes_per_step": alg}
+    if rank != 0:
+        return None
+    cpu, checked = None, None
+    if want_cpu and world == 1:
+        from oracle.segment import scatter_max, scatter_mean
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        inv, S = cells[2]
+        f = feats.cpu()
+        t0 = time.perf_counter()
+        mx, _ = scatter_max(f, inv, S)
+        mn = scatter_mean(f, inv, S)
+        back = mx[inv]
+        cpu = {"value": R / (time.perf_counter() - t0), "unit": "rows/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": "k=2 max + mean + gather back, all rows"}
+        h = out[2]
+        checked = bool(torch.equal(h["max"].cpu(), mx) and torch.equal(h["mean"].cpu(), mn)
+                       and torch.equal(h["back"].cpu(), back))
+    k2 = lines["k2"]
+    return {
+        "metric": "sparse pooling rows/s (scatter max + mean + gather back, k=2)",
+        "value": k2["rows_per_s"], "unit": "rows/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": k2["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 4: 16 batches x 2 polarity planes at 240x304, ~5% active "
+                               "pixels, Poisson(3) events, C=64 bf16", "l2": "flushed before every step",
+                   "per_k": lines},
+        "roofline": {"bound": "hbm", "achieved": k2["achieved_gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": k2["frac"], "peak_source": which, "alg_bytes_per_step": k2["alg_bytes_per_step"],
+                     "traffic": None},
+        "checked_bit_exact_vs_cpu": checked,
+        "gpu_launches": 9 * steps, "cpu_baseline": cpu, "clocks": clk.summary()}
+
+
 def run_other(args):
     world, rank, local, dev, dist = _dist_env()
     stream = torch.cuda.current_stream(dev)
@@ -376,119 +514,13 @@ def run_other(args):
                          "config": {"workload": "SSLA-S forward, batch 64 split across ranks (BASELINE config 5)"}})
             print(json.dumps(line), flush=True)
     elif args.workload == "recurrent":
-        from ssla_b200 import _lib
-
-        L = _lib.load()
-        N, Hh, Kk, Vv, Tt = 65536, 4, 32, 32, 20
-        gen = torch.Generator().manual_seed(3 + rank)
-        mk = lambda d: torch.randn(Tt, N, Hh, d, generator=gen).to(torch.bfloat16).to(dev)
-        q, k, v = mk(Kk), mk(Kk), mk(Vv)
-        g = (F.logsigmoid(torch.randn(Tt, N, Hh, Kk, generator=gen)) / 16).to(torch.bfloat16).to(dev)
-        o = torch.empty(Tt, N, Hh, Vv, device=dev, dtype=torch.bfloat16)
-        st = [torch.zeros(N, Hh, Kk, Vv, device=dev), torch.empty(N, Hh, Kk, Vv, device=dev)]
-        cu = torch.arange(N + 1, device=dev)
-        sp = stream.cuda_stream
-        it = [0]
-
-        def step():
-            t = it[0] % Tt
-            src, dst = st[it[0] % 2], st[(it[0] + 1) % 2]
-            _lib.check(L.ssla_recurrent_gla_fwd(q[t].data_ptr(), k[t].data_ptr(), v[t].data_ptr(), g[t].data_ptr(),
-                                                _lib.BF16, _lib.BF16, cu.data_ptr(), N, N, Hh, Kk, Vv, Kk ** -0.5,
-                                                src.data_ptr(), o[t].data_ptr(), dst.data_ptr(), sp), "recurrent")
-            it[0] += 1
-
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize(dev)
-        with Clocks(local) as clk:
-            secs = _max_over_ranks(_event_time(step, args.steps, stream), dist, dev)
-        bytes_step = 2 * N * Hh * Kk * Vv * 4 + N * Hh * (3 * Kk + 2 * Vv) * 2
+        line = recurrent_line(dev, world, rank, dist, local, args.steps, args.warmup, not args.no_cpu_baseline)
         if rank == 0:
-            gbs = bytes_step * args.steps / secs / 1e9
-            cpu = None
-            if not args.no_cpu_baseline and world == 1:
-                from oracle.gla import naive_gla_recurrent
-
-                torch.set_num_threads(os.cpu_count() or 1)
-                n_s = 4096
-                qs, ks, vs, gs = (x[0, :n_s].float().cpu() for x in (q, k, v, g))
-                t0 = time.perf_counter()
-                naive_gla_recurrent(qs, ks, vs, gs, torch.arange(n_s + 1), initial_state=torch.zeros(n_s, Hh, Kk, Vv),
-                                    output_final_state=True)
-                cpu = {"value": n_s / (time.perf_counter() - t0), "unit": "tokens/s", "cores": os.cpu_count(),
-                       "kind": "port", "sample": f"one streaming step of {n_s} sequences"}
-            print(json.dumps({
-                "metric": "fused_recurrent_gla streaming tokens/s", "value": world * N * args.steps / secs,
-                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "BASELINE config 3: 65536 sequences x H=4, K=V=32, one token per call, "
-                                       "fp32 state carried (ping-pong buffers), T=20 steps cycled",
-                           "l2": "state 1 GiB per buffer > L2"},
-                "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                             "peak_source": which, "alg_bytes_per_step": bytes_step, "traffic": None},
-                "gpu_launches": args.steps, "cpu_baseline": cpu, "clocks": clk.summary()}), flush=True)
+            print(json.dumps(line), flush=True)
     elif args.workload == "pool":
-        from ssla_b200.ops import segment as seg
-        from ssla_b200.synthetic import pooling_rows
-
-        feats, idx, cells = pooling_rows(seed=rank)
-        feats = feats.to(dev)
-        R, C = feats.shape
-        lines = {}
-        flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
-        for kk in (2, 4):
-            inv, S = cells[kk]
-            inv = inv.to(dev)
-            holder = {}
-
-            def step():
-                # cell ids of pixel-ordered rows are not monotonic: CSR (counting sort) each step
-                off, rows = seg.segment_csr(inv, S)
-                mx, _ = seg.segment_reduce(feats, off, rows, seg.MAX)
-                mn, _ = seg.segment_reduce(feats, off, rows, seg.MEAN)
-                holder["back"] = seg.gather_rows(mx, inv)
-                holder["mean"] = mn
-
-            for _ in range(args.warmup):
-                step()
-            torch.cuda.synchronize(dev)
-            secs = _max_over_ranks(_event_time(step, args.steps, stream, flush), dist, dev)
-            b_scatter = R * C * 2 + R * 8 + S * C * 2
-            b_gather = S * C * 2 + R * 8 + R * C * 2
-            alg = 2 * b_scatter + b_gather
-            gbs = alg * args.steps / secs / 1e9
-            lines[f"k{kk}"] = {"rows": R, "cells": S, "ms_per_step": 1e3 * secs / args.steps,
-                               "rows_per_s": world * R * args.steps / secs, "achieved_gbs": gbs, "frac": gbs / hbm,
-                               "alg_bytes_per_step": alg}
+        line = pool_line(dev, world, rank, dist, local, args.steps, args.warmup, not args.no_cpu_baseline)
         if rank == 0:
-            cpu = None
-            if not args.no_cpu_baseline and world == 1:
-                from oracle.segment import scatter_max, scatter_mean
-
-                torch.set_num_threads(os.cpu_count() or 1)
-                inv, S = cells[2]
-                f = feats.float().cpu()
-                t0 = time.perf_counter()
-                mx, _ = scatter_max(f, inv, S)
-                scatter_mean(f, inv, S)
-                mx[inv]
-                cpu = {"value": R / (time.perf_counter() - t0), "unit": "rows/s", "cores": os.cpu_count(),
-                       "kind": "port", "sample": "k=2 max + mean + gather back, all rows"}
-            k2 = lines["k2"]
-            print(json.dumps({
-                "metric": "sparse pooling rows/s (scatter max + mean + gather back, k=2)",
-                "value": k2["rows_per_s"], "unit": "rows/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": k2["ms_per_step"], "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "BASELINE config 4: 16 batches x 2 polarity planes at 240x304, ~5% active "
-                                       "pixels, Poisson(3) events, C=64 bf16", "l2": "flushed before every step",
-                           "per_k": lines},
-                "roofline": {"bound": "hbm", "achieved": k2["achieved_gbs"], "peak": hbm, "unit": "GB/s",
-                             "frac": k2["frac"], "peak_source": which, "alg_bytes_per_step": k2["alg_bytes_per_step"],
-                             "traffic": None},
-                "gpu_launches": 4 * args.steps, "cpu_baseline": cpu}), flush=True)
+            print(json.dumps(line), flush=True)
     elif args.workload == "events":
         import numpy as np
 
@@ -558,6 +590,8 @@ def main():
                     help="chunk: headline (BASELINE config 2); recurrent: config 3; pool: config 4; "
                          "model: config 5 frames/s")
     ap.add_argument("--no-model", action="store_true", help="skip the SSLA-S frames/s field of the headline")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config-3 (recurrent) and config-4 (pool) objects of the headline")
     ap.add_argument("--triton-reference", action="store_true",
                     help="also time the reference's own Triton chunk_gla / scan on this GPU (its autotuner "
                          "compiles every configuration: about 15 minutes on a fresh box)")
@@ -716,6 +750,9 @@ def main():
     e2e_value = world * TOKENS * args.steps / e2e_secs
 
     model_line = None if args.no_model else bench_model(dev, world, rank, dist, steps=3, warmup=2)
+    rec_line = None if args.no_extra else recurrent_line(dev, world, rank, dist, local, 10, 3,
+                                                         not args.no_cpu_baseline)
+    pool_ln = None if args.no_extra else pool_line(dev, world, rank, dist, local, 10, 3, not args.no_cpu_baseline)
     triton_ref = None
     if rank == 0 and world == 1 and args.triton_reference:
         triton_ref = triton_reference_line(dev, steps=10, warmup=3)
@@ -756,6 +793,8 @@ def main():
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "ssla_s": model_line,
+        "recurrent": rec_line,
+        "pool": pool_ln,
         "triton_reference": triton_ref,
     }
     print(json.dumps(line), flush=True)

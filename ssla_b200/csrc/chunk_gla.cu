@@ -158,8 +158,29 @@ template <> struct SVec<4> {
   }
 };
 
+template <> struct SVec<8> {
+  struct type {
+    float4 a, b;
+  };
+  static __device__ __forceinline__ type ld(const float* p) {
+    return {reinterpret_cast<const float4*>(p)[0], reinterpret_cast<const float4*>(p)[1]};
+  }
+  static __device__ __forceinline__ void st(float* p, type x) {
+    reinterpret_cast<float4*>(p)[0] = x.a;
+    reinterpret_cast<float4*>(p)[1] = x.b;
+  }
+  static __device__ __forceinline__ type fma(float d, type x, type y) {
+    return {SVec<4>::fma(d, x.a, y.a), SVec<4>::fma(d, x.b, y.b)};
+  }
+  static __device__ __forceinline__ type zero() { return {SVec<4>::zero(), SVec<4>::zero()}; }
+  template <typename T16> static __device__ __forceinline__ void st16(T16* p, float s, type x) {
+    SVec<4>::template st16<T16>(p, s, x.a);
+    SVec<4>::template st16<T16>(p + 4, s, x.b);
+  }
+};
+
 template <int VEC, typename T16>
-__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
+__global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG, VEC == 8 ? 2 : 4) state_scan_kernel(
     const float* __restrict__ dS, const float* __restrict__ decay,
     const int64_t* __restrict__ chunk_off, int64_t N, int H, int K, int V,
     const float* __restrict__ init, float* __restrict__ h32, const unsigned char* __restrict__ xflag,
@@ -168,7 +189,10 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
   using S = SVec<VEC>;
   using vec = typename S::type;
   constexpr bool kOut16 = !std::is_same<T16, float>::value;
-  constexpr int SCAN_U = VEC == 4 ? 4 : 8;  // chunks whose loads are in flight together
+  // chunks whose loads are in flight together; a segment of at most SCAN_U chunks keeps them in
+  // registers for the second pass (one round trip to memory in all)
+  constexpr int SCAN_U = VEC == 8 ? 8 : 4;
+  constexpr int LOOP_U = 4;  // batch of the general (longer segment) loops
   __shared__ float sA[SCAN_MAXSEG][SCAN_EL];
   __shared__ vec sB[SCAN_MAXSEG][SCAN_EL], sX[SCAN_MAXSEG][SCAN_EL];
   const int el = threadIdx.x % SCAN_EL, sg = threadIdx.x / SCAN_EL;
@@ -206,17 +230,28 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
   // (predicated, so a short segment still costs one round trip): they do not depend on B.
   float A = 1.f;
   vec B = S::zero();
-  for (int64_t i = 0; i < len; i += SCAN_U) {
-    float d[SCAN_U];
-    vec a[SCAN_U];
+  float d0[SCAN_U], e0[SCAN_U];  // the first batch, kept for pass 3 when it is the whole segment
+  vec a0[SCAN_U];
 #pragma unroll
-    for (int u = 0; u < SCAN_U; ++u) {
+  for (int u = 0; u < SCAN_U; ++u) {
+    const bool in = u < len;
+    d0[u] = in ? decay[cd + u * sd] : 1.f;
+    e0[u] = (kOut16 && in) ? escale[cd + u * sd] : 0.f;
+    a0[u] = in ? S::ld(dS + ce + u * sa) : S::zero();
+  }
+#pragma unroll
+  for (int u = 0; u < SCAN_U; ++u) { B = S::fma(d0[u], B, a0[u]); A *= d0[u]; }
+  for (int64_t i = SCAN_U; i < len; i += LOOP_U) {
+    float d[LOOP_U];
+    vec a[LOOP_U];
+#pragma unroll
+    for (int u = 0; u < LOOP_U; ++u) {
       const bool in = i + u < len;
       d[u] = in ? decay[cd + (i + u) * sd] : 1.f;
       a[u] = in ? S::ld(dS + ce + (i + u) * sa) : S::zero();
     }
 #pragma unroll
-    for (int u = 0; u < SCAN_U; ++u) { B = S::fma(d[u], B, a[u]); A *= d[u]; }
+    for (int u = 0; u < LOOP_U; ++u) { B = S::fma(d[u], B, a[u]); A *= d[u]; }
   }
   // 2. chain the segment start values
   vec x;
@@ -243,17 +278,28 @@ __global__ void __launch_bounds__(SCAN_EL * SCAN_MAXSEG) state_scan_kernel(
     if (!xflag || xflag[f]) S::st(h32 + e, val);
     if constexpr (kOut16) S::template st16<T16>(h16 + e, escale[dd], val);
   };
-  for (int64_t i = 0; i < len; i += SCAN_U) {
-    float d[SCAN_U];
-    vec a[SCAN_U];
+  if (len <= SCAN_U) {
 #pragma unroll
     for (int u = 0; u < SCAN_U; ++u) {
+      if (u < len) {
+        if (!xflag || xflag[cf + u * sf]) S::st(h32 + ce + u * sa, x);
+        if constexpr (kOut16) S::template st16<T16>(h16 + ce + u * sa, e0[u], x);
+      }
+      x = S::fma(d0[u], x, a0[u]);
+    }
+    return;
+  }
+  for (int64_t i = 0; i < len; i += LOOP_U) {
+    float d[LOOP_U];
+    vec a[LOOP_U];
+#pragma unroll
+    for (int u = 0; u < LOOP_U; ++u) {
       const bool in = i + u < len;
       d[u] = in ? decay[cd + (i + u) * sd] : 1.f;
       a[u] = in ? S::ld(dS + ce + (i + u) * sa) : S::zero();
     }
 #pragma unroll
-    for (int u = 0; u < SCAN_U; ++u) {
+    for (int u = 0; u < LOOP_U; ++u) {
       if (i + u < len) put(ce + (i + u) * sa, cd + (i + u) * sd, cf + (i + u) * sf, x);
       x = S::fma(d[u], x, a[u]);
     }
@@ -857,11 +903,14 @@ int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_
   // 4 consecutive value columns per thread when rows split evenly and the state arrays align
   const bool v4 = V % 4 == 0 &&
                   ((uintptr_t)dS | (uintptr_t)h32 | (uintptr_t)init | (uintptr_t)final_state | (uintptr_t)h16) % 16 == 0;
-  const int vec = v4 ? 4 : 1;
+  const bool v8 = v4 && V % 8 == 0;
+  const int vec = v8 ? 8 : (v4 ? 4 : 1);
   const int64_t threads = N * H * K * V / vec;
   if (threads == 0) return SSLA_OK;
-  // segments per element: enough threads for about one resident wave (148 SMs x 2048)
-  int64_t nseg = (int64_t)kNumSMs * 2048 / threads;
+  // segments per element: as many as keep the grid within one resident wave (about 1024
+  // threads per SM at 64 registers, 512 at the 8-wide variant's 128): a second wave would cost
+  // more than the extra segments save
+  int64_t nseg = (int64_t)kNumSMs * (vec == 8 ? 512 : 1024) / threads;
   nseg = nseg < 1 ? 1 : (nseg > SCAN_MAXSEG ? SCAN_MAXSEG : nseg);
   const dim3 grid(ceil_div(threads, SCAN_EL)), block(SCAN_EL * (int)nseg);
   auto go = [&](auto kern, auto* out16) {
@@ -869,13 +918,16 @@ int launch_state_scan(const float* dS, const float* decay, const int64_t* chunk_
                escale, final_state, reverse, (int)nseg);
   };
   if (!h16) {
-    if (v4) go(state_scan_kernel<4, float>, (float*)nullptr);
+    if (v8) go(state_scan_kernel<8, float>, (float*)nullptr);
+    else if (v4) go(state_scan_kernel<4, float>, (float*)nullptr);
     else go(state_scan_kernel<1, float>, (float*)nullptr);
   } else if (dtype16 == SSLA_BF16) {
-    if (v4) go(state_scan_kernel<4, __nv_bfloat16>, (__nv_bfloat16*)h16);
+    if (v8) go(state_scan_kernel<8, __nv_bfloat16>, (__nv_bfloat16*)h16);
+    else if (v4) go(state_scan_kernel<4, __nv_bfloat16>, (__nv_bfloat16*)h16);
     else go(state_scan_kernel<1, __nv_bfloat16>, (__nv_bfloat16*)h16);
   } else {
-    if (v4) go(state_scan_kernel<4, __half>, (__half*)h16);
+    if (v8) go(state_scan_kernel<8, __half>, (__half*)h16);
+    else if (v4) go(state_scan_kernel<4, __half>, (__half*)h16);
     else go(state_scan_kernel<1, __half>, (__half*)h16);
   }
   SSLA_CHECK_LAUNCH("chunk_gla state_scan");

@@ -219,19 +219,28 @@ __device__ __forceinline__ void gate_prep(float* __restrict__ E, float (*part)[D
 template <typename T>
 __device__ __forceinline__ void gate_qk(const unsigned char* sQ, const unsigned char* sK, unsigned char* dQ,
                                         unsigned char* dK, const float* __restrict__ E, const Own& me, float scale) {
+  // loads of both pieces before any store (dQ, dK may be the source tiles)
+  uint4 uq[2], uk[2];
+  float e[2][8];
 #pragma unroll
   for (int pc = 0; pc < 2; ++pc) {
     const int off = pc ? me.off1 : me.off0;
-    const uint4 uq = *reinterpret_cast<const uint4*>(sQ + off);
-    const uint4 uk = *reinterpret_cast<const uint4*>(sK + off);
-    const T* xq = reinterpret_cast<const T*>(&uq);
-    const T* xk = reinterpret_cast<const T*>(&uk);
-    const float* e = E + me.tr * LDG + me.tc + 32 * pc;
+    uq[pc] = *reinterpret_cast<const uint4*>(sQ + off);
+    uk[pc] = *reinterpret_cast<const uint4*>(sK + off);
+    const float* ep = E + me.tr * LDG + me.tc + 32 * pc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[pc][i] = ep[i];
+  }
+#pragma unroll
+  for (int pc = 0; pc < 2; ++pc) {
+    const int off = pc ? me.off1 : me.off0;
+    const T* xq = reinterpret_cast<const T*>(&uq[pc]);
+    const T* xk = reinterpret_cast<const T*>(&uk[pc]);
     float yq[8], yk[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      yq[i] = ldf(xq + i) * (scale * e[i]);
-      yk[i] = __fdividef(ldf(xk + i), e[i]);
+      yq[i] = ldf(xq + i) * (scale * e[pc][i]);
+      yk[i] = __fdividef(ldf(xk + i), e[pc][i]);
     }
     *reinterpret_cast<uint4*>(dQ + off) = pack8<T>(yq);
     *reinterpret_cast<uint4*>(dK + off) = pack8<T>(yk);
@@ -283,8 +292,8 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
 // Phase timing (built only with -DSSLA_PHASE_PROF, for kernel development): thread 0 of each
 // CTA records clock64() at numbered points of its first kPhaseItems items into g_phase
 // [CTA][item][point]; ssla_chunk_gla_phase_dump copies the table out.
-constexpr int kPhaseItems = 8, kPhasePts = 16, kPhaseCtas = 1024;
 #ifdef SSLA_PHASE_PROF
+constexpr int kPhaseItems = 8, kPhasePts = 32, kPhaseCtas = 1024;
 __device__ long long g_phase[kPhaseCtas * kPhaseItems * kPhasePts];
 #define PHASE(item, k)                                                                                  \
   do {                                                                                                  \
@@ -330,63 +339,6 @@ __device__ __forceinline__ bool decode_item(const Cursor& c, longlong2 e, Item& 
 }
 
 // Valid chunks form a prefix of the chunk table, so a CTA stops at its first invalid item.
-// `issue(item, stage)` runs on the last warp and starts the item's copies on full[stage];
-// `zero(item, stage)` clears rows past a partial chunk; `proc(item, stage, next)` computes.
-// With two stages proc calls next() (all threads) once the next item's copies may start (the
-// other stage is free); if proc returns without calling it, the loop does.  With one stage
-// the next copies start after the item.  A CTA that turned bad (a wait gave up) drains its
-// copies, poisons (NaN outputs) the rest of its items and leaves the loop.
-template <int NS, class Issue, class Zero, class Proc, class Poison>
-__device__ __forceinline__ void persistent_loop(int MC, int H, const longlong2* __restrict__ tab, uint64_t* full,
-                                                volatile int* bad, Issue issue, Zero zero, Proc proc, Poison poison) {
-  const int G = gridDim.x, gq = G / H, gr = G % H;
-  const bool w0 = threadIdx.x >= NT - 32;  // the last warp issues copies (thread 0 issues MMAs)
-  Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
-  Cursor c1 = c, c2;
-  c1.advance(gq, gr, H);
-  c2 = c1;
-  c2.advance(gq, gr, H);
-  Item cur;
-  bool have = decode_item(c, item_entry(c, MC, tab), cur);
-  longlong2 e_next = item_entry(c1, MC, tab);
-  if (have && w0) issue(cur, 0);
-  for (int i = 0; have; ++i) {
-    const int st = NS == 1 ? 0 : (i & 1);
-    const uint32_t par = NS == 1 ? (uint32_t)(i & 1) : (uint32_t)((i >> 1) & 1);
-    const longlong2 e_after = item_entry(c2, MC, tab);
-    Item nxt;
-    const bool nhave = decode_item(c1, e_next, nxt);
-    bool issued = false;
-    auto next = [&] {
-      if (NS == 2 && !issued && nhave && w0) issue(nxt, (i + 1) & 1);
-      issued = true;
-    };
-    counted_wait(&full[st], par, bad);
-    if (cur.len < BT) {
-      zero(cur, st);
-      __syncthreads();
-    }
-    proc(cur, st, next);
-    next();
-    fence_proxy_async();  // generic writes to this stage before the TMA refills it
-    __syncthreads();
-    if (*bad) {
-      // drain: the copies of this item (if its wait gave up) and of the next one
-      mbar_wait(&full[st], par);
-      if (NS == 2 && nhave) mbar_wait(&full[(i + 1) & 1], (uint32_t)(((i + 1) >> 1) & 1));
-      poison(cur);
-      Cursor pc = c1;
-      for (Item it; decode_item(pc, item_entry(pc, MC, tab), it); pc.advance(gq, gr, H)) poison(it);
-      break;
-    }
-    if (NS == 1 && nhave && w0) issue(nxt, 0);
-    cur = nxt;
-    have = nhave;
-    e_next = e_after;
-    c1 = c2;
-    c2.advance(gq, gr, H);
-  }
-}
 
 // Common prologue: TMEM columns, barriers, bad flag; ends with griddepcontrol.wait (the
 // predecessors wrote the chunk table / states this kernel reads).
@@ -403,12 +355,6 @@ __device__ __forceinline__ void prologue(uint32_t* tbase_s, uint32_t ncols, uint
   fence_after();
 }
 
-__device__ __forceinline__ void epilogue_end(uint32_t tb, uint32_t ncols) {
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if ((threadIdx.x >> 5) == 0) tmem_dealloc(tb, ncols);
-}
 
 // --------------------------------------------------------------------------- local state
 // stage: a tile | b tile | raw gate
@@ -420,113 +366,10 @@ struct LsSmem {
   unsigned int span_bits;
 };
 
-template <typename T, typename Tg, int NS>
-__global__ void __launch_bounds__(NT, 4) tc_local_state_kernel(
-    const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
-    const __grid_constant__ CUtensorMap mg, int mode, const longlong2* __restrict__ chunk_tab, int MC, int H,
-    float scale, float* __restrict__ dS, float* __restrict__ decay, float* __restrict__ escale,
-    unsigned char* __restrict__ xflag, int* __restrict__ xlist) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = align1024(smem_raw);
-  constexpr int STAGE = ls_stage_bytes<Tg>();
-  LsSmem& S = *reinterpret_cast<LsSmem*>(smem + NS * STAGE);
-  __shared__ uint64_t bars[3];  // MMA, full[0], full[1]
-  __shared__ uint32_t tbase_s;
-  __shared__ int s_bad;
-  volatile int* bad = &s_bad;
-  uint64_t* full = bars + 1;
-  const int tid = threadIdx.x;
-  prologue<3>(&tbase_s, 64, bars, bad);
-  const uint32_t tb = tbase_s;
-  uint32_t phase = 0;
-  const Epi ep;
-  const Own me;
-  const CUtensorMap* m16[2] = {&ma, &mb};
-  if (tid == 0)
-    for (const CUtensorMap* m : {&ma, &mb, &mg}) prefetch_tensormap(m);
-  griddep_wait();
-  persistent_loop<NS>(
-      MC, H, chunk_tab, full, bad,
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        issue_loads(b, m16, 2, b + 2 * TILE, &mg, gate_bytes<Tg>(), nullptr, nullptr, 0, 0, x.t0, x.head, &full[st]);
-      },
-      [&](const Item& x, int st) {
-        unsigned char* b = smem + st * STAGE;
-        zero_tail<Tg>(b, 2, b + 2 * TILE, x.len, me);
-      },
-      [&](const Item& x, int st, auto& next) {
-        next();  // short items: the next item's copies start right away
-        unsigned char* sA = smem + st * STAGE;
-        unsigned char* sB = sA + TILE;
-        const int64_t item = x.id(H);
-        // in-chunk prefix sums of the gate, fused with the in-place scaling of the a tile:
-        // mode 0 (state increment) by exp(gL - gc), mode 1 (adjoint increment) by scale exp(gc)
-        {
-          const int c = tid & 63, qt = tid >> 6;
-          const Tg* gr = reinterpret_cast<const Tg*>(sB + TILE);
-          if (tid == 0) S.span_bits = 0u;
-          float xs[RG];
-          float run = 0.f;
-#pragma unroll
-          for (int i = 0; i < RG; ++i) {
-            run += ldf(gr + (RG * qt + i) * D + c);
-            xs[i] = run;
-          }
-          S.part[qt][c] = run;
-          __syncthreads();
-          float off = 0.f, gl = 0.f, ref = 0.f;
-#pragma unroll
-          for (int j = 0; j < NG; ++j) {
-            const float pj = S.part[j][c];
-            if (j < qt) off += pj;
-            if (j <= 31 / RG) ref += pj;
-            gl += pj;
-          }
-          float m = 0.f;
-#pragma unroll
-          for (int i = 0; i < RG; ++i) {
-            const float gc = xs[i] + off;
-            T* e = reinterpret_cast<T*>(sA + toff(RG * qt + i, c));
-            const float f = mode == 0 ? __expf(gl - gc) : scale * __expf(gc);
-            stf(e, ldf(e) * f);
-            m = fmaxf(m, fabsf(gc - ref));
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if ((tid & 31) == 0) atomicMax(&S.span_bits, __float_as_uint(m));
-          if (qt == 0) {
-            decay[item * D + c] = __expf(gl);
-            escale[item * D + c] = mode == 0 ? __expf(ref) : __expf(gl - ref);
-          }
-        }
-        operands_ready();
-        if (tid == 0) {
-          mma64(tb, sA, 1, sB, 1, idesc_f16(64, 64, Fmt<T>::v, 1, 1), false);
-          commit(&bars[0]);
-          if (xflag) {
-            const bool exact = __uint_as_float(S.span_bits) > kTcSpan;
-            xflag[item] = exact ? 1 : 0;
-            if (exact) xlist[1 + atomicAdd(xlist, 1)] = (int)item;
-          }
-        }
-        wait_mma(&bars[0], phase, bad);
-        float v[1][16];
-        ld_acc<1>(ep, {tb}, v);
-        const bool poisoned = *bad;
-        float* out = dS + item * D * D;
-#pragma unroll
-        for (int p = 0; p < 8; ++p)
-          *reinterpret_cast<float2*>(out + ep.row(p) * D + ep.col(p)) =
-              poisoned ? make_float2(kNaN, kNaN) : make_float2(v[0][2 * p], v[0][2 * p + 1]);
-        fence_before();
-      },
-      [&](const Item& x) {
-        float* out = dS + x.id(H) * D * D;
-        for (int e = tid; e < D * D; e += NT) out[e] = kNaN;
-        if (tid < D) decay[x.id(H) * D + tid] = kNaN;
-      });
-  epilogue_end(tb, 64);
+// Byte offset of fp32 element (r, c) of a 64 x 64 tile kept as two 32-column halves, each in
+// the 128-byte-swizzled layout of a TMA box of 32 fp32 columns x 64 rows.
+__device__ __forceinline__ int toff32(int r, int c) {
+  return ((c >> 5) << 13) + (r << 7) + (((((c & 31) >> 2) ^ r) & 7) << 4) + ((c & 3) << 2);
 }
 
 // --------------------------------------------------------------------------- pipelined kernels
@@ -578,6 +421,157 @@ __device__ __forceinline__ void pipeline_end(uint32_t tb, uint32_t ncols) {
   __syncthreads();
   fence_after();
   if ((threadIdx.x >> 5) == 0) tmem_dealloc(tb, ncols);
+}
+
+// --------------------------------------------------------------------------- local state (pipelined)
+// Two CTAs per SM, each NT compute threads + a producer warp keeping LS_NS stages of (a tile,
+// b tile, raw gate) in flight; a stage is released by the tensor core's commit of the item's
+// MMA.  Per item: gate prefix sums fused with the in-place scaling of the a tile, one 64x64x64
+// MMA, the fp32 increment staged from TMEM into shared memory and written by a TMA store (the
+// load/store unit stays free for the next item's shared-memory work).
+constexpr int LS_NS = 3;
+
+template <typename T, typename Tg>
+__global__ void __launch_bounds__(NT + 32, 2) tc_local_state_kernel(
+    const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
+    const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mds, int mode,
+    const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, float* __restrict__ dS,
+    float* __restrict__ decay, float* __restrict__ escale, unsigned char* __restrict__ xflag,
+    int* __restrict__ xlist) {
+  constexpr int NS = LS_NS;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = align1024(smem_raw);
+  constexpr int STAGE = ls_stage_bytes<Tg>();
+  unsigned char* sOut = smem + NS * STAGE;  // 16 KB fp32 staging tile
+  LsSmem& S = *reinterpret_cast<LsSmem*>(sOut + 2 * TILE);
+  __shared__ uint64_t bars[1 + 2 * NS];  // mma, full[NS], empty[NS]
+  __shared__ uint32_t tbase_s;
+  __shared__ int s_bad;
+  volatile int* bad = &s_bad;
+  uint64_t* mma = bars;
+  uint64_t* full = bars + 1;
+  uint64_t* empty = bars + 1 + NS;
+  const int tid = threadIdx.x;
+  prologue<1 + 2 * NS>(&tbase_s, 64, bars, bad);
+  const uint32_t tb = tbase_s;
+  if (tid == 0)
+    for (const CUtensorMap* m : {&ma, &mb, &mg, &mds}) prefetch_tensormap(m);
+  int pitem = -1;
+  (void)pitem;
+  griddep_wait();
+  if (tid >= NT) {  // producer warp
+    const CUtensorMap* m16[2] = {&ma, &mb};
+    producer_loop<NS>(MC, H, chunk_tab, full, empty, bad, [&](const Item& x, int st) {
+      unsigned char* b = smem + st * STAGE;
+      issue_loads(b, m16, 2, b + 2 * TILE, &mg, gate_bytes<Tg>(), nullptr, nullptr, 0, 0, x.t0, x.head, &full[st]);
+    });
+  } else {
+    uint32_t phase = 0;
+    const Epi ep;
+    const Own me;
+    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+      ++pitem;
+      PHASE(pitem, 21);
+      counted_wait(&full[st], par, bad);
+      PHASE(pitem, 16);
+      unsigned char* sA = smem + st * STAGE;
+      unsigned char* sB = sA + TILE;
+      const int64_t item = x.id(H);
+      float* out = dS + item * D * D;
+      if (*bad) {  // the CTA gave up: NaN outputs, stage released
+        for (int e = tid; e < D * D; e += NT) out[e] = kNaN;
+        if (tid < D) decay[item * D + tid] = kNaN;
+        cbar();
+        if (tid == 0) mbar_arrive(&empty[st]);
+        return;
+      }
+      if (x.len < BT) {
+        zero_tail<Tg>(sA, 2, sB + TILE, x.len, me);
+        cbar();
+      }
+      // in-chunk prefix sums of the gate, fused with the in-place scaling of the a tile:
+      // mode 0 (state increment) by exp(gL - gc), mode 1 (adjoint increment) by scale exp(gc)
+      {
+        const int c = tid & 63, qt = tid >> 6;
+        const Tg* gr = reinterpret_cast<const Tg*>(sB + TILE);
+        if (tid == 0) S.span_bits = 0u;
+        float xs[RG];
+        float run = 0.f;
+#pragma unroll
+        for (int i = 0; i < RG; ++i) {
+          run += ldf(gr + (RG * qt + i) * D + c);
+          xs[i] = run;
+        }
+        PHASE(pitem, 24);
+        S.part[qt][c] = run;
+        cbar();
+        PHASE(pitem, 25);
+        float off = 0.f, gl = 0.f, ref = 0.f;
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+          const float pj = S.part[j][c];
+          if (j < qt) off += pj;
+          if (j <= 31 / RG) ref += pj;
+          gl += pj;
+        }
+        // all loads before any store: the compiler cannot tell the tile elements apart, so
+        // an interleaved load / store loop would run one element at a time
+        float m = 0.f, a[RG];
+#pragma unroll
+        for (int i = 0; i < RG; ++i) a[i] = ldf(reinterpret_cast<const T*>(sA + toff(RG * qt + i, c)));
+#pragma unroll
+        for (int i = 0; i < RG; ++i) {
+          const float gc = xs[i] + off;
+          a[i] *= mode == 0 ? __expf(gl - gc) : scale * __expf(gc);
+          m = fmaxf(m, fabsf(gc - ref));
+        }
+#pragma unroll
+        for (int i = 0; i < RG; ++i) stf(reinterpret_cast<T*>(sA + toff(RG * qt + i, c)), a[i]);
+        PHASE(pitem, 26);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) atomicMax(&S.span_bits, __float_as_uint(m));
+        PHASE(pitem, 27);
+        if (qt == 0) {
+          decay[item * D + c] = __expf(gl);
+          escale[item * D + c] = mode == 0 ? __expf(ref) : __expf(gl - ref);
+        }
+      }
+      PHASE(pitem, 17);
+      if (tid == 0) bulk_wait_read_all();  // the previous item's staged tile has been stored
+      operands_ready();
+      if (tid == 0) {
+        mma64(tb, sA, 1, sB, 1, idesc_f16(64, 64, Fmt<T>::v, 1, 1), false);
+        commit(mma);
+        commit(&empty[st]);  // the stage is free once the MMA has read it
+        if (xflag) {
+          const bool exact = __uint_as_float(S.span_bits) > kTcSpan;
+          xflag[item] = exact ? 1 : 0;
+          if (exact) xlist[1 + atomicAdd(xlist, 1)] = (int)item;
+        }
+      }
+      PHASE(pitem, 18);
+      wait_mma(mma, phase, bad);
+      PHASE(pitem, 19);
+      float v[1][16];
+      ld_acc<1>(ep, {tb}, v);
+      const bool poisoned = *bad;
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        *reinterpret_cast<float2*>(sOut + toff32(ep.row(p), ep.col(p))) =
+            poisoned ? make_float2(kNaN, kNaN) : make_float2(v[0][2 * p], v[0][2 * p + 1]);
+      fence_proxy_async();
+      fence_before();
+      cbar();
+      if (tid == 0) {
+        tma_store_2d(&mds, sOut, 0, (int)(item * D));
+        tma_store_2d(&mds, sOut + TILE, 32, (int)(item * D));
+        bulk_commit_group();
+      }
+      PHASE(pitem, 20);
+    });
+  }
+  pipeline_end(tb, 64);
 }
 
 // --------------------------------------------------------------------------- forward output
@@ -818,20 +812,25 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
       {
         float acc[2][16];
         ld_acc<2>(ep, {tQ, tK}, acc);
+        // loads of all pairs first, then the stores (see the local-state scaling loop)
+        float ee[16], gq[16], gk[16];
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
           const int r = ep.row(p), c = ep.col(p);
-          float* e = E + r * LDG + c;
-          const float e0 = e[0], e1 = e[1];
-          float q0 = acc[0][2 * p] * (scale * e0), q1 = acc[0][2 * p + 1] * (scale * e1);
-          float k0 = __fdividef(acc[1][2 * p], e0), k1 = __fdividef(acc[1][2 * p + 1], e1);
+          ee[2 * p] = E[r * LDG + c];
+          ee[2 * p + 1] = E[r * LDG + c + 1];
+          ld2_tile<T>(gQ, r, c, gq[2 * p], gq[2 * p + 1]);
+          ld2_tile<T>(gK, r, c, gk[2 * p], gk[2 * p + 1]);
+        }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          const int r = ep.row(p), c = ep.col(p);
+          float q0 = acc[0][2 * p] * (scale * ee[2 * p]), q1 = acc[0][2 * p + 1] * (scale * ee[2 * p + 1]);
+          float k0 = __fdividef(acc[1][2 * p], ee[2 * p]), k1 = __fdividef(acc[1][2 * p + 1], ee[2 * p + 1]);
           if (poisoned) q0 = q1 = k0 = k1 = kNaN;
           // dgc = q dq - k dk = Q^ dq~ - K^ dk~ (the gated tiles of this item)
-          float gq0, gq1, gk0, gk1;
-          ld2_tile<T>(gQ, r, c, gq0, gq1);
-          ld2_tile<T>(gK, r, c, gk0, gk1);
-          e[0] = gq0 * acc[0][2 * p] - gk0 * acc[1][2 * p];
-          e[1] = gq1 * acc[0][2 * p + 1] - gk1 * acc[1][2 * p + 1];
+          E[r * LDG + c] = gq[2 * p] * acc[0][2 * p] - gk[2 * p] * acc[1][2 * p];
+          E[r * LDG + c + 1] = gq[2 * p + 1] * acc[0][2 * p + 1] - gk[2 * p + 1] * acc[1][2 * p + 1];
           if (whole) {  // this thread's own elements: the gated tiles become the staged outputs
             st2_tile<T>(gQ, r, c, q0, q1);
             st2_tile<T>(gK, r, c, k0, k1);
@@ -935,6 +934,9 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         float acc[3][16];
         ld_acc<3>(ep, {tA, tdA, tS}, acc);
         float dgl0 = 0.f, dgl1 = 0.f;  // rows r0, r0 + 8
+        float dh[16];  // dH' pairs, loaded before the tile stores (see the local-state loop)
+#pragma unroll
+        for (int p = 0; p < 8; ++p) ld2_tile<T>(sDH, ep.row(p), ep.col(p), dh[2 * p], dh[2 * p + 1]);
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
           const int r = ep.row(p), c = ep.col(p);
@@ -942,9 +944,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
           st2_tile<T>(sA, r, c, m0 ? 0.f : acc[0][2 * p], m1 ? 0.f : acc[0][2 * p + 1]);
           st2_tile<T>(sdA, r, c, m0 ? 0.f : acc[1][2 * p], m1 ? 0.f : acc[1][2 * p + 1]);
           // row r of S is key index r: dH'[r, :] . S[r, :]
-          float d0, d1;
-          ld2_tile<T>(sDH, r, c, d0, d1);
-          const float t = fmaf(d0, acc[2][2 * p], d1 * acc[2][2 * p + 1]);
+          const float t = fmaf(dh[2 * p], acc[2][2 * p], dh[2 * p + 1] * acc[2][2 * p + 1]);
           if (p & 1) dgl1 += t; else dgl0 += t;
         }
         dgl0 += __shfl_xor_sync(0xffffffffu, dgl0, 1);
@@ -1062,6 +1062,15 @@ int make_state_map(CUtensorMap* m, const void* base, int dtype, int64_t rows) {
   return encode(m, tmap_dtype(dtype), 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// 2-D view [rows, 64] of fp32 per-item tiles (64 rows per (chunk, head)), box of 32 columns x
+// 64 rows with the 128-byte swizzle (a tile is stored as two column halves).
+int make_f32_rows_map(CUtensorMap* m, const float* base, int64_t rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)D};
+  return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 #define SSLA_DISPATCH_TC(dtype, dtype_g, T, Tg, ...)                                    \
   [&]() -> int {                                                                        \
     if (dtype == SSLA_BF16) {                                                           \
@@ -1099,19 +1108,19 @@ int tc_local_state(int dtype, int dtype_g, int mode, const void* a_src, const vo
                    float* decay, float* escale, unsigned char* xflag, int* xlist, cudaStream_t s) {
   if (MC * H == 0) return SSLA_OK;
   if (int rc = check_sizes(T, MC, H)) return rc;
-  CUtensorMap ma, mb, mg;
+  CUtensorMap ma, mb, mg, mds;
   int rc;
   if ((rc = make_map(&ma, a_src, dtype, T, H, true)) || (rc = make_map(&mb, b_src, dtype, T, H, true)) ||
-      (rc = make_map(&mg, g, dtype_g, T, H, false)))
+      (rc = make_map(&mg, g, dtype_g, T, H, false)) || (rc = make_f32_rows_map(&mds, dS, MC * H * D)))
     return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
-    auto kern = tc_local_state_kernel<T_, Tg, 2>;
-    const size_t smem = 2 * ls_stage_bytes<Tg>() + sizeof(LsSmem) + kAlignSlack;
+    auto kern = tc_local_state_kernel<T_, Tg>;
+    const size_t smem = LS_NS * ls_stage_bytes<Tg>() + 2 * TILE + sizeof(LsSmem) + kAlignSlack;
     unsigned grid = 0;
-    int rc2 = persistent_grid(kern, smem, 64, MC * H, grid);
+    int rc2 = persistent_grid(kern, smem, 64, MC * H, grid, NT + 32);
     if (rc2) return rc2;
-    launch_pdl(kern, dim3(grid), dim3(NT), smem, s, ma, mb, mg, mode, chunk_tab, (int)MC, (int)H, scale, dS, decay,
-               escale, xflag, xlist);
+    launch_pdl(kern, dim3(grid), dim3(NT + 32), smem, s, ma, mb, mg, mds, mode, chunk_tab, (int)MC, (int)H, scale,
+               dS, decay, escale, xflag, xlist);
     SSLA_CHECK_LAUNCH("chunk_gla tc_local_state");
     return SSLA_OK;
   });
