@@ -29,14 +29,24 @@ __global__ void __launch_bounds__(256) scan_fwd_kernel(const Tu* __restrict__ u,
   float acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-  int64_t off = bos * C + c;
-  for (int64_t t = bos; t < eos; ++t, off += C) {
-    float xu[VEC], xg[VEC];
-    Vec<Tu, VEC>::load(u + off, xu);
-    Vec<Tg, VEC>::load(g + off, xg);
+  // tokens in batches of U: the batch's loads are issued together (they do not depend on the
+  // running value), so a sequence costs one memory round trip per U tokens, not per token
+  constexpr int U = 4;
+  for (int64_t t0 = bos; t0 < eos; t0 += U) {
+    float xu[U][VEC], xg[U][VEC];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = __fadd_rn(__fmul_rn(acc[i], xg[i]), xu[i]);
-    Vec<Tu, VEC>::store(h + off, acc);
+    for (int j = 0; j < U; ++j)
+      if (t0 + j < eos) {
+        Vec<Tu, VEC>::load(u + (t0 + j) * C + c, xu[j]);
+        Vec<Tg, VEC>::load(g + (t0 + j) * C + c, xg[j]);
+      }
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (t0 + j < eos) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) acc[i] = __fadd_rn(__fmul_rn(acc[i], xg[j][i]), xu[j][i]);
+        Vec<Tu, VEC>::store(h + (t0 + j) * C + c, acc);
+      }
   }
 }
 
@@ -56,26 +66,40 @@ __global__ void __launch_bounds__(256) scan_bwd_kernel(const Tu* __restrict__ do
   float dh[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) dh[i] = 0.f;
-  for (int64_t t = eos - 1; t >= bos; --t) {
-    const int64_t off = t * C + c;
-    float xdo[VEC], xg[VEC], xh[VEC], xdg[VEC];
-    Vec<Tu, VEC>::load(dout + off, xdo);
-    Vec<Tg, VEC>::load(g + off, xg);
-    if (t > bos) {
-      Vec<Tu, VEC>::load(h + off - C, xh);
-    } else {
+  // tokens in batches of U from the end, loads of a batch issued together (as the forward)
+  constexpr int U = 4;
+  for (int64_t t1 = eos - 1; t1 >= bos; t1 -= U) {
+    float xdo[U][VEC], xg[U][VEC], xh[U][VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) xh[i] = 0.f;
+    for (int j = 0; j < U; ++j) {
+      const int64_t t = t1 - j;
+      if (t >= bos) {
+        Vec<Tu, VEC>::load(dout + t * C + c, xdo[j]);
+        Vec<Tg, VEC>::load(g + t * C + c, xg[j]);
+        if (t > bos) {
+          Vec<Tu, VEC>::load(h + (t - 1) * C + c, xh[j]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) xh[j][i] = 0.f;
+        }
+      }
     }
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      dh[i] = __fadd_rn(dh[i], xdo[i]);
-      xdg[i] = __fmul_rn(dh[i], xh[i]);
-    }
-    Vec<Tg, VEC>::store(dg + off, xdg);
-    Vec<Tu, VEC>::store(du + off, dh);
+    for (int j = 0; j < U; ++j) {
+      const int64_t t = t1 - j;
+      if (t >= bos) {
+        float xdg[VEC];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) dh[i] = __fmul_rn(dh[i], xg[i]);
+        for (int i = 0; i < VEC; ++i) {
+          dh[i] = __fadd_rn(dh[i], xdo[j][i]);
+          xdg[i] = __fmul_rn(dh[i], xh[j][i]);
+        }
+        Vec<Tg, VEC>::store(dg + t * C + c, xdg);
+        Vec<Tu, VEC>::store(du + t * C + c, dh);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) dh[i] = __fmul_rn(dh[i], xg[j][i]);
+      }
+    }
   }
 }
 
