@@ -45,39 +45,19 @@ __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __rest
   const int64_t c = (idx - seq * CV) * 4;
   const int64_t bos = cu[seq], eos = cu[seq + 1];
   float h[4] = {0.f, 0.f, 0.f, 0.f};
-  // events in batches of U: the batch's row indices, then its rows, are loaded together (they do
-  // not depend on the running state), so a patch costs two round trips per U events
-  constexpr int U = 4;
-  for (int64_t t0 = bos; t0 < eos; t0 += U) {
-    int64_t kk[U], dd[U];
+  for (int64_t t = bos; t < eos; ++t) {
+    const float* row = y + key[t] * 3 * C + c;
+    const float4 q = *reinterpret_cast<const float4*>(row);
+    const float4 v = *reinterpret_cast<const float4*>(row + C);
+    const float4 gp = *reinterpret_cast<const float4*>(row + 2 * C);
+    const float qa[4] = {q.x, q.y, q.z, q.w}, va[4] = {v.x, v.y, v.z, v.w}, ga[4] = {gp.x, gp.y, gp.z, gp.w};
+    float o[4];
 #pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (t0 + j < eos) {
-        kk[j] = key[t0 + j];
-        dd[j] = dst[t0 + j];
-      }
-    float4 q[U], v[U], gp[U];
-#pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (t0 + j < eos) {
-        const float* row = y + kk[j] * 3 * C + c;
-        q[j] = *reinterpret_cast<const float4*>(row);
-        v[j] = *reinterpret_cast<const float4*>(row + C);
-        gp[j] = *reinterpret_cast<const float4*>(row + 2 * C);
-      }
-#pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (t0 + j < eos) {
-        const float qa[4] = {q[j].x, q[j].y, q[j].z, q[j].w}, va[4] = {v[j].x, v[j].y, v[j].z, v[j].w},
-                    ga[4] = {gp[j].x, gp[j].y, gp[j].z, gp[j].w};
-        float o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          h[i] = __fadd_rn(__fmul_rn(h[i], sigmoid_f(ga[i])), va[i]);
-          o[i] = __fmul_rn(qa[i], h[i]);
-        }
-        *reinterpret_cast<float4*>(z + dd[j] * C + c) = make_float4(o[0], o[1], o[2], o[3]);
-      }
+    for (int i = 0; i < 4; ++i) {
+      h[i] = __fadd_rn(__fmul_rn(h[i], sigmoid_f(ga[i])), va[i]);
+      o[i] = __fmul_rn(qa[i], h[i]);
+    }
+    *reinterpret_cast<float4*>(z + dst[t] * C + c) = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
