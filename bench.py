@@ -47,13 +47,14 @@ FWD_BYTES = 4 * _E * 2 + _S + _E * 2 + _S
 BWD_BYTES = 5 * _E * 2 + 2 * _S + 3 * _E * 2 + _E * 4 + _S
 ALG_BYTES = FWD_BYTES + BWD_BYTES
 ALG_FLOPS = 12 * 2 * K * V * TOKENS * H
-# DRAM bytes (read + write) of one backward call, from the ncu capture summarised in
-# profiles/chunk_gla_c2_dram_traffic.md (cold caches)
-BWD_DRAM_BYTES = 124_600_000
+# DRAM bytes (read + write) of one ssla_chunk_gla_bwd call: dram__bytes_read.sum +
+# dram__bytes_write.sum of its launches (adjoint increments, reverse state scan, tensor-core
+# backward, exact path), from an ncu capture of `bench.py --leg profile-chunk` (cold L2).
+BWD_DRAM_BYTES = 105_900_000
 METRIC = "chunk-GLA fwd+bwd tokens/s"
-# fwd: chunk table, local state, state scan, tensor-core output, exact-path launch; bwd: the
-# same five (chunk table, adjoint increments, reverse scan, tensor-core backward, exact path)
-LAUNCHES_PER_STEP = 10
+# fwd: chunk table, local state, state scan, tensor-core output, exact-path launch; bwd reuses the
+# saved chunk table: adjoint increments, reverse scan, tensor-core backward, exact path
+LAUNCHES_PER_STEP = 9
 
 
 def make_inputs(seed: int, device="cpu"):
@@ -445,10 +446,15 @@ def recurrent_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
         "gpu_launches": steps, "cpu_baseline": cpu, "clocks": clk.summary()}
 
 
+# count, block scan, block prefix, fill, one-pass pool (plus a memset of the counts)
+POOL_LAUNCHES = 5
+
+
 def pool_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
     """scatter max + mean into 2x2 / 4x4 cells and gather back, through the
-    torch_scatter-equivalent CSR path (cell ids of pixel-ordered rows are not monotonic, so each
-    step builds the row lists by a counting sort).  The CPU leg also checks the k=2 results."""
+    one-pass ``ssla_scatter_pool`` (cell ids of pixel-ordered rows are not monotonic, so each
+    step builds the row lists by a counting sort, then one kernel reduces every cell and writes
+    its max back to the cell's rows).  The CPU leg also checks the k=2 results bit for bit."""
     from ssla_b200.ops import segment as seg
     from ssla_b200.synthetic import pooling_rows
 
@@ -466,20 +472,15 @@ def pool_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
             holder = {}
 
             def step():
-                off, rows = seg.segment_csr(inv, S)
-                mx, _ = seg.segment_reduce(feats, off, rows, seg.MAX)
-                mn, _ = seg.segment_reduce(feats, off, rows, seg.MEAN)
-                holder["back"] = seg.gather_rows(mx, inv)
-                holder["max"], holder["mean"] = mx, mn
+                holder.update(seg.scatter_pool(feats, inv, S, want_back=True))
 
             for _ in range(warmup):
                 step()
             torch.cuda.synchronize(dev)
             secs = _max_over_ranks(_event_time(step, steps, stream, flush), dist, dev)
             out[kk] = holder
-            b_scatter = R * C * 2 + R * 8 + S * C * 2
-            b_gather = S * C * 2 + R * 8 + R * C * 2
-            alg = 2 * b_scatter + b_gather
+            # rows and their cell ids read once; pooled max and mean and the rows' gathered max written
+            alg = R * C * 2 + R * 8 + 2 * S * C * 2 + R * C * 2
             gbs = alg * steps / secs / 1e9
             lines[f"k{kk}"] = {"rows": R, "cells": S, "ms_per_step": 1e3 * secs / steps,
                                "rows_per_s": world * R * steps / secs, "achieved_gbs": gbs, "frac": gbs / hbm,
@@ -515,7 +516,7 @@ def pool_line(dev, world, rank, dist, local, steps, warmup, want_cpu):
                      "frac": k2["frac"], "peak_source": which, "alg_bytes_per_step": k2["alg_bytes_per_step"],
                      "traffic": None},
         "checked_bit_exact_vs_cpu": checked,
-        "gpu_launches": 9 * steps, "cpu_baseline": cpu, "clocks": clk.summary()}
+        "gpu_launches": POOL_LAUNCHES * steps, "cpu_baseline": cpu, "clocks": clk.summary()}
 
 
 def run_other(args):
@@ -594,6 +595,69 @@ def run_other(args):
         dist.destroy_process_group()
 
 
+def profile_leg(args):
+    """Small fixed workloads for ncu captures of one kernel family (no timing, no JSON):
+    chunk (config 2 fwd+bwd through the C ABI), recurrent (one streaming step of 16384
+    sequences: 268 MB of state, larger than L2), pool (config 4 k=2 one-pass pooling), scan
+    (the largest MOS_S scan shape, fwd+bwd).  Each runs ``--steps`` times after nothing else."""
+    from ssla_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    L = _lib.load()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    case = args.leg[len("profile-"):]
+    if case == "chunk":
+        d = {n: t.to(dev) for n, t in make_inputs(1000).items()}
+        BF = _lib.BF16
+        wsb = L.ssla_chunk_gla_workspace_bytes(B, B * T, H, K, V, BF, BF)
+        stb = L.ssla_chunk_gla_states_bytes(B, B * T, H, K, V, BF, BF)
+        ws = torch.empty(wsb, device=dev, dtype=torch.uint8)
+        st = torch.empty(stb, device=dev, dtype=torch.uint8)
+        o, ht = torch.empty_like(d["v"]), torch.empty(B, H, K, V, device=dev)
+        dq, dk, dv = torch.empty_like(d["q"]), torch.empty_like(d["k"]), torch.empty_like(d["v"])
+        dg, dh0 = torch.empty(B * T, H, K, device=dev), torch.empty(B, H, K, V, device=dev)
+        for _ in range(args.steps):
+            _lib.check(L.ssla_chunk_gla_fwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["g"].data_ptr(),
+                                            BF, BF, d["cu"].data_ptr(), B, B * T, H, K, V, K ** -0.5,
+                                            d["h0"].data_ptr(), o.data_ptr(), ht.data_ptr(), st.data_ptr(), stb,
+                                            ws.data_ptr(), wsb, sp), "fwd")
+            _lib.check(L.ssla_chunk_gla_bwd(d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(), d["g"].data_ptr(),
+                                            BF, BF, d["cu"].data_ptr(), B, B * T, H, K, V, K ** -0.5, st.data_ptr(),
+                                            stb, d["do"].data_ptr(), d["dht"].data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                            dv.data_ptr(), dg.data_ptr(), dh0.data_ptr(), ws.data_ptr(), wsb, sp),
+                       "bwd")
+    elif case == "recurrent":
+        N, Hh, Kk, Vv = 16384, 4, 32, 32
+        gen = torch.Generator().manual_seed(0)
+        mk = lambda dd: torch.randn(N, Hh, dd, generator=gen).to(dev, torch.bfloat16)
+        q, k, v = mk(Kk), mk(Kk), mk(Vv)
+        g = (F.logsigmoid(torch.randn(N, Hh, Kk, generator=gen)) / 16).to(dev, torch.bfloat16)
+        s0 = torch.randn(N, Hh, Kk, Vv, device=dev)
+        s1, o = torch.empty_like(s0), torch.empty(N, Hh, Vv, device=dev, dtype=torch.bfloat16)
+        cu = torch.arange(N + 1, device=dev)
+        for _ in range(args.steps):
+            _lib.check(L.ssla_recurrent_gla_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), 1, 1,
+                                                cu.data_ptr(), N, N, Hh, Kk, Vv, Kk ** -0.5, s0.data_ptr(),
+                                                o.data_ptr(), s1.data_ptr(), sp), "recurrent")
+    elif case == "pool":
+        from ssla_b200.ops import segment as seg
+        from ssla_b200.synthetic import pooling_rows
+
+        feats, _, cells = pooling_rows(seed=0)
+        feats, (inv, S) = feats.to(dev), cells[2]
+        inv = inv.to(dev)
+        for _ in range(args.steps):
+            seg.scatter_pool(feats, inv, S, want_back=True)
+    elif case == "scan":
+        from ssla_b200.ops.common.scan import scan
+
+        u, g, cu, dh = scan_inputs(dev)[1]
+        for _ in range(args.steps):
+            scan(u.detach().requires_grad_(), g.detach().requires_grad_(), cu).backward(dh)
+    torch.cuda.synchronize(dev)
+    print(f"profile case {case}: {args.steps} step(s) done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -612,10 +676,15 @@ def main():
     ap.add_argument("--triton-full-autotune", action="store_true",
                     help="let the reference's Triton autotuner try every configuration (did not finish within "
                          "45 minutes here); by default each kernel keeps its first configuration")
-    ap.add_argument("--leg", default=None, choices=["triton-reference"], help=argparse.SUPPRESS)
+    ap.add_argument("--leg", default=None,
+                    choices=["triton-reference", "profile-chunk", "profile-recurrent", "profile-pool", "profile-scan"],
+                    help="triton-reference: internal subprocess leg; profile-*: small fixed workload of one "
+                         "kernel family for ncu captures (runs --steps times, prints no result line)")
     args = ap.parse_args()
     if args.leg == "triton-reference":
         return run_triton_reference(args)
+    if args.leg and args.leg.startswith("profile-"):
+        return profile_leg(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload != "chunk":
@@ -794,10 +863,14 @@ def main():
                    "per_rank_tokens": TOKENS, "l2": "flushed (256 MB write) before every timed step",
                    "parallelism": f"independent sequence shards x{world}"},
         "roofline": {"bound": "hbm",
-                     "scope": "dominant launch: the ssla_chunk_gla_bwd call (chunk table, adjoint increments, "
+                     "scope": "dominant launch: the ssla_chunk_gla_bwd call (adjoint increments, "
                               "reverse state scan, tensor-core backward, exact-path launch), CUDA events",
                      "achieved": bwd_gbs, "peak": hbm, "unit": "GB/s", "frac": bwd_gbs / hbm,
-                     "peak_source": which, "traffic": BWD_DRAM_BYTES, "alg_bytes": BWD_BYTES,
+                     "peak_source": which, "traffic": BWD_DRAM_BYTES,
+                     "traffic_source": "constant: ncu dram__bytes_read.sum + dram__bytes_write.sum of the bwd "
+                                       "call's launches (bench.py --leg profile-chunk, cold L2), not measured "
+                                       "in this run",
+                     "alg_bytes": BWD_BYTES,
                      "backward_ms": bwd_s * 1e3,
                      "forward": {"achieved": fwd_gbs, "frac": fwd_gbs / hbm, "ms": fwd_s * 1e3},
                      "step": {"achieved": step_gbs, "frac": step_gbs / hbm, "alg_bytes": ALG_BYTES},

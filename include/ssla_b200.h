@@ -170,6 +170,19 @@ int ssla_segment_reduce(const void* src, int dtype, const int64_t* seg_offsets, 
 /* out[r,:] = src[index[r],:]  (row gather; inverse of pooling, layers/sparse_pooling.py) */
 int ssla_gather_rows(const void* src, int dtype, const int64_t* index, int64_t R, int64_t C,
                      void* out, ssla_stream_t stream);
+/* Sparse pooling in one pass (layers/sparse_pooling.py:33 with pool_func = scatter_max and
+ * scatter_mean, followed by the gather back pooled[index]): from an arbitrary row->segment
+ * index, out_max [S,C] (+ arg [S,C], first maximal row, R for empty segments), out_mean [S,C]
+ * and back [R,C] = out_max[index[r]], all with the semantics of ssla_segment_reduce above
+ * (same results bit for bit).  Every output is optional (NULL); back needs out_max.
+ * seg_offsets [S+1] (optional) receives the segment offsets of the counting sort.  Rows whose
+ * index lies outside [0, S) are ignored and their back row is left untouched.  The one-pass
+ * kernel handles C * element size a power-of-two multiple of 16 bytes up to 512 bytes with
+ * 16-byte aligned buffers; other shapes run the CSR + reductions + gather sequence. */
+size_t ssla_scatter_pool_workspace_bytes(int64_t R, int64_t S);
+int ssla_scatter_pool(const void* src, int dtype, const int64_t* index, int64_t R, int64_t S, int64_t C,
+                      void* out_max, int64_t* arg, void* out_mean, void* back, int64_t* seg_offsets,
+                      void* workspace, size_t workspace_bytes, ssla_stream_t stream);
 /* out[d,:] = sum over p with index[p]==d of src[p,:], fp32 sum in ascending p; zero rows
  * for unused d.  Deterministic replacement of utils/async_utils.py:243-264
  * (zeros(E,C).index_add_(0, idx, src)). */

@@ -46,6 +46,8 @@ SIGNATURES = {
     "ssla_segment_csr": (i32, [p, i64, i64, p, p, p, sz, p]),
     "ssla_segment_reduce": (i32, [p, i32, p, p, i64, i64, i64, i32, p, p, p]),
     "ssla_gather_rows": (i32, [p, i32, p, i64, i64, p, p]),
+    "ssla_scatter_pool_workspace_bytes": (sz, [i64, i64]),
+    "ssla_scatter_pool": (i32, [p, i32, p, i64, i64, i64, p, p, p, p, p, p, sz, p]),
     "ssla_index_add_rows_workspace_bytes": (sz, [i64, i64]),
     "ssla_index_add_rows": (i32, [p, i32, p, i64, i64, i64, p, p, sz, p]),
     "ssla_mos_patch_scan_fwd": (i32, [p, p, p, p, i64, i64, p, p]),

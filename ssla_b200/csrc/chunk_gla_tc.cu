@@ -403,14 +403,31 @@ __device__ __forceinline__ void producer_loop(int MC, int H, const longlong2* __
   }
 }
 
-// Consumer item walk: calls body(item, stage, parity) for the CTA's items in order.
+// Consumer item walk: calls body(item, stage, parity, exact) for the CTA's items in order;
+// `exact` is the item's exact-path flag (xflag, when given).  The next item's chunk-table entry
+// and flag are loaded before the current body runs, so no global-load latency sits between two
+// items.
 template <int NS, class Body>
-__device__ __forceinline__ void consumer_loop(int MC, int H, const longlong2* __restrict__ tab, Body body) {
+__device__ __forceinline__ void consumer_loop(int MC, int H, const longlong2* __restrict__ tab,
+                                              const unsigned char* __restrict__ xflag, Body body) {
   const int G = gridDim.x, gq = G / H, gr = G % H;
   Cursor c{(int)blockIdx.x / H, (int)blockIdx.x % H};
+  auto flag_of = [&](const Cursor& k) -> bool {
+    return xflag && k.cid < MC && xflag[(int64_t)k.cid * H + k.head] != 0;
+  };
+  longlong2 e = item_entry(c, MC, tab);
+  bool f = flag_of(c);
   Item x;
-  for (int i = 0; decode_item(c, item_entry(c, MC, tab), x); ++i, c.advance(gq, gr, H))
-    body(x, i % NS, (uint32_t)((i / NS) & 1));
+  for (int i = 0; decode_item(c, e, x); ++i) {
+    Cursor cn = c;
+    cn.advance(gq, gr, H);
+    const longlong2 en = item_entry(cn, MC, tab);
+    const bool fn = flag_of(cn);
+    body(x, i % NS, (uint32_t)((i / NS) & 1), f);
+    c = cn;
+    e = en;
+    f = fn;
+  }
 }
 
 // End of a producer/consumer kernel: every thread (producer included) meets; the TMA stores of
@@ -469,7 +486,7 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_local_state_kernel(
     uint32_t phase = 0;
     const Epi ep;
     const Own me;
-    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+    consumer_loop<NS>(MC, H, chunk_tab, nullptr, [&](const Item& x, int st, uint32_t par, bool) {
       ++pitem;
       PHASE(pitem, 21);
       counted_wait(&full[st], par, bad);
@@ -651,7 +668,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
         }
       }
     };
-    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+    consumer_loop<NS>(MC, H, chunk_tab, xflag, [&](const Item& x, int st, uint32_t par, bool exact) {
       counted_wait(&full[st], par, bad);
       unsigned char* sQ = smem + st * STAGE;
       unsigned char* sK = sQ + TILE;
@@ -661,7 +678,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
         zero_tail<Tg>(sQ, 3, sH + TILE, x.len, me);
         cbar();
       }
-      if (xflag[x.id(H)] || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
+      if (exact || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
         if (pending) finish(prev, prev_b);
         pending = false;
         if (*bad) {
@@ -874,7 +891,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
       }
       PHASE(ci - 1, 13);
     };
-    consumer_loop<NS>(MC, H, chunk_tab, [&](const Item& x, int st, uint32_t par) {
+    consumer_loop<NS>(MC, H, chunk_tab, xflag, [&](const Item& x, int st, uint32_t par, bool exact) {
       PHASE(ci, 0);
       counted_wait(&full[st], par, bad);
       PHASE(ci, 1);
@@ -888,7 +905,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         zero_tail<Tg>(rQ, 4, sDH + TILE, x.len, me);
         cbar();
       }
-      if (xflag[x.id(H)] || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
+      if (exact || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
         if (pending) finish(prev, prev_b);
         pending = false;
         if (*bad) poison_rows(x);

@@ -55,6 +55,45 @@ template <> struct Vec<__half, 4> {
   }
 };
 
+// 16-byte vectors of 16-bit types (8 elements).
+template <typename T2> struct Pair16;
+template <> struct Pair16<__nv_bfloat16> {
+  using P = __nv_bfloat162;
+  static __device__ __forceinline__ P pack(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+template <> struct Pair16<__half> {
+  using P = __half2;
+  static __device__ __forceinline__ P pack(float a, float b) { return __floats2half2_rn(a, b); }
+};
+
+template <typename T> struct Vec8x16 {
+  using P = typename Pair16<T>::P;
+  static __device__ __forceinline__ void load(const T* p, float* x) {
+    uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    unpack(r, x);
+  }
+  static __device__ __forceinline__ void unpack(uint4 r, float* x) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      P a = *reinterpret_cast<const P*>(&w[i]);
+      x[2 * i] = __low2float(a);
+      x[2 * i + 1] = __high2float(a);
+    }
+  }
+  static __device__ __forceinline__ void store(T* p, const float* x) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      P a = Pair16<T>::pack(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&a);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+template <> struct Vec<__nv_bfloat16, 8> : Vec8x16<__nv_bfloat16> {};
+template <> struct Vec<__half, 8> : Vec8x16<__half> {};
+
 inline bool aligned_to(const void* p, size_t a) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 }  // namespace ssla

@@ -81,6 +81,41 @@ def gather_rows(src: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def scatter_pool(src: torch.Tensor, index: torch.Tensor, num_segments: int, want_max: bool = True,
+                 want_mean: bool = True, want_back: bool = False, want_arg: bool = False,
+                 want_offsets: bool = False) -> dict:
+    """Scatter max and mean of the rows of ``src [R, C]`` into ``num_segments`` segments of an
+    arbitrary ``index [R]``, plus the gather of the max back to every row (``back = max[index]``),
+    in one pass (``ssla_scatter_pool``).  Returns a dict with the requested of ``max``, ``arg``,
+    ``mean``, ``back`` and ``offsets``; results equal :func:`segment_reduce` / :func:`gather_rows`
+    bit for bit."""
+    _lib.require_cuda(src, index, what="scatter_pool")
+    src = src.contiguous()
+    index = _i64(index)
+    R, C = src.shape
+    S = int(num_segments)
+    L = _lib.load()
+    dev = src.device
+    res = {}
+    if want_max or want_back or want_arg:
+        res["max"] = torch.empty((S, C), device=dev, dtype=src.dtype)
+    if want_arg:
+        res["arg"] = torch.empty((S, C), device=dev, dtype=torch.int64)
+    if want_mean:
+        res["mean"] = torch.empty((S, C), device=dev, dtype=src.dtype)
+    if want_back:
+        res["back"] = torch.empty((R, C), device=dev, dtype=src.dtype)
+    if want_offsets:
+        res["offsets"] = torch.empty(S + 1, device=dev, dtype=torch.int64)
+    nb = L.ssla_scatter_pool_workspace_bytes(R, S)
+    ws = torch.empty(max(nb, 1), device=dev, dtype=torch.uint8)
+    _lib.check(L.ssla_scatter_pool(src.data_ptr(), _lib.dtype_code(src), index.data_ptr(), R, S, C,
+                                   _lib.ptr(res.get("max")), _lib.ptr(res.get("arg")), _lib.ptr(res.get("mean")),
+                                   _lib.ptr(res.get("back")), _lib.ptr(res.get("offsets")), ws.data_ptr(), nb,
+                                   _lib.stream_of(src)), "scatter_pool")
+    return res
+
+
 def index_add_rows(src: torch.Tensor, index: torch.Tensor, num_rows: int) -> torch.Tensor:
     """``zeros(num_rows, C).index_add_(0, index, src)`` with a fixed (ascending-row) sum order."""
     _lib.require_cuda(src, index, what="index_add_rows")
@@ -164,3 +199,45 @@ def index_add_rows_ad(src: torch.Tensor, index: torch.Tensor, num_rows: int) -> 
 def segment_reduce_ad(src: torch.Tensor, seg_of_row: torch.Tensor, offsets: torch.Tensor, rows, op: int):
     """Differentiable segment reduction; ``seg_of_row`` is the segment id of every row."""
     return _SegmentReduce.apply(src.contiguous(), _i64(seg_of_row), offsets, rows, op)
+
+
+class _ScatterPool(torch.autograd.Function):
+    """One-pass scatter max (with argmax) or mean of an arbitrary index, with gradients:
+    max routes the output gradient to the arg-max row, mean spreads it over the segment."""
+
+    @staticmethod
+    def forward(ctx, src, index, num_segments, op):
+        is_max = op == MAX
+        res = scatter_pool(src, index, num_segments, want_max=is_max, want_mean=not is_max, want_arg=is_max,
+                           want_offsets=not is_max)
+        ctx.op = op
+        ctx.shape = src.shape
+        if is_max:
+            ctx.save_for_backward(res["arg"])
+            ctx.mark_non_differentiable(res["arg"])
+            return res["max"], res["arg"]
+        ctx.save_for_backward(index, res["offsets"])
+        return res["mean"], res["offsets"]
+
+    @staticmethod
+    def backward(ctx, grad, _unused):
+        R, C = ctx.shape
+        grad = grad.contiguous()
+        if ctx.op == MAX:
+            (arg,) = ctx.saved_tensors
+            gin = torch.zeros((R + 1, C), device=grad.device, dtype=grad.dtype)  # row R: empty segments
+            gin.scatter_(0, arg, grad)
+            return gin[:R], None, None, None
+        index, offsets = ctx.saved_tensors
+        cnt = (offsets[1:] - offsets[:-1]).clamp(min=1).to(grad.dtype)
+        return gather_rows(grad, index) / gather_rows(cnt.view(-1, 1).contiguous(), index), None, None, None
+
+
+def scatter_max_ad(src: torch.Tensor, index: torch.Tensor, num_segments: int):
+    """Differentiable one-pass ``(max, argmax)`` of an arbitrary index (torch_scatter.scatter_max)."""
+    return _ScatterPool.apply(src.contiguous(), _i64(index), int(num_segments), MAX)
+
+
+def scatter_mean_ad(src: torch.Tensor, index: torch.Tensor, num_segments: int) -> torch.Tensor:
+    """Differentiable one-pass mean of an arbitrary index (torch_scatter.scatter_mean)."""
+    return _ScatterPool.apply(src.contiguous(), _i64(index), int(num_segments), MEAN)[0]

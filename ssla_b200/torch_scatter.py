@@ -3,7 +3,8 @@
 Drop-in for the imports of layers/sparse_pooling.py:5.  The index may be ``[R]`` or the
 ``[R, C]`` expansion of one row index that sparse pooling passes (layers/sparse_pooling.py:33);
 only ``dim=0`` on 2-D ``src`` is supported, which is the only form the reference uses.  The
-reduction runs on the GPU through a deterministic CSR (see ``ssla_b200.ops.segment``).
+reductions run on the GPU: max and mean through the one-pass ``ssla_scatter_pool`` kernel,
+sum through a deterministic CSR (see ``ssla_b200.ops.segment``).
 """
 from __future__ import annotations
 
@@ -37,15 +38,12 @@ scatter_add = scatter_sum
 
 def scatter_mean(src, index, dim=-1, out=None, dim_size: Optional[int] = None):
     index, S = _prep(src, index, dim, dim_size)
-    off, rows = _seg.segment_csr(index, S)
-    return _seg.segment_reduce_ad(src, index, off, rows, _seg.MEAN)
+    return _seg.scatter_mean_ad(src, index, S)
 
 
 def scatter_max(src, index, dim=-1, out=None, dim_size: Optional[int] = None):
     index, S = _prep(src, index, dim, dim_size)
-    off, rows = _seg.segment_csr(index, S)
-    arg = _seg.segment_reduce(src.detach(), off, rows, _seg.MAX, want_arg=True)[1]
-    return _seg.segment_reduce_ad(src, index, off, rows, _seg.MAX), arg
+    return _seg.scatter_max_ad(src, index, S)
 
 
 def scatter(src, index, dim=-1, out=None, dim_size=None, reduce: str = "sum"):

@@ -177,6 +177,10 @@ def test_c4_pooling_full_size_bit_exact(k):
     mn2, _ = seg.segment_reduce(f, off, rows, seg.MEAN)
     assert torch.equal(mx2.cpu(), mx_r) and torch.equal(arg2.cpu(), arg_r) and torch.equal(mn2.cpu(), mean_r)
     assert torch.equal(seg.gather_rows(mx2, ic).cpu(), back_r)
+    # the one-pass kernel (max + argmax + mean + gather back)
+    res = seg.scatter_pool(f, ic, S, want_back=True, want_arg=True)
+    assert torch.equal(res["max"].cpu(), mx_r) and torch.equal(res["arg"].cpu(), arg_r)
+    assert torch.equal(res["mean"].cpu(), mean_r) and torch.equal(res["back"].cpu(), back_r)
     # sorted-segment path on the rows re-ordered by cell (stable): same values, argmax mapped back
     perm = torch.sort(inv, stable=True)[1]
     ps = perm.cuda()
@@ -186,3 +190,51 @@ def test_c4_pooling_full_size_bit_exact(k):
     assert torch.equal(mx3.cpu(), mx_r) and torch.equal(mn3.cpu(), mean_r)
     a3 = arg3.cpu()
     assert torch.equal(torch.where(a3 < R, perm[a3.clamp(max=R - 1)], a3), arg_r)
+
+
+@pytest.mark.parametrize("dtype,C", [(torch.bfloat16, 64), (torch.float32, 64), (torch.float16, 256),
+                                     (torch.bfloat16, 8), (torch.float32, 4), (torch.bfloat16, 24)])
+def test_scatter_pool_one_pass_bit_exact(dtype, C):
+    """``ssla_scatter_pool`` (max + argmax + mean + gather back in one pass) against the CPU
+    oracle for every lane-group width (C * element size from 16 to 512 bytes), the general-width
+    sequence (C=24 bf16), segments longer than the lane group (sorted through the rank-count
+    path), empty segments, ties, and rows with out-of-range ids (ignored; their back row is not
+    written)."""
+    from ssla_b200.ops import segment as seg
+
+    gen = torch.Generator().manual_seed(C)
+    R, S = 30000, 6000
+    idx = torch.randint(0, S, (R,), generator=gen)
+    idx[:70] = 11                      # a segment far longer than any lane group
+    idx[100:110] = -1                  # out of range: ignored
+    idx[200:205] = S
+    idx[idx == 5] = 6                  # segment 5 empty
+    src = torch.randn(R, C, generator=gen)
+    src[::9] = src[4]
+    src = src.to(dtype)
+    keep = (idx >= 0) & (idx < S)
+    rows = keep.nonzero().squeeze(1)
+    mx_r, arg_r = oseg.scatter_max(src[rows], idx[rows], S)
+    arg_r = torch.where(arg_r < rows.numel(), rows[arg_r.clamp(max=rows.numel() - 1)], torch.full_like(arg_r, R))
+    mean_r = oseg.scatter_mean(src[rows], idx[rows], S)
+    res = seg.scatter_pool(src.cuda(), idx.cuda(), S, want_back=True, want_arg=True, want_offsets=True)
+    assert torch.equal(res["max"].cpu(), mx_r)
+    assert torch.equal(res["arg"].cpu(), arg_r)
+    assert torch.equal(res["mean"].cpu(), mean_r)
+    assert torch.equal(res["back"].cpu()[rows], mx_r[idx[rows]])
+    cnt = torch.bincount(idx[rows], minlength=S)
+    assert res["offsets"].cpu().tolist() == [0] + torch.cumsum(cnt, 0).tolist()
+    # subsets of the outputs
+    only_mean = seg.scatter_pool(src.cuda(), idx.cuda(), S, want_max=False)
+    assert set(only_mean) == {"mean"} and torch.equal(only_mean["mean"].cpu(), mean_r)
+
+
+def test_scatter_pool_empty_inputs():
+    from ssla_b200.ops import segment as seg
+
+    res = seg.scatter_pool(torch.zeros(0, 64, dtype=torch.bfloat16).cuda(), torch.zeros(0, dtype=torch.int64).cuda(),
+                           3, want_arg=True, want_offsets=True)
+    assert res["max"].abs().sum() == 0 and res["mean"].abs().sum() == 0
+    assert (res["arg"] == 0).all() and res["offsets"].tolist() == [0, 0, 0, 0]
+    res = seg.scatter_pool(torch.randn(4, 64).cuda(), torch.tensor([0, 0, 1, 1]).cuda(), 0)
+    assert res["max"].shape == (0, 64)
