@@ -593,11 +593,13 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_local_state_kernel(
 
 // --------------------------------------------------------------------------- forward output
 // stage: q | k | v | H' tiles | raw gate.  Q^ and K^ are gated in place.
+// Two CTAs per SM (two independent item pipelines): two stages each, and the staged output
+// tile shares its buffer with the score tile A.
 template <typename Tg> __host__ __device__ constexpr int fo_stage_bytes() { return 4 * TILE + gate_bytes<Tg>(); }
-constexpr int FO_NS = 3;
+constexpr int FO_NS = 2;
 
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
+__global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mg,
     const __grid_constant__ CUtensorMap mh, const __grid_constant__ CUtensorMap mo,
@@ -608,8 +610,8 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
   unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = fo_stage_bytes<Tg>();
   unsigned char* sA = smem + NS * STAGE;
-  unsigned char* sOut = sA + TILE;
-  GateSmem& G = *reinterpret_cast<GateSmem*>(sOut + TILE);
+  unsigned char* sOut = sA;  // the previous item's output is staged in the score tile's buffer
+  GateSmem& G = *reinterpret_cast<GateSmem*>(sA + TILE);
   __shared__ uint64_t bars[2 + 2 * NS];  // batch 1, batch 2, full[NS], empty[NS]
   __shared__ uint32_t tbase_s;
   __shared__ int s_bad;
@@ -700,17 +702,18 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_fwd_o_kernel(
         commit(&bars[0]);
       }
       if (pending) finish(prev, prev_b);
+      if (tid == 0) bulk_wait_read_all();  // the staged output (same buffer as A) has been read
       wait_mma(&bars[0], ph1, bad);
       {
         float a[1][16];
         ld_acc<1>(ep, {tA}, a);
+        cbar();  // thread 0's wait above covers every thread's writes to A below
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
           const int r = ep.row(p), c = ep.col(p);
           st2_tile<T>(sA, r, c, c > r ? 0.f : a[0][2 * p], c + 1 > r ? 0.f : a[0][2 * p + 1]);
         }
       }
-      if (tid == 0) bulk_wait_read_all();  // the staged output tile is free again
       operands_ready();
       if (tid == 0) {
         mma64(tO, sA, 0, sV, 1, idesc_f16(64, 64, F, 0, 1), true);  // O += A V
@@ -1156,7 +1159,7 @@ int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v
     return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
     auto kern = tc_fwd_o_kernel<T_, Tg>;
-    const size_t smem = FO_NS * fo_stage_bytes<Tg>() + 2 * TILE + sizeof(GateSmem) + kAlignSlack;
+    const size_t smem = FO_NS * fo_stage_bytes<Tg>() + TILE + sizeof(GateSmem) + kAlignSlack;
     unsigned grid = 0;
     int rc2 = persistent_grid(kern, smem, 256, MC * H, grid, NT + 32);
     if (rc2) return rc2;

@@ -49,6 +49,8 @@ __global__ void count_kernel(const int64_t* __restrict__ index, int64_t R, int64
 __global__ void __launch_bounds__(1024) scan_blocks_kernel(const int* __restrict__ counts,
                                                            int64_t S, int64_t* __restrict__ off,
                                                            int64_t* __restrict__ block_sums) {
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ int64_t ws[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t i = (int64_t)blockIdx.x * 1024 + tid;
@@ -104,6 +106,8 @@ __global__ void add_block_base_kernel(int64_t* __restrict__ off, int64_t S,
 __global__ void __launch_bounds__(1024) add_block_prefix_kernel(int64_t* __restrict__ off, int64_t S,
                                                                 const int64_t* __restrict__ block_sums,
                                                                 int64_t nb, int* __restrict__ counts) {
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ int64_t red[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int64_t part = 0;
@@ -126,6 +130,8 @@ __global__ void __launch_bounds__(1024) add_block_prefix_kernel(int64_t* __restr
 __global__ void fill_kernel(const int64_t* __restrict__ index, int64_t R, int64_t S,
                             const int64_t* __restrict__ off, int* __restrict__ cursor,
                             int64_t* __restrict__ tmp) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= R) return;
   const int64_t s = index[r];
@@ -137,6 +143,8 @@ __global__ void fill_kernel(const int64_t* __restrict__ index, int64_t R, int64_
 // One warp per segment: rows[off[s] + rank(x)] = x, rank = #{y in segment : y < x}.
 __global__ void rank_sort_kernel(const int64_t* __restrict__ off, int64_t S,
                                  const int64_t* __restrict__ tmp, int64_t* __restrict__ rows) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (s >= S) return;
@@ -348,19 +356,25 @@ template <> struct Row16<float> {
 template <typename T, int G, bool ARG>
 __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
     const T* __restrict__ src, const int64_t* __restrict__ off, const int64_t* __restrict__ tmp,
-    int64_t* __restrict__ sorted, int64_t R, int64_t S, int64_t C, T* __restrict__ out_max,
-    int64_t* __restrict__ arg, T* __restrict__ out_mean, T* __restrict__ back) {
+    int64_t* __restrict__ sorted, int R, int S, T* __restrict__ out_max, int64_t* __restrict__ arg,
+    T* __restrict__ out_mean, T* __restrict__ back) {
+  griddep_launch_dependents();
+  griddep_wait();
+  // Row ids, offsets and counts fit in 32 bits (the launcher checks R < 2^31); the row width
+  // C = G * V is a compile-time constant, so no 64-bit index arithmetic is issued per row.
   constexpr int V = Row16<T>::V;
+  constexpr int C = G * V;
   constexpr int kWin = 4;
+  constexpr int kNone = 0x7fffffff;
   const int lane = threadIdx.x & 31, gl = lane & (G - 1);
   const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G;
+  const int s = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G);
   if (s >= S) return;  // the whole group leaves together
-  const int64_t b = off[s], n = off[s + 1] - b;
-  const int64_t c = (int64_t)gl * V;
+  const int b = (int)off[s], n = (int)off[s + 1] - b;
+  const int c = gl * V;
   const float lo = lowest_of<T>();
   float mx[V], sm[V];
-  int64_t am[ARG ? V : 1];
+  int am[ARG ? V : 1];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     mx[i] = lo;
@@ -368,37 +382,37 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
     if (ARG) am[i] = R;
   }
   const bool small = n <= G;
-  int64_t mine = INT64_MAX;  // small: the gl-th smallest row id of the segment
+  int mine = kNone;  // small: the gl-th smallest row id of the segment
   if (small) {
-    const int64_t id = gl < n ? tmp[b + gl] : INT64_MAX;
+    const int id = gl < n ? (int)tmp[b + gl] : kNone;
     int rank = 0;
 #pragma unroll
     for (int j = 0; j < G; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       const int rj = __shfl_sync(gmask, rank, j, G);
-      const int64_t yj = __shfl_sync(gmask, id, j, G);
+      const int yj = __shfl_sync(gmask, id, j, G);
       if (rj == gl) mine = yj;
     }
   } else {
-    for (int64_t i = gl; i < n; i += G) {
-      const int64_t x = tmp[b + i];
-      int64_t rank = 0;
-      for (int64_t j = 0; j < n; ++j) rank += tmp[b + j] < x;
+    for (int i = gl; i < n; i += G) {
+      const int x = (int)tmp[b + i];
+      int rank = 0;
+      for (int j = 0; j < n; ++j) rank += (int)tmp[b + j] < x;
       sorted[b + rank] = x;
     }
     __syncwarp(gmask);
   }
-  for (int64_t p0 = 0; p0 < n; p0 += G) {
-    if (!small) mine = p0 + gl < n ? sorted[b + p0 + gl] : INT64_MAX;
-    const int m = (int)(n - p0 < G ? n - p0 : G);
+  for (int p0 = 0; p0 < n; p0 += G) {
+    if (!small) mine = p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
+    const int m = n - p0 < G ? n - p0 : G;
     for (int w0 = 0; w0 < m; w0 += kWin) {
-      int64_t rid[kWin];
+      int rid[kWin];
       uint4 raw[kWin];
 #pragma unroll
       for (int u = 0; u < kWin; ++u) {
         rid[u] = __shfl_sync(gmask, mine, (w0 + u) & (G - 1), G);
-        if (w0 + u < m) raw[u] = __ldg(reinterpret_cast<const uint4*>(src + rid[u] * C + c));
+        if (w0 + u < m) raw[u] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)rid[u] * C + c));
       }
 #pragma unroll
       for (int u = 0; u < kWin; ++u) {
@@ -420,24 +434,25 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
 #pragma unroll
   for (int i = 0; i < V; ++i)
     if (mx[i] == lo) mx[i] = 0.f;
-  if (out_max) Vec<T, V>::store(out_max + s * C + c, mx);
+  const size_t o = (size_t)s * C + c;
+  if (out_max) Vec<T, V>::store(out_max + o, mx);
   if (ARG) {
 #pragma unroll
-    for (int i = 0; i < V; ++i) arg[s * C + c + i] = am[i];
+    for (int i = 0; i < V; ++i) arg[o + i] = am[i];
   }
   if (out_mean) {
     const float cnt = (float)(n > 0 ? n : 1);
 #pragma unroll
     for (int i = 0; i < V; ++i) sm[i] = __fdiv_rn(sm[i], cnt);
-    Vec<T, V>::store(out_mean + s * C + c, sm);
+    Vec<T, V>::store(out_mean + o, sm);
   }
   if (back) {
-    for (int64_t p0 = 0; p0 < n; p0 += G) {
-      if (!small) mine = p0 + gl < n ? sorted[b + p0 + gl] : INT64_MAX;
-      const int m = (int)(n - p0 < G ? n - p0 : G);
+    for (int p0 = 0; p0 < n; p0 += G) {
+      if (!small) mine = p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
+      const int m = n - p0 < G ? n - p0 : G;
       for (int u = 0; u < m; ++u) {
-        const int64_t r = __shfl_sync(gmask, mine, u, G);
-        Vec<T, V>::store(back + r * C + c, mx);
+        const int r = __shfl_sync(gmask, mine, u, G);
+        Vec<T, V>::store(back + (size_t)r * C + c, mx);
       }
     }
   }
@@ -503,18 +518,18 @@ int build_csr(const int64_t* index, int64_t R, int64_t S, int64_t* off, int64_t*
       return SSLA_ERR_CUDA;
     }
     if (R > 0) count_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, counts);
-    scan_blocks_kernel<<<(unsigned)nb, 1024, 0, s>>>(counts, S, off, block_sums);
+    launch_pdl(scan_blocks_kernel, dim3((unsigned)nb), dim3(1024), 0, s, (const int*)counts, S, off, block_sums);
   }
   if (S > 0 && nb <= 1024) {
-    add_block_prefix_kernel<<<(unsigned)nb, 1024, 0, s>>>(off, S, block_sums, nb, counts);
+    launch_pdl(add_block_prefix_kernel, dim3((unsigned)nb), dim3(1024), 0, s, off, S, (const int64_t*)block_sums, nb, counts);
   } else {
     scan_totals_kernel<<<1, 32, 0, s>>>(block_sums, nb, S, off);
     if (S > 0) add_block_base_kernel<<<ceil_div(S, 256), 256, 0, s>>>(off, S, block_sums, counts);
   }
   if (S > 0) {
     if (R > 0) {
-      fill_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, off, counts, tmp);
-      rank_sort_kernel<<<ceil_div(S * 32, 256), 256, 0, s>>>(off, S, tmp, rows);
+      launch_pdl(fill_kernel, dim3(ceil_div(R, 256)), dim3(256), 0, s, index, R, S, (const int64_t*)off, counts, tmp);
+      launch_pdl(rank_sort_kernel, dim3(ceil_div(S * 32, 256)), dim3(256), 0, s, (const int64_t*)off, S, (const int64_t*)tmp, rows);
     }
   }
   SSLA_CHECK_LAUNCH("ssla_segment_csr");
@@ -623,11 +638,11 @@ void launch_pool(unsigned grid, cudaStream_t s, const void* src, const int64_t* 
                  int64_t* sorted, int64_t R, int64_t S, int64_t C, void* out_max, int64_t* arg, void* out_mean,
                  void* back) {
   if (arg)
-    pool_fused_kernel<T, G, true><<<grid, 256, 0, s>>>((const T*)src, off, tmp, sorted, R, S, C, (T*)out_max,
-                                                       arg, (T*)out_mean, (T*)back);
+    launch_pdl(pool_fused_kernel<T, G, true>, dim3(grid), dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
+               (int)S, (T*)out_max, arg, (T*)out_mean, (T*)back);
   else
-    pool_fused_kernel<T, G, false><<<grid, 256, 0, s>>>((const T*)src, off, tmp, sorted, R, S, C, (T*)out_max,
-                                                        nullptr, (T*)out_mean, (T*)back);
+    launch_pdl(pool_fused_kernel<T, G, false>, dim3(grid), dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
+               (int)S, (T*)out_max, (int64_t*)nullptr, (T*)out_mean, (T*)back);
 }
 
 template <typename T>
@@ -638,7 +653,7 @@ int run_pool(const void* src, int dtype, const int64_t* index, int64_t R, int64_
   const int64_t G = C / V;
   const bool fused = C % V == 0 && (G == 1 || G == 2 || G == 4 || G == 8 || G == 16 || G == 32) &&
                      aligned_to(src, 16) && aligned_to(out_max, 16) && aligned_to(out_mean, 16) &&
-                     aligned_to(back, 16);
+                     aligned_to(back, 16) && R < (int64_t)INT32_MAX && S < (int64_t)INT32_MAX;
   if (!fused) {
     // general widths: sorted CSR, one reduction per output, then the row gather
     int rc = build_csr(index, R, S, off, sorted, p, s);
@@ -659,14 +674,14 @@ int run_pool(const void* src, int dtype, const int64_t* index, int64_t R, int64_
     return SSLA_ERR_CUDA;
   }
   if (R > 0) count_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, counts);
-  scan_blocks_kernel<<<(unsigned)nb, 1024, 0, s>>>(counts, S, off, block_sums);
+  launch_pdl(scan_blocks_kernel, dim3((unsigned)nb), dim3(1024), 0, s, (const int*)counts, S, off, block_sums);
   if (nb <= 1024) {
-    add_block_prefix_kernel<<<(unsigned)nb, 1024, 0, s>>>(off, S, block_sums, nb, counts);
+    launch_pdl(add_block_prefix_kernel, dim3((unsigned)nb), dim3(1024), 0, s, off, S, (const int64_t*)block_sums, nb, counts);
   } else {
     scan_totals_kernel<<<1, 32, 0, s>>>(block_sums, nb, S, off);
     add_block_base_kernel<<<ceil_div(S, 256), 256, 0, s>>>(off, S, block_sums, counts);
   }
-  if (R > 0) fill_kernel<<<ceil_div(R, 256), 256, 0, s>>>(index, R, S, off, counts, tmp);
+  if (R > 0) launch_pdl(fill_kernel, dim3(ceil_div(R, 256)), dim3(256), 0, s, index, R, S, (const int64_t*)off, counts, tmp);
   const unsigned grid = (unsigned)ceil_div(S * G, 256);
   switch (G) {
     case 1: launch_pool<T, 1>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
