@@ -300,17 +300,31 @@ def triton_reference_line(dev, steps, warmup, full_autotune=False):
     return out
 
 
+def _init_nccl(dev, rank, world):
+    """NCCL process group for this rank.  NCCL's own INIT log goes to stderr (stdout carries only
+    the result line), and every rank reports the communicator size it joined, checked with one
+    all-reduce of ones."""
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    dist.init_process_group("nccl", device_id=dev)
+    one = torch.ones(1, device=dev)
+    dist.all_reduce(one)
+    print(f"[bench] rank {rank}/{world}: NCCL {'.'.join(map(str, torch.cuda.nccl.version()))} communicator "
+          f"on {dev} ({torch.cuda.get_device_name(dev)}), all-reduce of ones = {int(one.item())} "
+          f"(nranks ok: {int(one.item()) == world})", file=sys.stderr, flush=True)
+    return dist
+
+
 def _dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", device_id=dev)
+    dist = _init_nccl(dev, rank, world) if world > 1 else None
     return world, rank, local, dev, dist
 
 
@@ -695,11 +709,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", device_id=dev)
+    dist = _init_nccl(dev, rank, world) if world > 1 else None
 
     from ssla_b200 import _lib
     from ssla_b200.ops.gla.chunk import chunk_gla
