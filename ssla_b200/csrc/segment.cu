@@ -78,22 +78,52 @@ __global__ void __launch_bounds__(1024) scan_blocks_kernel(const int* __restrict
   if (tid == 1023) block_sums[blockIdx.x] = before + incl;
 }
 
-// Sequential exclusive scan of the (few) block totals, then off[S] = number of rows.
-__global__ void scan_totals_kernel(int64_t* __restrict__ block_sums, int64_t nb, int64_t S,
-                                   int64_t* __restrict__ off) {
-  if (threadIdx.x != 0) return;
-  int64_t acc = 0;
-  for (int64_t b = 0; b < nb; ++b) {
-    const int64_t x = block_sums[b];
-    block_sums[b] = acc;
-    acc += x;
+// Exclusive scan of the block totals in place, by one CTA of 1024 threads walking them 1024 at a
+// time with a running carry, then off[S] = number of rows (for nb > 1024; fewer blocks use
+// add_block_prefix_kernel).
+__global__ void __launch_bounds__(1024) scan_totals_kernel(int64_t* __restrict__ block_sums, int64_t nb,
+                                                           int64_t S, int64_t* __restrict__ off) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int64_t ws[32];
+  __shared__ int64_t carry_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int64_t carry = 0;
+  for (int64_t base = 0; base < nb; base += 1024) {
+    const int64_t i = base + tid;
+    const int64_t x = i < nb ? block_sums[i] : 0;
+    int64_t incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) ws[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int64_t w = ws[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      ws[lane] = w;
+    }
+    __syncthreads();
+    const int64_t before = carry + (warp > 0 ? ws[warp - 1] : 0);
+    if (i < nb) block_sums[i] = before + incl - x;
+    if (tid == 1023) carry_s = before + incl;
+    __syncthreads();
+    carry = carry_s;
   }
-  off[S] = acc;
+  if (tid == 0) off[S] = carry;
 }
 
 __global__ void add_block_base_kernel(int64_t* __restrict__ off, int64_t S,
                                       const int64_t* __restrict__ block_sums,
                                       int* __restrict__ counts) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= S) return;
   off[i] += block_sums[i / 1024];
@@ -344,17 +374,22 @@ template <> struct Row16<float> {
 
 // Scatter max + mean of every segment and the gather of the max back to its rows, in one
 // pass over the rows (the sparse pooling of layers/sparse_pooling.py:33 followed by the
-// inverse lookup pooled[index]).  A group of G lanes owns one segment; each lane holds 16 bytes
-// (V channels) of a row, so G * V == C.  The segment's row ids arrive unsorted from the
-// counting-sort fill; a segment of at most G rows is put in ascending order by a shuffle rank
-// sort in registers, a longer one by a rank count over its list (written to `sorted`).  Rows
-// are then loaded kWin at a time (all loads issued before any is combined) and reduced in
-// ascending row order: max keeps the first maximal row (strict >), the sum is fp32 with
-// round-to-nearest adds, mean = sum / max(count, 1), empty segments give 0 (arg R).  (A
-// persistent variant walking segments with a grid stride and prefetching the next segment's
-// offsets and row ids measured slower: 51 vs 42 us on the config-4 k=2 pooling.)
-template <typename T, int G, bool ARG>
-__global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
+// inverse lookup pooled[index]); with MODE kPoolSum, the plain ascending-order sum
+// (the index_add_ gather-back of utils/async_utils.py:243-264).  A group of GP lanes (GP the
+// power of two >= G) owns one segment; lane gl < G holds 16 bytes (V channels) of a row, so
+// G * V == C.  The segment's row ids arrive unsorted from the counting-sort fill; up to
+// kSlots * GP of them are ranked in registers (each lane keeps kSlots ids, every id is
+// compared with every other through shuffles) and handed to the lanes in ascending order,
+// longer segments by a rank count over the list written to `sorted`.  Rows are loaded kWin at
+// a time (all loads issued before any is combined) and reduced in ascending row order: max
+// keeps the first maximal row (strict >), the sum is fp32 with round-to-nearest adds, mean =
+// sum / max(count, 1), empty segments give 0 (arg R).  (A persistent variant walking segments
+// with a grid stride and prefetching the next segment's offsets and row ids measured slower:
+// 51 vs 42 us on the config-4 k=2 pooling.)
+constexpr int kPoolMaxMean = 0, kPoolArg = 1, kPoolSum = 2;
+
+template <typename T, int G, int MODE>
+__global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kernel(
     const T* __restrict__ src, const int64_t* __restrict__ off, const int64_t* __restrict__ tmp,
     int64_t* __restrict__ sorted, int R, int S, T* __restrict__ out_max, int64_t* __restrict__ arg,
     T* __restrict__ out_mean, T* __restrict__ back) {
@@ -364,14 +399,18 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
   // C = G * V is a compile-time constant, so no 64-bit index arithmetic is issued per row.
   constexpr int V = Row16<T>::V;
   constexpr int C = G * V;
+  constexpr int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : G <= 8 ? 8 : G <= 16 ? 16 : 32;
+  constexpr int kSlots = GP >= 8 ? 2 : 4;
   constexpr int kWin = 4;
   constexpr int kNone = 0x7fffffff;
-  const int lane = threadIdx.x & 31, gl = lane & (G - 1);
-  const unsigned gmask = G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane & ~(G - 1)));
-  const int s = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G);
+  constexpr bool ARG = MODE == kPoolArg, SUM = MODE == kPoolSum;
+  const int lane = threadIdx.x & 31, gl = lane & (GP - 1);
+  const unsigned gmask = GP == 32 ? 0xffffffffu : (((1u << GP) - 1u) << (lane & ~(GP - 1)));
+  const int s = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / GP);
   if (s >= S) return;  // the whole group leaves together
   const int b = (int)off[s], n = (int)off[s + 1] - b;
-  const int c = gl * V;
+  const bool data = gl < G;  // lanes G..GP-1 only take part in the shuffles
+  const int c = (data ? gl : 0) * V;
   const float lo = lowest_of<T>();
   float mx[V], sm[V];
   int am[ARG ? V : 1];
@@ -381,21 +420,43 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
     sm[i] = 0.f;
     if (ARG) am[i] = R;
   }
-  const bool small = n <= G;
-  int mine = kNone;  // small: the gl-th smallest row id of the segment
+  const bool small = n <= kSlots * GP;
+  int mine[kSlots];  // small: slot k of lane gl holds the (k * GP + gl)-th smallest row id
+#pragma unroll
+  for (int k = 0; k < kSlots; ++k) mine[k] = kNone;
   if (small) {
-    const int id = gl < n ? (int)tmp[b + gl] : kNone;
-    int rank = 0;
+    int id[kSlots], rank[kSlots];
 #pragma unroll
-    for (int j = 0; j < G; ++j) rank += __shfl_sync(gmask, id, j, G) < id;
+    for (int k = 0; k < kSlots; ++k) {
+      id[k] = k * GP + gl < n ? (int)tmp[b + k * GP + gl] : kNone;
+      rank[k] = 0;
+    }
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int rj = __shfl_sync(gmask, rank, j, G);
-      const int yj = __shfl_sync(gmask, id, j, G);
-      if (rj == gl) mine = yj;
+    for (int kk = 0; kk < kSlots; ++kk) {
+      if (kk * GP < n) {  // uniform over the group
+#pragma unroll
+        for (int j = 0; j < GP; ++j) {
+          const int y = __shfl_sync(gmask, id[kk], j, GP);
+#pragma unroll
+          for (int k = 0; k < kSlots; ++k) rank[k] += y < id[k];
+        }
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < kSlots; ++kk) {
+      if (kk * GP < n) {
+#pragma unroll
+        for (int j = 0; j < GP; ++j) {
+          const int rj = __shfl_sync(gmask, rank[kk], j, GP);
+          const int yj = __shfl_sync(gmask, id[kk], j, GP);
+#pragma unroll
+          for (int k = 0; k < kSlots; ++k)
+            if (rj == k * GP + gl) mine[k] = yj;
+        }
+      }
     }
   } else {
-    for (int i = gl; i < n; i += G) {
+    for (int i = gl; i < n; i += GP) {
       const int x = (int)tmp[b + i];
       int rank = 0;
       for (int j = 0; j < n; ++j) rank += (int)tmp[b + j] < x;
@@ -403,25 +464,34 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
     }
     __syncwarp(gmask);
   }
-  for (int p0 = 0; p0 < n; p0 += G) {
-    if (!small) mine = p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
-    const int m = n - p0 < G ? n - p0 : G;
+  // the rows of slot window p0 (GP rows, ascending) as one lane value each
+  auto window_ids = [&](int p0, int k) -> int {
+    if (small) return mine[k];
+    return p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
+  };
+#pragma unroll 1
+  for (int k = 0, p0 = 0; p0 < n; ++k, p0 += GP) {
+    int w = kNone;
+#pragma unroll
+    for (int kk = 0; kk < kSlots; ++kk)
+      if (kk == (small ? k : 0)) w = window_ids(p0, kk);
+    const int m = n - p0 < GP ? n - p0 : GP;
     for (int w0 = 0; w0 < m; w0 += kWin) {
       int rid[kWin];
       uint4 raw[kWin];
 #pragma unroll
       for (int u = 0; u < kWin; ++u) {
-        rid[u] = __shfl_sync(gmask, mine, (w0 + u) & (G - 1), G);
-        if (w0 + u < m) raw[u] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)rid[u] * C + c));
+        rid[u] = __shfl_sync(gmask, w, (w0 + u) & (GP - 1), GP);
+        if (data && w0 + u < m) raw[u] = __ldg(reinterpret_cast<const uint4*>(src + (size_t)rid[u] * C + c));
       }
 #pragma unroll
       for (int u = 0; u < kWin; ++u) {
-        if (w0 + u < m) {
+        if (data && w0 + u < m) {
           float x[V];
           Row16<T>::unpack(raw[u], x);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
-            if (x[i] > mx[i]) {
+            if (!SUM && x[i] > mx[i]) {
               mx[i] = x[i];
               if (ARG) am[i] = rid[u];
             }
@@ -431,10 +501,15 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
       }
     }
   }
+  if (!data) return;
+  const size_t o = (size_t)s * C + c;
+  if (SUM) {
+    Vec<T, V>::store(out_mean + o, sm);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < V; ++i)
     if (mx[i] == lo) mx[i] = 0.f;
-  const size_t o = (size_t)s * C + c;
   if (out_max) Vec<T, V>::store(out_max + o, mx);
   if (ARG) {
 #pragma unroll
@@ -447,13 +522,10 @@ __global__ void __launch_bounds__(256, ARG ? 2 : 4) pool_fused_kernel(
     Vec<T, V>::store(out_mean + o, sm);
   }
   if (back) {
-    for (int p0 = 0; p0 < n; p0 += G) {
-      if (!small) mine = p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
-      const int m = n - p0 < G ? n - p0 : G;
-      for (int u = 0; u < m; ++u) {
-        const int r = __shfl_sync(gmask, mine, u, G);
-        Vec<T, V>::store(back + (size_t)r * C + c, mx);
-      }
+    // row ids straight from the list (in any order: each row's store is independent)
+    for (int u = 0; u < n; ++u) {
+      const int r = (int)tmp[b + u];
+      Vec<T, V>::store(back + (size_t)r * C + c, mx);
     }
   }
 }
@@ -523,8 +595,10 @@ int build_csr(const int64_t* index, int64_t R, int64_t S, int64_t* off, int64_t*
   if (S > 0 && nb <= 1024) {
     launch_pdl(add_block_prefix_kernel, dim3((unsigned)nb), dim3(1024), 0, s, off, S, (const int64_t*)block_sums, nb, counts);
   } else {
-    scan_totals_kernel<<<1, 32, 0, s>>>(block_sums, nb, S, off);
-    if (S > 0) add_block_base_kernel<<<ceil_div(S, 256), 256, 0, s>>>(off, S, block_sums, counts);
+    launch_pdl(scan_totals_kernel, dim3(1), dim3(1024), 0, s, block_sums, nb, S, off);
+    if (S > 0)
+      launch_pdl(add_block_base_kernel, dim3(ceil_div(S, 256)), dim3(256), 0, s, off, S, (const int64_t*)block_sums,
+                 counts);
   }
   if (S > 0) {
     if (R > 0) {
@@ -608,55 +682,43 @@ extern "C" size_t ssla_index_add_rows_workspace_bytes(int64_t P, int64_t D) {
   return a256(8 * (size_t)(D + 1)) + a256(8 * (size_t)P) + csr_ws_bytes(P, D);
 }
 
-extern "C" int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_t P,
-                                   int64_t D, int64_t C, void* out, void* workspace,
-                                   size_t workspace_bytes, ssla_stream_t stream) {
-  SSLA_CHECK_ARG(dtype_ok(dtype), "ssla_index_add_rows: bad dtype");
-  SSLA_CHECK_ARG(P >= 0 && D >= 0 && C >= 0, "ssla_index_add_rows: negative size");
-  if (D == 0 || C == 0) return SSLA_OK;
-  SSLA_CHECK_ARG(out && workspace && (P == 0 || (src && index)), "ssla_index_add_rows: null pointer");
-  const size_t need = ssla_index_add_rows_workspace_bytes(P, D);
-  if (workspace_bytes < need) {
-    set_error("ssla_index_add_rows: workspace of %zu bytes < %zu needed", workspace_bytes, need);
-    return SSLA_ERR_WORKSPACE;
-  }
-  cudaStream_t s = (cudaStream_t)stream;
-  char* p = (char*)workspace;
-  int64_t* off = (int64_t*)p;
-  p += a256(8 * (size_t)(D + 1));
-  int64_t* rows = (int64_t*)p;
-  p += a256(8 * (size_t)P);
-  int rc = build_csr(index, P, D, off, rows, p, s);
-  if (rc) return rc;
-  return SSLA_DISPATCH_DTYPE(dtype, T, [&] { return run_reduce<T>(src, off, rows, P, D, C, 0, out, nullptr, s); });
-}
-
 namespace ssla {
 namespace {
 template <typename T, int G>
-void launch_pool(unsigned grid, cudaStream_t s, const void* src, const int64_t* off, const int64_t* tmp,
-                 int64_t* sorted, int64_t R, int64_t S, int64_t C, void* out_max, int64_t* arg, void* out_mean,
-                 void* back) {
-  if (arg)
-    launch_pdl(pool_fused_kernel<T, G, true>, dim3(grid), dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
+void launch_pool(int mode, cudaStream_t s, const void* src, const int64_t* off, const int64_t* tmp,
+                 int64_t* sorted, int64_t R, int64_t S, void* out_max, int64_t* arg, void* out_mean, void* back) {
+  constexpr int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : G <= 8 ? 8 : G <= 16 ? 16 : 32;
+  const dim3 grid((unsigned)ceil_div(S * GP, 256));
+  if (mode == kPoolArg)
+    launch_pdl(pool_fused_kernel<T, G, kPoolArg>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
                (int)S, (T*)out_max, arg, (T*)out_mean, (T*)back);
+  else if (mode == kPoolSum)
+    launch_pdl(pool_fused_kernel<T, G, kPoolSum>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
+               (int)S, (T*)nullptr, (int64_t*)nullptr, (T*)out_mean, (T*)nullptr);
   else
-    launch_pdl(pool_fused_kernel<T, G, false>, dim3(grid), dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
-               (int)S, (T*)out_max, (int64_t*)nullptr, (T*)out_mean, (T*)back);
+    launch_pdl(pool_fused_kernel<T, G, kPoolMaxMean>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted,
+               (int)R, (int)S, (T*)out_max, (int64_t*)nullptr, (T*)out_mean, (T*)back);
 }
 
+// Counting sort of the row ids by segment (offsets + ids in arrival order), then the one-pass
+// kernel.  Row widths whose 16-byte lane count G is not in {1, 2, 3, 4, 6, 8, 12, 16, 24, 32}
+// take the sorted-CSR sequence (reductions + row gather) instead.  mode kPoolSum writes the
+// segment sums to out_mean.
 template <typename T>
-int run_pool(const void* src, int dtype, const int64_t* index, int64_t R, int64_t S, int64_t C, void* out_max,
-             int64_t* arg, void* out_mean, void* back, int64_t* off, int64_t* sorted, char* p, int* counts,
-             int64_t nb, int64_t* block_sums, int64_t* tmp, cudaStream_t s) {
+int run_pool(int mode, const void* src, int dtype, const int64_t* index, int64_t R, int64_t S, int64_t C,
+             void* out_max, int64_t* arg, void* out_mean, void* back, int64_t* off, int64_t* sorted, char* p,
+             int* counts, int64_t nb, int64_t* block_sums, int64_t* tmp, cudaStream_t s) {
   constexpr int V = 16 / (int)sizeof(T);
   const int64_t G = C / V;
-  const bool fused = C % V == 0 && (G == 1 || G == 2 || G == 4 || G == 8 || G == 16 || G == 32) &&
-                     aligned_to(src, 16) && aligned_to(out_max, 16) && aligned_to(out_mean, 16) &&
-                     aligned_to(back, 16) && R < (int64_t)INT32_MAX && S < (int64_t)INT32_MAX;
+  const bool g_ok = G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8 || G == 12 || G == 16 || G == 24 ||
+                    G == 32;
+  const bool fused = C % V == 0 && g_ok && aligned_to(src, 16) && aligned_to(out_max, 16) &&
+                     aligned_to(out_mean, 16) && aligned_to(back, 16) && R < (int64_t)INT32_MAX &&
+                     S < (int64_t)INT32_MAX;
   if (!fused) {
     // general widths: sorted CSR, one reduction per output, then the row gather
     int rc = build_csr(index, R, S, off, sorted, p, s);
+    if (!rc && mode == kPoolSum) return run_reduce<T>(src, off, sorted, R, S, C, SSLA_REDUCE_SUM, out_mean, nullptr, s);
     if (!rc && (out_max || arg)) {
       T* mx = (T*)out_max;
       if (!mx) {
@@ -678,19 +740,27 @@ int run_pool(const void* src, int dtype, const int64_t* index, int64_t R, int64_
   if (nb <= 1024) {
     launch_pdl(add_block_prefix_kernel, dim3((unsigned)nb), dim3(1024), 0, s, off, S, (const int64_t*)block_sums, nb, counts);
   } else {
-    scan_totals_kernel<<<1, 32, 0, s>>>(block_sums, nb, S, off);
-    add_block_base_kernel<<<ceil_div(S, 256), 256, 0, s>>>(off, S, block_sums, counts);
+    launch_pdl(scan_totals_kernel, dim3(1), dim3(1024), 0, s, block_sums, nb, S, off);
+    launch_pdl(add_block_base_kernel, dim3(ceil_div(S, 256)), dim3(256), 0, s, off, S, (const int64_t*)block_sums,
+               counts);
   }
   if (R > 0) launch_pdl(fill_kernel, dim3(ceil_div(R, 256)), dim3(256), 0, s, index, R, S, (const int64_t*)off, counts, tmp);
-  const unsigned grid = (unsigned)ceil_div(S * G, 256);
+  if (mode != kPoolSum) mode = arg ? kPoolArg : kPoolMaxMean;
+#define SSLA_POOL_G(GG) \
+  case GG: launch_pool<T, GG>(mode, s, src, off, tmp, sorted, R, S, out_max, arg, out_mean, back); break
   switch (G) {
-    case 1: launch_pool<T, 1>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
-    case 2: launch_pool<T, 2>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
-    case 4: launch_pool<T, 4>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
-    case 8: launch_pool<T, 8>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
-    case 16: launch_pool<T, 16>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
-    default: launch_pool<T, 32>(grid, s, src, off, tmp, sorted, R, S, C, out_max, arg, out_mean, back); break;
+    SSLA_POOL_G(1);
+    SSLA_POOL_G(2);
+    SSLA_POOL_G(3);
+    SSLA_POOL_G(4);
+    SSLA_POOL_G(6);
+    SSLA_POOL_G(8);
+    SSLA_POOL_G(12);
+    SSLA_POOL_G(16);
+    SSLA_POOL_G(24);
+    default: launch_pool<T, 32>(mode, s, src, off, tmp, sorted, R, S, out_max, arg, out_mean, back); break;
   }
+#undef SSLA_POOL_G
   SSLA_CHECK_LAUNCH("ssla_scatter_pool");
   return SSLA_OK;
 }
@@ -729,7 +799,37 @@ extern "C" int ssla_scatter_pool(const void* src, int dtype, const int64_t* inde
   int64_t* tmp = (int64_t*)((char*)block_sums + a256(8 * (size_t)(nb + 1)));
   if (C == 0) return build_csr(index, R, S, off, sorted, p, s);
   return SSLA_DISPATCH_DTYPE(dtype, T, [&] {
-    return run_pool<T>(src, dtype, index, R, S, C, out_max, arg, out_mean, back, off, sorted, p, counts, nb,
-                       block_sums, tmp, s);
+    return run_pool<T>(kPoolMaxMean, src, dtype, index, R, S, C, out_max, arg, out_mean, back, off, sorted, p, counts,
+                       nb, block_sums, tmp, s);
+  });
+}
+
+// Deterministic index_add: the one-pass kernel in sum mode over the counting-sorted row lists
+// (same workspace layout as ssla_scatter_pool).
+extern "C" int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_t P,
+                                   int64_t D, int64_t C, void* out, void* workspace,
+                                   size_t workspace_bytes, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(dtype_ok(dtype), "ssla_index_add_rows: bad dtype");
+  SSLA_CHECK_ARG(P >= 0 && D >= 0 && C >= 0, "ssla_index_add_rows: negative size");
+  if (D == 0 || C == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(out && workspace && (P == 0 || (src && index)), "ssla_index_add_rows: null pointer");
+  const size_t need = ssla_index_add_rows_workspace_bytes(P, D);
+  if (workspace_bytes < need) {
+    set_error("ssla_index_add_rows: workspace of %zu bytes < %zu needed", workspace_bytes, need);
+    return SSLA_ERR_WORKSPACE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  char* p = (char*)workspace;
+  int64_t* off = (int64_t*)p;
+  p += a256(8 * (size_t)(D + 1));
+  int64_t* sorted = (int64_t*)p;
+  p += a256(8 * (size_t)P);
+  int* counts = (int*)p;
+  const int64_t nb = (D + 1023) / 1024;
+  int64_t* block_sums = (int64_t*)(p + a256(4 * (size_t)D));
+  int64_t* tmp = (int64_t*)((char*)block_sums + a256(8 * (size_t)(nb + 1)));
+  return SSLA_DISPATCH_DTYPE(dtype, T, [&] {
+    return run_pool<T>(kPoolSum, src, dtype, index, P, D, C, nullptr, nullptr, out, nullptr, off, sorted, p, counts,
+                       nb, block_sums, tmp, s);
   });
 }

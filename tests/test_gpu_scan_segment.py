@@ -193,13 +193,15 @@ def test_c4_pooling_full_size_bit_exact(k):
 
 
 @pytest.mark.parametrize("dtype,C", [(torch.bfloat16, 64), (torch.float32, 64), (torch.float16, 256),
-                                     (torch.bfloat16, 8), (torch.float32, 4), (torch.bfloat16, 24)])
+                                     (torch.bfloat16, 8), (torch.float32, 4), (torch.bfloat16, 24),
+                                     (torch.float32, 12), (torch.float32, 96), (torch.bfloat16, 96),
+                                     (torch.float32, 20)])
 def test_scatter_pool_one_pass_bit_exact(dtype, C):
     """``ssla_scatter_pool`` (max + argmax + mean + gather back in one pass) against the CPU
-    oracle for every lane-group width (C * element size from 16 to 512 bytes), the general-width
-    sequence (C=24 bf16), segments longer than the lane group (sorted through the rank-count
-    path), empty segments, ties, and rows with out-of-range ids (ignored; their back row is not
-    written)."""
+    oracle for lane-group widths of 1 to 32 lanes of 16 bytes, power-of-two and not (C=24 bf16:
+    3 lanes, C=12 fp32: 3, C=96 fp32: 24, C=96 bf16: 12), the general-width sequence (C=20
+    fp32), segments longer than the register slots (sorted through the rank-count path), empty
+    segments, ties, and rows with out-of-range ids (ignored; their back row is not written)."""
     from ssla_b200.ops import segment as seg
 
     gen = torch.Generator().manual_seed(C)
@@ -238,3 +240,35 @@ def test_scatter_pool_empty_inputs():
     assert (res["arg"] == 0).all() and res["offsets"].tolist() == [0, 0, 0, 0]
     res = seg.scatter_pool(torch.randn(4, 64).cuda(), torch.tensor([0, 0, 1, 1]).cuda(), 0)
     assert res["max"].shape == (0, 64)
+
+
+@pytest.mark.parametrize("C", [4, 12, 24, 48, 96, 20])
+def test_index_add_rows_widths(C):
+    """Deterministic index_add (one-pass kernel in sum mode) against CPU ``index_add_`` for the
+    MoS layer widths (fp32, C = 12 / 24 / 48 / 96 give 3 / 6 / 12 / 24 lanes of 16 bytes), a
+    general width (C=20) and segments of up to ~30 rows."""
+    from ssla_b200.ops import segment as seg
+
+    gen = torch.Generator().manual_seed(100 + C)
+    P, D = 60000, 7000
+    idx = torch.randint(0, D, (P,), generator=gen)
+    idx[:30] = 5
+    src = torch.randn(P, C, generator=gen)
+    ref = torch.zeros(D, C).index_add_(0, idx, src)
+    assert torch.equal(seg.index_add_rows(src.cuda(), idx.cuda(), D).cpu(), ref)
+
+
+def test_segment_csr_many_blocks():
+    """CSR offsets when the segment count needs more than 1024 scan blocks (the chunked
+    totals scan): offsets and the ascending row order per segment."""
+    from ssla_b200.ops import segment as seg
+
+    gen = torch.Generator().manual_seed(9)
+    S = 1024 * 1024 + 4097
+    R = 3 * S
+    idx = torch.randint(0, S, (R,), generator=gen)
+    off, rows = seg.segment_csr(idx.cuda(), S)
+    cnt = torch.bincount(idx, minlength=S)
+    ref_off = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(cnt, 0)])
+    assert torch.equal(off.cpu(), ref_off)
+    assert torch.equal(rows.cpu(), torch.sort(idx, stable=True)[1])
