@@ -199,6 +199,12 @@ int ssla_index_add_rows(const void* src, int dtype, const int64_t* index, int64_
 int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const int64_t* dst,
                             const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
                             ssla_stream_t stream);
+/* The same with the row indices formed from the routing's (src, pos) pair of each patch event:
+ * key = src * P + pos (src when P == 1), dst = src * Pg + pos, or dst = t (the patch event's
+ * own row) when Pg == 0; pos may be NULL when P == 1 and Pg <= 1 (pos = 0). */
+int ssla_mos_patch_scan_routed_fwd(const float* y, const int64_t* src, const int64_t* pos, int64_t P, int64_t Pg,
+                                   const int64_t* cu_seqlens, int64_t n_seqs, int64_t C, float* z,
+                                   ssla_stream_t stream);
 /* The same with the projection done in the kernel: [q | v | g] = w[pos[t]] @ x[src[t]], with
  * w [P, 3C, I] fp32 (the q/v/g projections folded into the per-position scatter weights) and
  * x [*, I] the layer input rows.  w must fit in shared memory

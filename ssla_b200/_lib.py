@@ -51,6 +51,7 @@ SIGNATURES = {
     "ssla_index_add_rows_workspace_bytes": (sz, [i64, i64]),
     "ssla_index_add_rows": (i32, [p, i32, p, i64, i64, i64, p, p, sz, p]),
     "ssla_mos_patch_scan_fwd": (i32, [p, p, p, p, i64, i64, p, p]),
+    "ssla_mos_patch_scan_routed_fwd": (i32, [p, p, p, i64, i64, p, i64, i64, p, p]),
     "ssla_route_pixel_map": (i32, [p, p, p, i64, i64, i64, i64, p, p, p]),
     "ssla_route_groups_time_sorted": (i32, [p, p, p, i64, p, p]),
     "ssla_route_field_lengths": (i32, [p, p] + [i64] * 11 + [p, p]),

@@ -33,9 +33,15 @@ namespace {
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
+// Patch event t of a sequence reads y row key(t) and writes z row dst(t).  INDEXED: both come
+// from the key / dst arrays; otherwise they are formed from the routing's (src, pos) pair as
+// key = src * P + pos (src when P == 1) and dst = src * Pg + pos (dst = t when Pg == 0), which
+// saves the elementwise passes that would build the two index arrays.
+template <bool INDEXED>
 __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __restrict__ y,
                                                              const int64_t* __restrict__ key,
                                                              const int64_t* __restrict__ dst,
+                                                             int64_t P, int64_t Pg,
                                                              const int64_t* __restrict__ cu, int64_t n_seqs,
                                                              int64_t C, float* __restrict__ z) {
   const int64_t CV = C / 4;
@@ -46,7 +52,16 @@ __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __rest
   const int64_t bos = cu[seq], eos = cu[seq + 1];
   float h[4] = {0.f, 0.f, 0.f, 0.f};
   for (int64_t t = bos; t < eos; ++t) {
-    const float* row = y + key[t] * 3 * C + c;
+    int64_t kt, dt;
+    if (INDEXED) {
+      kt = key[t];
+      dt = dst[t];
+    } else {  // key = src, dst = pos (possibly null)
+      const int64_t sv = key[t], pv = dst ? dst[t] : 0;
+      kt = P > 1 ? sv * P + pv : sv;
+      dt = Pg > 0 ? sv * Pg + pv : t;
+    }
+    const float* row = y + kt * 3 * C + c;
     const float4 q = *reinterpret_cast<const float4*>(row);
     const float4 v = *reinterpret_cast<const float4*>(row + C);
     const float4 gp = *reinterpret_cast<const float4*>(row + 2 * C);
@@ -57,7 +72,7 @@ __global__ void __launch_bounds__(256) mos_patch_scan_kernel(const float* __rest
       h[i] = __fadd_rn(__fmul_rn(h[i], sigmoid_f(ga[i])), va[i]);
       o[i] = __fmul_rn(qa[i], h[i]);
     }
-    *reinterpret_cast<float4*>(z + dst[t] * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(z + dt * C + c) = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -270,9 +285,25 @@ extern "C" int ssla_mos_patch_scan_fwd(const float* y, const int64_t* key, const
   SSLA_CHECK_ARG(y && key && dst && cu && z, "ssla_mos_patch_scan_fwd: null pointer");
   SSLA_CHECK_ARG(aligned_to(y, 16) && aligned_to(z, 16), "ssla_mos_patch_scan_fwd: y and z must be 16-byte aligned");
   const int64_t threads = n_seqs * (C / 4);
-  mos_patch_scan_kernel<<<(unsigned)ceil_div(threads, 256), 256, 0, (cudaStream_t)stream>>>(y, key, dst, cu, n_seqs, C,
-                                                                                           z);
+  mos_patch_scan_kernel<true><<<(unsigned)ceil_div(threads, 256), 256, 0, (cudaStream_t)stream>>>(
+      y, key, dst, 0, 0, cu, n_seqs, C, z);
   SSLA_CHECK_LAUNCH("ssla_mos_patch_scan_fwd");
+  return SSLA_OK;
+}
+
+extern "C" int ssla_mos_patch_scan_routed_fwd(const float* y, const int64_t* src, const int64_t* pos, int64_t P,
+                                              int64_t Pg, const int64_t* cu, int64_t n_seqs, int64_t C, float* z,
+                                              ssla_stream_t stream) {
+  SSLA_CHECK_ARG(n_seqs >= 0 && C > 0 && C % 4 == 0 && P >= 1 && Pg >= 0,
+                 "ssla_mos_patch_scan_routed_fwd: bad sizes (C=%lld must be a positive multiple of 4)", (long long)C);
+  if (n_seqs == 0) return SSLA_OK;
+  SSLA_CHECK_ARG(y && src && cu && z && (pos || (P == 1 && Pg <= 1)), "ssla_mos_patch_scan_routed_fwd: null pointer");
+  SSLA_CHECK_ARG(aligned_to(y, 16) && aligned_to(z, 16),
+                 "ssla_mos_patch_scan_routed_fwd: y and z must be 16-byte aligned");
+  const int64_t threads = n_seqs * (C / 4);
+  mos_patch_scan_kernel<false><<<(unsigned)ceil_div(threads, 256), 256, 0, (cudaStream_t)stream>>>(
+      y, src, pos, P, Pg, cu, n_seqs, C, z);
+  SSLA_CHECK_LAUNCH("ssla_mos_patch_scan_routed_fwd");
   return SSLA_OK;
 }
 

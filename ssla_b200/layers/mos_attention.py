@@ -143,17 +143,18 @@ class MosAttention(nn.Module):
         rows = src.numel()
         if Pg == 1:
             qh = torch.empty((rows, C), device=residual.device, dtype=torch.float32)
-            dst = torch.arange(rows, device=residual.device)
         else:
             qh = torch.zeros((E * Pg, C), device=residual.device, dtype=torch.float32)
-            dst = src * Pg + pos_id  # unique (event, position) pairs
         if _mos.use_patch_scan_proj(E, P, C, self.input_size):
             # projection inside the scan kernel (weights in shared memory): no [E, P*3C] buffer
+            dst = torch.arange(rows, device=residual.device) if Pg == 1 else src * Pg + pos_id
             _mos.patch_scan_proj(residual, w_all, src, pos_id if P > 1 else torch.zeros_like(src), dst, cu, qh)
         else:
             y = g_rows(residual)  # rows (e, p) of 3C
-            key = src if P == 1 else src * P + pos_id
-            _mos.patch_scan(y.view(-1, 3 * C), key, dst, cu, C, qh)
+            # key = src * P + pos and dst = src * Pg + pos (unique (event, position) pairs), or the
+            # patch event's own row when Pg == 1, are formed inside the kernel
+            _mos.patch_scan_routed(y.view(-1, 3 * C), src, pos_id if (P > 1 or Pg > 1) else None, P,
+                                   0 if Pg == 1 else Pg, cu, C, qh)
         if Pg == 1:
             out = g_back(index_add_rows_ad(qh, src, E))
         else:

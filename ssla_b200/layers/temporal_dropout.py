@@ -4,7 +4,10 @@ from __future__ import annotations
 
 import torch
 
+from ..ops.segment import gather_rows_ad
 from .async_sparse_module import AsyncSparseModule
+
+_ROW_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 
 class TemporalDropout(AsyncSparseModule):
@@ -29,6 +32,8 @@ class TemporalDropout(AsyncSparseModule):
             j = torch.arange(total, device=dev) - kstart[seq]
             first = torch.remainder(lengths - 1, w)  # offset of the first kept event
             idx = start[seq] + first[seq] + j * w
-        return {"events": inputs["events"][idx], "time": inputs["time"][idx], "lengths": keep_n,
+        ev = inputs["events"]
+        kept = gather_rows_ad(ev, idx) if (ev.dim() == 2 and ev.is_cuda and ev.dtype in _ROW_DTYPES) else ev[idx]
+        return {"events": kept, "time": inputs["time"][idx], "lengths": keep_n,
                 "batch_id": inputs["batch_id"], "h": inputs["h"], "w": inputs["w"],
                 "batch_size": inputs["batch_size"]}

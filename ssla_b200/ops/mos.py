@@ -36,6 +36,26 @@ def patch_scan(y: torch.Tensor, key: torch.Tensor, dst: torch.Tensor, cu_seqlens
     return z
 
 
+def patch_scan_routed(y: torch.Tensor, src: torch.Tensor, pos: Optional[torch.Tensor], P: int, Pg: int,
+                      cu_seqlens: torch.Tensor, C: int, z: torch.Tensor) -> torch.Tensor:
+    """``patch_scan`` with key = src * P + pos (src when P == 1) and dst = src * Pg + pos (the
+    patch event's own row when Pg == 0) formed inside the kernel; ``pos`` may be None when P == 1
+    and Pg <= 1."""
+    _lib.require_cuda(y, src, cu_seqlens, z, what="patch_scan_routed")
+    if y.dtype != torch.float32 or z.dtype != torch.float32:
+        raise TypeError("patch_scan_routed: fp32 tensors expected")
+    if y.shape[-1] != 3 * C or z.shape[-1] != C or not z.is_contiguous():
+        raise ValueError("patch_scan_routed: y must have 3C columns, z C contiguous columns")
+    y = y.contiguous()
+    src = src.to(torch.int64).contiguous()
+    pos = None if pos is None else pos.to(torch.int64).contiguous()
+    cu = cu_seqlens.to(torch.int64).contiguous()
+    _lib.check(_lib.load().ssla_mos_patch_scan_routed_fwd(y.data_ptr(), src.data_ptr(), _lib.ptr(pos), P, Pg,
+                                                          cu.data_ptr(), cu.numel() - 1, C, z.data_ptr(),
+                                                          _lib.stream_of(y)), "patch_scan_routed")
+    return z
+
+
 PROJ_SMEM_LIMIT = 112 * 1024  # weights of the in-kernel projection must fit this
 # The GEMM-fed patch scan is faster (measured on B200: 2.28e3 vs 2.17e3 SSLA-S frames/s) but
 # materialises [events, positions * 3C] fp32 rows; above this size the projection moves into

@@ -383,3 +383,36 @@ def test_preprocess_delay_matches_oracle():
     got = preprocess_inputs(ev.cuda(), ln.cuda(), (240, 304), 50)
     for key in ("events", "time", "batch_id", "h", "w", "lengths"):
         assert torch.equal(got[key].cpu(), ref[key]), key
+
+
+@pytest.mark.parametrize("P,Pg", [(9, 9), (9, 0), (1, 0), (1, 9)])
+def test_patch_scan_routed_matches_indexed(P, Pg):
+    """The patch scan with key / dst formed in the kernel from (src, pos) equals the scan over
+    explicitly built index arrays, bit for bit."""
+    from ssla_b200.ops import mos as _mos
+
+    gen = torch.Generator().manual_seed(P * 10 + Pg)
+    E, C, n = 5000, 12, 20000
+    src = torch.randint(0, E, (n,), generator=gen)
+    pos = torch.randint(0, P if P > 1 else 9, (n,), generator=gen)
+    cuts = torch.randperm(n - 1, generator=gen)[:3000].sort().values + 1
+    cu = torch.cat([torch.zeros(1, dtype=torch.int64), cuts, torch.tensor([n])])
+    y = torch.randn(E * P, 3 * C, generator=gen)
+    key = src * P + pos if P > 1 else src
+    dst = src * Pg + pos if Pg > 0 else torch.arange(n)
+    rows_out = E * Pg if Pg > 0 else n
+    z_ref = torch.zeros(rows_out, C).cuda()
+    z = torch.zeros(rows_out, C).cuda()
+    if Pg > 0:  # (event, position) pairs must be unique for a deterministic result
+        keep = torch.zeros(n, dtype=torch.bool)
+        seen = set()
+        for i, d in enumerate(dst.tolist()):
+            if d not in seen:
+                seen.add(d)
+                keep[i] = True
+        src, pos, key, dst = src[keep], pos[keep], key[keep], dst[keep]
+        n = src.numel()
+        cu = torch.unique(torch.clamp(cu, max=n))
+    _mos.patch_scan(y.cuda(), key.cuda(), dst.cuda(), cu.cuda(), C, z_ref)
+    _mos.patch_scan_routed(y.cuda(), src.cuda(), pos.cuda() if (P > 1 or Pg > 0) else None, P, Pg, cu.cuda(), C, z)
+    assert torch.equal(z.cpu(), z_ref.cpu())
