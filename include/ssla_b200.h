@@ -233,6 +233,10 @@ int ssla_layernorm_residual_fwd(const float* x, const float* r, const float* w, 
  *                          outside the frame are skipped and counted in *bad.
  *   ssla_route_groups_time_sorted: *bad = 1 if some group's times decrease.
  *   ssla_route_field_lengths: flen[b*oh*ow + f] = events in field f of sample b.
+ *   ssla_route_compact_fields: the non-empty fields of flen [nf] in ascending order:
+ *                    field_ids, lengths and event offsets field_off (each sized for nf, field_off
+ *                    for nf + 1; the first F entries written, field_off[F] = total), and
+ *                    stats[4] = {flags[0], flags[1], F, total events} (flags may be NULL: 0).
  *   ssla_route_fill: for the non-empty fields field_ids[F] (ascending) with output offsets
  *                    field_off[F+1]: src (event index), pos (window position) and time of every
  *                    routed event, ordered by (time, pos, event) within each field.
@@ -244,6 +248,10 @@ int ssla_route_groups_time_sorted(const int64_t* gstart, const int64_t* glen, co
 int ssla_route_field_lengths(const int* map, const int64_t* glen, int64_t B, int64_t H, int64_t W,
                              int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
                              int64_t oh, int64_t ow, int64_t* flen, ssla_stream_t stream);
+size_t ssla_route_compact_fields_workspace_bytes(int64_t nf);
+int ssla_route_compact_fields(const int64_t* flen, int64_t nf, const int* flags, int64_t* field_ids,
+                              int64_t* lengths, int64_t* field_off, int64_t* stats, void* workspace,
+                              size_t workspace_bytes, ssla_stream_t stream);
 int ssla_route_fill(const int* map, const int64_t* gstart, const int64_t* glen, const int64_t* gtime,
                     int64_t B, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
                     int64_t pt, int64_t pl, int64_t oh, int64_t ow, const int64_t* field_ids,

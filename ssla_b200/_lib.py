@@ -55,6 +55,8 @@ SIGNATURES = {
     "ssla_route_pixel_map": (i32, [p, p, p, i64, i64, i64, i64, p, p, p]),
     "ssla_route_groups_time_sorted": (i32, [p, p, p, i64, p, p]),
     "ssla_route_field_lengths": (i32, [p, p] + [i64] * 11 + [p, p]),
+    "ssla_route_compact_fields_workspace_bytes": (sz, [i64]),
+    "ssla_route_compact_fields": (i32, [p, i64, p, p, p, p, p, p, sz, p]),
     "ssla_route_fill": (i32, [p, p, p, p] + [i64] * 11 + [p, p, i64, p, p, p, p]),
     "ssla_mos_patch_scan_proj_smem_bytes": (sz, [i64, i64, i64]),
     "ssla_mos_patch_scan_proj_fwd": (i32, [p, i64, p, i64, p, p, p, p, i64, i64, p, p]),

@@ -153,6 +153,110 @@ __global__ void __launch_bounds__(kFillThreads) fill_kernel(
   }
 }
 
+// Compaction of the non-empty fields (flen > 0) in ascending field order, three passes:
+// per-block (1024 fields) exclusive prefixes of the non-empty count and of the event count,
+// one CTA scanning the block totals in place (1024 at a time with a carry), and a scatter of
+// field id, length and event offset to each non-empty field's rank.
+__device__ __forceinline__ void block_scan2(int64_t& a, int64_t& b, int64_t* wa, int64_t* wb, int64_t& ta,
+                                            int64_t& tb) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int64_t ia = a, ib = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t ya = __shfl_up_sync(0xffffffffu, ia, o), yb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ya;
+      ib += yb;
+    }
+  }
+  if (lane == 31) {
+    wa[warp] = ia;
+    wb[warp] = ib;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int64_t xa = wa[lane], xb = wb[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t ya = __shfl_up_sync(0xffffffffu, xa, o), yb = __shfl_up_sync(0xffffffffu, xb, o);
+      if (lane >= o) {
+        xa += ya;
+        xb += yb;
+      }
+    }
+    wa[lane] = xa;
+    wb[lane] = xb;
+  }
+  __syncthreads();
+  const int64_t pa = warp > 0 ? wa[warp - 1] : 0, pb = warp > 0 ? wb[warp - 1] : 0;
+  ta = wa[31];
+  tb = wb[31];
+  a = pa + ia - a;  // exclusive
+  b = pb + ib - b;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) field_block_scan_kernel(const int64_t* __restrict__ flen, int64_t nf,
+                                                                int64_t* __restrict__ pre_cnt,
+                                                                int64_t* __restrict__ pre_len,
+                                                                int64_t* __restrict__ bsum) {
+  __shared__ int64_t wa[32], wb[32];
+  const int64_t f = (int64_t)blockIdx.x * 1024 + threadIdx.x;
+  const int64_t l = f < nf ? flen[f] : 0;
+  int64_t a = l > 0 ? 1 : 0, b = l, ta, tb;
+  block_scan2(a, b, wa, wb, ta, tb);
+  if (f < nf) {
+    pre_cnt[f] = a;
+    pre_len[f] = b;
+  }
+  if (threadIdx.x == 0) {
+    bsum[2 * blockIdx.x] = ta;
+    bsum[2 * blockIdx.x + 1] = tb;
+  }
+}
+
+// stats = {flags[0], flags[1], non-empty fields, routed events}
+__global__ void __launch_bounds__(1024) field_totals_kernel(int64_t* __restrict__ bsum, int64_t nb,
+                                                            const int* __restrict__ flags,
+                                                            int64_t* __restrict__ stats) {
+  __shared__ int64_t wa[32], wb[32];
+  int64_t ca = 0, cb = 0;
+  for (int64_t base = 0; base < nb; base += 1024) {
+    const int64_t i = base + threadIdx.x;
+    int64_t a = i < nb ? bsum[2 * i] : 0, b = i < nb ? bsum[2 * i + 1] : 0, ta, tb;
+    block_scan2(a, b, wa, wb, ta, tb);
+    if (i < nb) {
+      bsum[2 * i] = ca + a;
+      bsum[2 * i + 1] = cb + b;
+    }
+    ca += ta;
+    cb += tb;
+  }
+  if (threadIdx.x == 0) {
+    stats[0] = flags ? flags[0] : 0;
+    stats[1] = flags ? flags[1] : 0;
+    stats[2] = ca;
+    stats[3] = cb;
+  }
+}
+
+__global__ void field_scatter_kernel(const int64_t* __restrict__ flen, int64_t nf,
+                                     const int64_t* __restrict__ pre_cnt, const int64_t* __restrict__ pre_len,
+                                     const int64_t* __restrict__ bsum, const int64_t* __restrict__ stats,
+                                     int64_t* __restrict__ field_ids, int64_t* __restrict__ lengths,
+                                     int64_t* __restrict__ off) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f == 0) off[stats[2]] = stats[3];
+  if (f >= nf) return;
+  const int64_t l = flen[f];
+  if (l <= 0) return;
+  const int64_t blk = f >> 10;
+  const int64_t k = bsum[2 * blk] + pre_cnt[f];
+  field_ids[k] = f;
+  lengths[k] = l;
+  off[k] = bsum[2 * blk + 1] + pre_len[f];
+}
+
 int check_geo(const Geo& g) {
   SSLA_CHECK_ARG(g.B >= 0 && g.H > 0 && g.W > 0 && g.kh > 0 && g.kw > 0 && g.sh > 0 && g.sw > 0 && g.oh >= 0 &&
                      g.ow >= 0,
@@ -218,5 +322,36 @@ extern "C" int ssla_route_fill(const int* map, const int64_t* gstart, const int6
   else SSLA_FILL(32);
 #undef SSLA_FILL
   SSLA_CHECK_LAUNCH("ssla_route_fill");
+  return SSLA_OK;
+}
+
+extern "C" size_t ssla_route_compact_fields_workspace_bytes(int64_t nf) {
+  const int64_t nb = (nf + 1023) / 1024;
+  return (size_t)(2 * nf + 2 * nb + 2) * sizeof(int64_t);
+}
+
+extern "C" int ssla_route_compact_fields(const int64_t* flen, int64_t nf, const int* flags, int64_t* field_ids,
+                                         int64_t* lengths, int64_t* field_off, int64_t* stats, void* workspace,
+                                         size_t workspace_bytes, ssla_stream_t stream) {
+  SSLA_CHECK_ARG(nf >= 0, "ssla_route_compact_fields: bad size");
+  SSLA_CHECK_ARG(stats && field_off && (nf == 0 || (flen && field_ids && lengths && workspace)),
+                 "ssla_route_compact_fields: null pointer");
+  if (workspace_bytes < ssla_route_compact_fields_workspace_bytes(nf)) {
+    set_error("ssla_route_compact_fields: workspace of %zu bytes < %zu needed", workspace_bytes,
+              ssla_route_compact_fields_workspace_bytes(nf));
+    return SSLA_ERR_WORKSPACE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t nb = (nf + 1023) / 1024;
+  int64_t* pre_cnt = (int64_t*)workspace;
+  int64_t* pre_len = pre_cnt + nf;
+  int64_t* bsum = pre_len + nf;
+  if (nb > 0)
+    field_block_scan_kernel<<<(unsigned)nb, 1024, 0, s>>>(flen, nf, pre_cnt, pre_len, bsum);
+  field_totals_kernel<<<1, 1024, 0, s>>>(bsum, nb, flags, stats);
+  field_scatter_kernel<<<(unsigned)(nf > 0 ? ceil_div(nf, 256) : 1), 256, 0, s>>>(flen, nf, pre_cnt, pre_len, bsum,
+                                                                                   stats, field_ids, lengths,
+                                                                                   field_off);
+  SSLA_CHECK_LAUNCH("ssla_route_compact_fields");
   return SSLA_OK;
 }

@@ -141,21 +141,22 @@ def _replicate_gpu(gr_batch_id, gr_h, gr_w, gr_lengths, gr_time, geo, batch_size
     flen = torch.empty(max(B * oh * ow, 1), dtype=torch.int64, device=dev)
     _lib.check(L.ssla_route_field_lengths(pmap.data_ptr(), glen.data_ptr(), B, H, W, kh, kw, sh, sw, pt, pl, oh, ow,
                                           flen.data_ptr(), st), "route_field_lengths")
-    # non-empty fields in ascending id order, compacted by a scatter to their running count
-    # (the one host read of the routing: flags, field count and event count together)
+    # non-empty fields in ascending id order with their lengths and event offsets (compaction
+    # kernels), then the one host read of the routing: flags, field count and event count
     nf_all = B * oh * ow
-    nonempty = flen[:nf_all] > 0
-    rank = torch.cumsum(nonempty, 0)
-    stats = torch.cat([flags.to(torch.int64), rank[-1:] if nf_all else rank.new_zeros(1), flen[:nf_all].sum().view(1)])
+    fid_buf = torch.empty(max(nf_all, 1), dtype=torch.int64, device=dev)
+    len_buf = torch.empty(max(nf_all, 1), dtype=torch.int64, device=dev)
+    off_buf = torch.empty(nf_all + 1, dtype=torch.int64, device=dev)
+    stats = torch.empty(4, dtype=torch.int64, device=dev)
+    nws = L.ssla_route_compact_fields_workspace_bytes(nf_all)
+    ws = torch.empty(max(nws, 8), dtype=torch.uint8, device=dev)
+    _lib.check(L.ssla_route_compact_fields(flen.data_ptr(), nf_all, flags.data_ptr(), fid_buf.data_ptr(),
+                                           len_buf.data_ptr(), off_buf.data_ptr(), stats.data_ptr(), ws.data_ptr(),
+                                           nws, st), "route_compact_fields")
     bad_coord, unsorted, F, n_ev = stats.tolist()
     if bad_coord or unsorted:
         return None
-    field_ids = torch.empty(F + 1, dtype=torch.int64, device=dev)
-    field_ids.scatter_(0, torch.where(nonempty, rank - 1, F), torch.arange(nf_all, device=dev))
-    field_ids = field_ids[:F]
-    lengths = flen[field_ids]
-    off = torch.zeros(F + 1, dtype=torch.int64, device=dev)
-    torch.cumsum(lengths, 0, out=off[1:])
+    field_ids, lengths, off = fid_buf[:F], len_buf[:F], off_buf[:F + 1]
     src = torch.empty(n_ev, dtype=torch.int64, device=dev)
     pos = torch.empty(n_ev, dtype=torch.int64, device=dev)
     t = torch.empty(n_ev, dtype=torch.int64, device=dev)
