@@ -218,6 +218,45 @@ __global__ void __launch_bounds__(RM_THREADS) rows_matmul_kernel(const float* __
 }
 
 // One thread per row (C <= 32).
+// Rows of C = 4 * L floats (L <= 32 lanes of one float4 each), GP lanes per row (GP the power
+// of two >= L): coalesced 16-byte loads of x and r, mean and variance (two passes over the
+// registers) reduced by xor shuffles inside the lane group.
+template <int GP>
+__global__ void __launch_bounds__(256) ln_row_vec4_kernel(const float* __restrict__ x, const float* __restrict__ r,
+                                                          const float* __restrict__ w, const float* __restrict__ b,
+                                                          int64_t rows, int C, float eps, float* __restrict__ out) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = t / GP;
+  const int gl = (int)(t % GP);
+  const int L = C >> 2;
+  const bool on = row < rows && gl < L;
+  const int64_t o = row * C + 4 * gl;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (on) {
+    v = *reinterpret_cast<const float4*>(x + o);
+    if (r) {
+      const float4 u = *reinterpret_cast<const float4*>(r + o);
+      v.x += u.x;
+      v.y += u.y;
+      v.z += u.z;
+      v.w += u.w;
+    }
+  }
+  float s = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+  for (int k = GP / 2; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k, GP);
+  const float mean = s / C;
+  const float dx = v.x - mean, dy = v.y - mean, dz = v.z - mean, dw = v.w - mean;
+  float q = on ? fmaf(dx, dx, fmaf(dy, dy, fmaf(dz, dz, dw * dw))) : 0.f;
+#pragma unroll
+  for (int k = GP / 2; k > 0; k >>= 1) q += __shfl_xor_sync(0xffffffffu, q, k, GP);
+  const float rstd = rsqrtf(q / C + eps);
+  if (!on) return;
+  const float4 ww = *reinterpret_cast<const float4*>(w + 4 * gl), bb = *reinterpret_cast<const float4*>(b + 4 * gl);
+  *reinterpret_cast<float4*>(out + o) =
+      make_float4(dx * rstd * ww.x + bb.x, dy * rstd * ww.y + bb.y, dz * rstd * ww.z + bb.z, dw * rstd * ww.w + bb.w);
+}
+
 __global__ void __launch_bounds__(256) ln_row_thread_kernel(const float* __restrict__ x, const float* __restrict__ r,
                                                             const float* __restrict__ w, const float* __restrict__ b,
                                                             int64_t rows, int C, float eps, float* __restrict__ out) {
@@ -381,7 +420,21 @@ extern "C" int ssla_layernorm_residual_fwd(const float* x, const float* r, const
   if (rows == 0) return SSLA_OK;
   SSLA_CHECK_ARG(x && w && b && out, "ssla_layernorm_residual_fwd: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  if (C <= 32) {
+  const bool vec4 = C % 4 == 0 && C <= 128 && ((uintptr_t)x | (uintptr_t)r | (uintptr_t)w | (uintptr_t)b |
+                                                (uintptr_t)out) % 16 == 0;
+  if (vec4) {
+    const int L = (int)(C / 4);
+    const int GP = L <= 1 ? 1 : L <= 2 ? 2 : L <= 4 ? 4 : L <= 8 ? 8 : L <= 16 ? 16 : 32;
+    const unsigned grid = (unsigned)ceil_div(rows * GP, 256);
+    switch (GP) {
+      case 1: ln_row_vec4_kernel<1><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+      case 2: ln_row_vec4_kernel<2><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+      case 4: ln_row_vec4_kernel<4><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+      case 8: ln_row_vec4_kernel<8><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+      case 16: ln_row_vec4_kernel<16><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+      default: ln_row_vec4_kernel<32><<<grid, 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out); break;
+    }
+  } else if (C <= 32) {
     ln_row_thread_kernel<<<(unsigned)ceil_div(rows, 256), 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out);
   } else {
     ln_row_warp_kernel<<<(unsigned)ceil_div(rows * 32, 256), 256, 0, s>>>(x, r, w, b, rows, (int)C, eps, out);

@@ -153,7 +153,7 @@ def test_layers_backward_runs():
     assert g is not None and torch.isfinite(g).all() and g.abs().sum() > 0
 
 
-@pytest.mark.parametrize("C", [1, 7, 12, 32, 48, 96, 256])
+@pytest.mark.parametrize("C", [1, 4, 7, 12, 24, 32, 48, 96, 128, 256])
 def test_layernorm_residual_matches_torch(C):
     from ssla_b200.ops.mos import layernorm_residual
 
