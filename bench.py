@@ -354,6 +354,57 @@ def _event_time(fn, n, stream, flush=None):
 MODEL_B = 64  # batch 64 split across ranks
 
 
+def model_kernel_fractions(run_forward, hbm):
+    """Per-call CUDA-event time and algorithmic bytes of the model's four largest kernel families
+    over one extra forward (outside any timed region): the split-TF32 projection GEMMs (A rows
+    read + output written), the MoS patch scan (gathered projected rows + indices + output rows),
+    the fused LayerNorm (x, residual, output) and the routing (replicate_to_fields: 24 B per routed
+    event + 16 B per field; its one host read included).  Each call is bracketed by a device
+    synchronize, so small calls carry their launch latency.  The functions are wrapped only for
+    this forward and restored afterwards."""
+    from ssla_b200.ops import mos as _mos
+    from ssla_b200.utils import routing as _routing
+
+    rec = {}
+
+    def wrap(mod, attr, name, nbytes):
+        fn = getattr(mod, attr)
+
+        def w(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            out = fn(*a, **k)
+            e1.record()
+            torch.cuda.synchronize()
+            us, b = rec.get(name, (0.0, 0))
+            rec[name] = (us + 1e3 * e0.elapsed_time(e1), b + nbytes(out, *a, **k))
+            return out
+
+        setattr(mod, attr, w)
+        return fn
+
+    saved = [
+        (_mos, "matmul_tc", wrap(_mos, "matmul_tc", "gemm_tf32x3",
+                                 lambda out, a, *r, **k: 4 * (a.numel() + out.numel()))),
+        (_mos, "patch_scan_routed", wrap(_mos, "patch_scan_routed", "mos_patch_scan",
+                                         lambda out, y, src, pos, P, Pg, cu, C, z: src.numel() * (
+                                             16 * C + 8 + (8 if pos is not None else 0)) + 8 * cu.numel())),
+        (_mos, "layernorm_residual", wrap(_mos, "layernorm_residual", "layernorm_residual",
+                                          lambda out, x, r, *a, **k: 4 * x.numel() * (3 if r is not None else 2))),
+        (_routing, "_replicate_gpu", wrap(_routing, "_replicate_gpu", "routing",
+                                          lambda out, *a, **k: 0 if out is None else
+                                          24 * out["src"].numel() + 16 * out["field_id"].numel())),
+    ]
+    try:
+        run_forward()
+    finally:
+        for mod, attr, fn in saved:
+            setattr(mod, attr, fn)
+    return {n: {"us": us, "alg_bytes": b, "achieved_gbs": b / us / 1e3, "frac": b / us / 1e3 / hbm}
+            for n, (us, b) in sorted(rec.items(), key=lambda kv: -kv[1][0])}
+
+
 def bench_model(dev, world, rank, dist, steps=3, warmup=2, variant="S"):
     """SSLA forward (preprocessing, layer stack, grids, YOLOX decode) on this rank's share of a
     64-sample batch of synthetic 100 ms / 240x304 event streams, then one NCCL all_gather of the
@@ -392,7 +443,15 @@ def bench_model(dev, world, rank, dist, steps=3, warmup=2, variant="S"):
         dist.barrier()
     torch.cuda.synchronize(dev)
     secs = _max_over_ranks(_event_time(step, steps, stream), dist, dev)
+    kernels = None
+    if rank == 0:
+        def forward_once():
+            with torch.no_grad():
+                m(ev_h.to(dev), ln_h.to(dev))
+
+        kernels = model_kernel_fractions(forward_once, peaks()[0])
     return {"metric": f"SSLA-{variant} forward frames/s", "value": MODEL_B * steps / secs, "unit": "frames/s",
+            "kernels": kernels,
             "events_per_s": n_events * steps / secs, "ms_per_batch": 1e3 * secs / steps, "batch": MODEL_B,
             "per_rank_batch": b - a, "scaling": "strong", "steps": steps, "warmup": warmup,
             "includes": "host->device event copy, preprocessing, 14 layers, grids, head decode, NCCL gather",
