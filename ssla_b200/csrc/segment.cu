@@ -392,9 +392,11 @@ template <typename T, int G, int MODE>
 __global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kernel(
     const T* __restrict__ src, const int64_t* __restrict__ off, const int64_t* __restrict__ tmp,
     int64_t* __restrict__ sorted, int R, int S, T* __restrict__ out_max, int64_t* __restrict__ arg,
-    T* __restrict__ out_mean, T* __restrict__ back) {
+    T* __restrict__ out_mean, T* __restrict__ back, bool presorted) {
   griddep_launch_dependents();
   griddep_wait();
+  // presorted: the ids of each segment are already ascending in `tmp` (a sorted CSR), or, with
+  // tmp == nullptr, the segment is the row range itself (sorted index: ids b .. b+n-1).
   // Row ids, offsets and counts fit in 32 bits (the launcher checks R < 2^31); the row width
   // C = G * V is a compile-time constant, so no 64-bit index arithmetic is issued per row.
   constexpr int V = Row16<T>::V;
@@ -424,7 +426,11 @@ __global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kern
   int mine[kSlots];  // small: slot k of lane gl holds the (k * GP + gl)-th smallest row id
 #pragma unroll
   for (int k = 0; k < kSlots; ++k) mine[k] = kNone;
-  if (small) {
+  auto id_at = [&](int i) -> int { return tmp ? (int)tmp[b + i] : b + i; };
+  if (small && presorted) {
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k) mine[k] = k * GP + gl < n ? id_at(k * GP + gl) : kNone;
+  } else if (small) {
     int id[kSlots], rank[kSlots];
 #pragma unroll
     for (int k = 0; k < kSlots; ++k) {
@@ -455,7 +461,7 @@ __global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kern
         }
       }
     }
-  } else {
+  } else if (!presorted) {
     for (int i = gl; i < n; i += GP) {
       const int x = (int)tmp[b + i];
       int rank = 0;
@@ -467,7 +473,8 @@ __global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kern
   // the rows of slot window p0 (GP rows, ascending) as one lane value each
   auto window_ids = [&](int p0, int k) -> int {
     if (small) return mine[k];
-    return p0 + gl < n ? (int)sorted[b + p0 + gl] : kNone;
+    if (p0 + gl >= n) return kNone;
+    return presorted ? id_at(p0 + gl) : (int)sorted[b + p0 + gl];
   };
 #pragma unroll 1
   for (int k = 0, p0 = 0; p0 < n; ++k, p0 += GP) {
@@ -524,7 +531,7 @@ __global__ void __launch_bounds__(256, MODE == kPoolArg ? 2 : 4) pool_fused_kern
   if (back) {
     // row ids straight from the list (in any order: each row's store is independent)
     for (int u = 0; u < n; ++u) {
-      const int r = (int)tmp[b + u];
+      const int r = id_at(u);
       Vec<T, V>::store(back + (size_t)r * C + c, mx);
     }
   }
@@ -618,6 +625,14 @@ size_t csr_ws_bytes(int64_t R, int64_t S) {
 }  // namespace
 }  // namespace ssla
 
+namespace ssla {
+namespace {
+template <typename T>
+int reduce_one_pass(const void* src, const int64_t* off, const int64_t* rows, int64_t R, int64_t S, int64_t C,
+                    int op, void* out, int64_t* arg, cudaStream_t s);
+}  // namespace
+}  // namespace ssla
+
 using namespace ssla;
 
 extern "C" int ssla_segment_offsets_sorted(const int64_t* index, int64_t R, int64_t S,
@@ -655,8 +670,10 @@ extern "C" int ssla_segment_reduce(const void* src, int dtype, const int64_t* se
   if (S == 0 || C == 0) return SSLA_OK;
   SSLA_CHECK_ARG(seg_offsets && out && (R == 0 || src), "ssla_segment_reduce: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
-  return SSLA_DISPATCH_DTYPE(dtype, T,
-                             [&] { return run_reduce<T>(src, seg_offsets, rows, R, S, C, op, out, arg, s); });
+  return SSLA_DISPATCH_DTYPE(dtype, T, [&] {
+    const int rc = reduce_one_pass<T>(src, seg_offsets, rows, R, S, C, op, out, arg, s);
+    return rc != SSLA_ERR_UNSUPPORTED ? rc : run_reduce<T>(src, seg_offsets, rows, R, S, C, op, out, arg, s);
+  });
 }
 
 extern "C" int ssla_gather_rows(const void* src, int dtype, const int64_t* index, int64_t R,
@@ -686,18 +703,54 @@ namespace ssla {
 namespace {
 template <typename T, int G>
 void launch_pool(int mode, cudaStream_t s, const void* src, const int64_t* off, const int64_t* tmp,
-                 int64_t* sorted, int64_t R, int64_t S, void* out_max, int64_t* arg, void* out_mean, void* back) {
+                 int64_t* sorted, int64_t R, int64_t S, void* out_max, int64_t* arg, void* out_mean, void* back,
+                 bool presorted = false) {
   constexpr int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : G <= 8 ? 8 : G <= 16 ? 16 : 32;
   const dim3 grid((unsigned)ceil_div(S * GP, 256));
   if (mode == kPoolArg)
     launch_pdl(pool_fused_kernel<T, G, kPoolArg>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
-               (int)S, (T*)out_max, arg, (T*)out_mean, (T*)back);
+               (int)S, (T*)out_max, arg, (T*)out_mean, (T*)back, presorted);
   else if (mode == kPoolSum)
     launch_pdl(pool_fused_kernel<T, G, kPoolSum>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted, (int)R,
-               (int)S, (T*)nullptr, (int64_t*)nullptr, (T*)out_mean, (T*)nullptr);
+               (int)S, (T*)nullptr, (int64_t*)nullptr, (T*)out_mean, (T*)nullptr, presorted);
   else
     launch_pdl(pool_fused_kernel<T, G, kPoolMaxMean>, grid, dim3(256), 0, s, (const T*)src, off, tmp, sorted,
-               (int)R, (int)S, (T*)out_max, (int64_t*)nullptr, (T*)out_mean, (T*)back);
+               (int)R, (int)S, (T*)out_max, (int64_t*)nullptr, (T*)out_mean, (T*)back, presorted);
+}
+
+// One reduction over segments whose ids are already ascending (a sorted CSR, or the row ranges of
+// a sorted index when rows == nullptr) by the one-pass kernel: no sort, 16-byte lanes.
+// SSLA_ERR_UNSUPPORTED (nothing launched) when the row width or alignment does not fit it.
+template <typename T>
+int reduce_one_pass(const void* src, const int64_t* off, const int64_t* rows, int64_t R, int64_t S, int64_t C,
+                    int op, void* out, int64_t* arg, cudaStream_t s) {
+  constexpr int V = 16 / (int)sizeof(T);
+  const int64_t G = C / V;
+  const bool ok = C % V == 0 &&
+                  (G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8 || G == 12 || G == 16 || G == 24 ||
+                   G == 32) &&
+                  aligned_to(src, 16) && aligned_to(out, 16) && R < (int64_t)INT32_MAX && S < (int64_t)INT32_MAX;
+  if (!ok) return SSLA_ERR_UNSUPPORTED;
+  const int mode = op == SSLA_REDUCE_SUM ? kPoolSum : (op == SSLA_REDUCE_MAX && arg ? kPoolArg : kPoolMaxMean);
+  void* mx = op == SSLA_REDUCE_MAX ? out : nullptr;
+  void* mean = op == SSLA_REDUCE_MAX ? nullptr : out;
+#define SSLA_RED1(GG) \
+  case GG: launch_pool<T, GG>(mode, s, src, off, rows, nullptr, R, S, mx, arg, mean, nullptr, true); break
+  switch (G) {
+    SSLA_RED1(1);
+    SSLA_RED1(2);
+    SSLA_RED1(3);
+    SSLA_RED1(4);
+    SSLA_RED1(6);
+    SSLA_RED1(8);
+    SSLA_RED1(12);
+    SSLA_RED1(16);
+    SSLA_RED1(24);
+    default: launch_pool<T, 32>(mode, s, src, off, rows, nullptr, R, S, mx, arg, mean, nullptr, true); break;
+  }
+#undef SSLA_RED1
+  SSLA_CHECK_LAUNCH("ssla_segment_reduce");
+  return SSLA_OK;
 }
 
 // Counting sort of the row ids by segment (offsets + ids in arrival order), then the one-pass
