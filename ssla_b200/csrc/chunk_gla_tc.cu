@@ -361,10 +361,21 @@ __device__ __forceinline__ void prologue(uint32_t* tbase_s, uint32_t ncols, uint
 template <typename Tg> __host__ __device__ constexpr int gate_bytes() { return BT * D * (int)sizeof(Tg); }
 template <typename Tg> __host__ __device__ constexpr int ls_stage_bytes() { return 2 * TILE + gate_bytes<Tg>(); }
 
+// Local-state gate scan: thread (column pair 2 * (t % 32), group t / 32) scans LS_RG rows.
+constexpr int LS_NG = NT / 32, LS_RG = BT / LS_NG;
 struct LsSmem {
-  float part[NG][D];
+  alignas(16) float part[LS_NG][D];
   unsigned int span_bits;
 };
+
+// Two consecutive gate values (columns c, c + 1) of a raw, unswizzled 64 x 64 gate tile.
+template <typename Tg> __device__ __forceinline__ float2 ld2_gate(const unsigned char* raw, int r, int c) {
+  const Tg* p = reinterpret_cast<const Tg*>(raw) + r * D + c;
+  return make_float2(ldf(p), ldf(p + 1));
+}
+template <> __device__ __forceinline__ float2 ld2_gate<float>(const unsigned char* raw, int r, int c) {
+  return *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(raw) + r * D + c);
+}
 
 // Byte offset of fp32 element (r, c) of a 64 x 64 tile kept as two 32-column halves, each in
 // the 128-byte-swizzled layout of a TMA box of 32 fp32 columns x 64 rows.
@@ -507,51 +518,65 @@ __global__ void __launch_bounds__(NT + 32, 3) tc_local_state_kernel(
         cbar();
       }
       // in-chunk prefix sums of the gate, fused with the in-place scaling of the a tile:
-      // mode 0 (state increment) by exp(gL - gc), mode 1 (adjoint increment) by scale exp(gc)
+      // mode 0 (state increment) by exp(gL - gc), mode 1 (adjoint increment) by scale exp(gc).
+      // Thread (column pair c, c + 1; group qt) scans rows LS_RG * qt .. + LS_RG - 1, so every
+      // shared-memory access moves two elements.
       {
-        const int c = tid & 63, qt = tid >> 6;
-        const Tg* gr = reinterpret_cast<const Tg*>(sB + TILE);
+        const int c = 2 * (tid & 31), qt = tid >> 5;
         if (tid == 0) S.span_bits = 0u;
-        float xs[RG];
-        float run = 0.f;
+        float2 xs[LS_RG];
+        float r0 = 0.f, r1 = 0.f;
 #pragma unroll
-        for (int i = 0; i < RG; ++i) {
-          run += ldf(gr + (RG * qt + i) * D + c);
-          xs[i] = run;
+        for (int i = 0; i < LS_RG; ++i) {
+          const float2 gv = ld2_gate<Tg>(sB + TILE, LS_RG * qt + i, c);
+          r0 += gv.x;
+          r1 += gv.y;
+          xs[i] = make_float2(r0, r1);
         }
         PHASE(pitem, 24);
-        S.part[qt][c] = run;
+        *reinterpret_cast<float2*>(&S.part[qt][c]) = make_float2(r0, r1);
         cbar();
         PHASE(pitem, 25);
-        float off = 0.f, gl = 0.f, ref = 0.f;
+        float off0 = 0.f, off1 = 0.f, gl0 = 0.f, gl1 = 0.f, ref0 = 0.f, ref1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < NG; ++j) {
-          const float pj = S.part[j][c];
-          if (j < qt) off += pj;
-          if (j <= 31 / RG) ref += pj;
-          gl += pj;
+        for (int j = 0; j < LS_NG; ++j) {
+          const float2 pj = *reinterpret_cast<const float2*>(&S.part[j][c]);
+          const float p0 = pj.x, p1 = pj.y;
+          if (j < qt) {
+            off0 += p0;
+            off1 += p1;
+          }
+          if (j <= 31 / LS_RG) {
+            ref0 += p0;
+            ref1 += p1;
+          }
+          gl0 += p0;
+          gl1 += p1;
         }
         // all loads before any store: the compiler cannot tell the tile elements apart, so
-        // an interleaved load / store loop would run one element at a time
-        float m = 0.f, a[RG];
+        // an interleaved load / store loop would run one pair at a time
+        float m = 0.f, a0[LS_RG], a1[LS_RG];
 #pragma unroll
-        for (int i = 0; i < RG; ++i) a[i] = ldf(reinterpret_cast<const T*>(sA + toff(RG * qt + i, c)));
+        for (int i = 0; i < LS_RG; ++i) ld2_tile<T>(sA, LS_RG * qt + i, c, a0[i], a1[i]);
 #pragma unroll
-        for (int i = 0; i < RG; ++i) {
-          const float gc = xs[i] + off;
-          a[i] *= mode == 0 ? __expf(gl - gc) : scale * __expf(gc);
-          m = fmaxf(m, fabsf(gc - ref));
+        for (int i = 0; i < LS_RG; ++i) {
+          const float gc0 = xs[i].x + off0, gc1 = xs[i].y + off1;
+          a0[i] *= mode == 0 ? __expf(gl0 - gc0) : scale * __expf(gc0);
+          a1[i] *= mode == 0 ? __expf(gl1 - gc1) : scale * __expf(gc1);
+          m = fmaxf(m, fmaxf(fabsf(gc0 - ref0), fabsf(gc1 - ref1)));
         }
 #pragma unroll
-        for (int i = 0; i < RG; ++i) stf(reinterpret_cast<T*>(sA + toff(RG * qt + i, c)), a[i]);
+        for (int i = 0; i < LS_RG; ++i) st2_tile<T>(sA, LS_RG * qt + i, c, a0[i], a1[i]);
         PHASE(pitem, 26);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) atomicMax(&S.span_bits, __float_as_uint(m));
         PHASE(pitem, 27);
         if (qt == 0) {
-          decay[item * D + c] = __expf(gl);
-          escale[item * D + c] = mode == 0 ? __expf(ref) : __expf(gl - ref);
+          decay[item * D + c] = __expf(gl0);
+          decay[item * D + c + 1] = __expf(gl1);
+          escale[item * D + c] = mode == 0 ? __expf(ref0) : __expf(gl0 - ref0);
+          escale[item * D + c + 1] = mode == 0 ? __expf(ref1) : __expf(gl1 - ref1);
         }
       }
       PHASE(pitem, 17);
