@@ -756,23 +756,26 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
 }
 
 // --------------------------------------------------------------------------- backward
-// stage: q | k | v | do | H' | dH' tiles | raw gate.  Double-buffered work tiles: gated Q^, K^
-// (which become the staged dq, dk tiles of the item's epilogue), gate factors E (then dgc);
-// single: the score tiles A, dA and the staged dv tile.
+// stage: q | k | v | do | H' | dH' tiles | raw gate.  Work tiles: gated Q^, K^ (which become
+// the staged dq, dk tiles of the item's epilogue), the score tiles A and dA (A's buffer then
+// stages dv), gate factors E (then dgc).  Two CTAs per SM, one stage and 256 TMEM columns each:
+// a CTA runs its items one after another (the second MMA batch reuses the first batch's TMEM
+// columns once their epilogue has read them), and the two CTAs of an SM overlap each other's
+// chains; the producer refills the stage while the CTA writes the item's outputs.
 template <typename Tg> __host__ __device__ constexpr int bw_stage_bytes() { return 6 * TILE + gate_bytes<Tg>(); }
-constexpr int BW_NS = 2;
+constexpr int BW_NS = 1;
 
 struct BwSmem {
-  float E[2][BT * LDG];  // exp(gc - ref) per buffer; dgc scratch in the epilogue
-  float part[NG][D];     // gate-scan group sums
-  float dpart[NG][D];    // dg reverse-cumsum group sums
-  float hd[NG][D];       // H'.dH' partial sums per key row
-  float gp[2][D];        // dH'.S partial sums per key row, per column half
-  float dgl[2][D];       // dgL per key index, per buffer
+  float E[BT * LDG];   // exp(gc - ref); dgc scratch in the epilogue
+  float part[NG][D];   // gate-scan group sums
+  float dpart[NG][D];  // dg reverse-cumsum group sums
+  float hd[NG][D];     // H'.dH' partial sums per key row
+  float gp[2][D];      // dH'.S partial sums per key row, per column half
+  float dgl[D];        // dgL per key index
 };
 
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
+__global__ void __launch_bounds__(NT + 32, 2) tc_bwd_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
     const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mh,
@@ -784,12 +787,12 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = align1024(smem_raw);
   constexpr int STAGE = bw_stage_bytes<Tg>();
-  unsigned char* sQg = smem + NS * STAGE;  // [2] tiles
-  unsigned char* sKg = sQg + 2 * TILE;     // [2] tiles
-  unsigned char* sA = sKg + 2 * TILE;
+  unsigned char* gQ = smem + NS * STAGE;
+  unsigned char* gK = gQ + TILE;
+  unsigned char* sA = gK + TILE;
   unsigned char* sdA = sA + TILE;
-  unsigned char* sOut = sdA + TILE;
-  BwSmem& W = *reinterpret_cast<BwSmem*>(sOut + TILE);
+  unsigned char* sOut = sA;  // dv is staged in A's buffer once the second batch has read A
+  BwSmem& W = *reinterpret_cast<BwSmem*>(sdA + TILE);
   __shared__ uint64_t bars[2 + 2 * NS];  // batch 1, batch 2, full[NS], empty[NS]
   __shared__ uint32_t tbase_s;
   __shared__ int s_bad;
@@ -797,13 +800,13 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
   uint64_t* full = bars + 2;
   uint64_t* empty = bars + 2 + NS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  prologue<2 + 2 * NS>(&tbase_s, 512, bars, bad);
+  prologue<2 + 2 * NS>(&tbase_s, 256, bars, bad);
   const uint32_t tb = tbase_s;
   if (tid == 0)
     for (const CUtensorMap* m : {&mq, &mk, &mv, &mdo, &mg, &mh, &mdh, &mdq, &mdk, &mdv}) prefetch_tensormap(m);
   constexpr uint32_t F = Fmt<T>::v;
-  // TMEM: batch 1 (A, dA, S) at columns 0..191, batch 2 (dq~, dk~, dv) at 256..447
-  const uint32_t tA = tb, tdA = tb + 64, tS = tb + 128, tQ = tb + 256, tK = tb + 320, tV = tb + 384;
+  // TMEM: batch 1 (A, dA, S) and then batch 2 (dv, dq~, dk~) at columns 0..191
+  const uint32_t tA = tb, tdA = tb + 64, tS = tb + 128, tV = tb, tQ = tb + 64, tK = tb + 128;
   griddep_wait();
   if (tid >= NT) {  // producer warp
     const CUtensorMap* m16[4] = {&mq, &mk, &mv, &mdo};
@@ -819,9 +822,6 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
     const Own me;
     uint32_t ph1 = 0, ph2 = 0;
     int ci = 0;
-    bool pending = false;
-    Item prev{};
-    int prev_b = 0;
     auto poison_rows = [&](const Item& x) {
       const int64_t base = (x.t0 * H + x.head) * D;
       for (int e = tid; e < x.len * D; e += NT) {
@@ -832,17 +832,15 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         dg[off] = kNaN;
       }
     };
-    // epilogue of the pending item (buffer pb): dv, dq, dk and dg
-    auto finish = [&](const Item& x, int pb) {
+    // epilogue of the item: dv, dq, dk and dg (after its second MMA batch)
+    auto finish = [&](const Item& x) {
       PHASE(ci - 1, 10);
       wait_mma(&bars[1], ph2, bad);
       PHASE(ci - 1, 11);
       const bool poisoned = *bad;
       const bool whole = x.len == BT;
       const int64_t base = (x.t0 * H + x.head) * D;
-      unsigned char* gQ = sQg + pb * TILE;
-      unsigned char* gK = sKg + pb * TILE;
-      float* E = W.E[pb];
+      float* E = W.E;
       {
         float z[1][16];
         ld_acc<1>(ep, {tV}, z);
@@ -876,7 +874,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
           // dgc = q dq - k dk = Q^ dq~ - K^ dk~ (the gated tiles of this item)
           E[r * LDG + c] = gq[2 * p] * acc[0][2 * p] - gk[2 * p] * acc[1][2 * p];
           E[r * LDG + c + 1] = gq[2 * p + 1] * acc[0][2 * p + 1] - gk[2 * p + 1] * acc[1][2 * p + 1];
-          if (whole) {  // this thread's own elements: the gated tiles become the staged outputs
+          if (whole) {  // the gated tiles become the staged outputs
             st2_tile<T>(gQ, r, c, q0, q1);
             st2_tile<T>(gK, r, c, k0, k1);
           } else if (r < x.len) {
@@ -908,7 +906,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         }
         W.dpart[qt][c] = run;
         cbar();
-        float after = W.dgl[pb][c];
+        float after = W.dgl[c];
 #pragma unroll
         for (int j = 0; j < NG; ++j)
           if (j > qt) after += W.dpart[j][c];
@@ -934,19 +932,17 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         cbar();
       }
       if (exact || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
-        if (pending) finish(prev, prev_b);
-        pending = false;
         if (*bad) poison_rows(x);
         cbar();
         if (tid == 0) mbar_arrive(&empty[st]);
         return;
       }
-      const int b = ci & 1;
-      unsigned char* gQ = sQg + b * TILE;
-      unsigned char* gK = sKg + b * TILE;
-      gate_prep<Tg>(W.E[b], W.part, sDH + TILE);
+      // the previous item's output stores have read gQ, gK and A before they are written again
+      // (gate_qk and the score epilogue come after gate_prep's barriers)
+      if (tid == 0) bulk_wait_read_all();
+      gate_prep<Tg>(W.E, W.part, sDH + TILE);
       PHASE(ci, 2);
-      gate_qk<T>(rQ, rK, gQ, gK, W.E[b], me, scale);
+      gate_qk<T>(rQ, rK, gQ, gK, W.E, me, scale);
       operands_ready();
       PHASE(ci, 3);
       if (tid == 0) {
@@ -971,8 +967,6 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         W.hd[me.tc >> 3][me.tr] = hd;
       }
       PHASE(ci, 4);
-      if (pending) finish(prev, prev_b);
-      PHASE(ci, 5);
       wait_mma(&bars[0], ph1, bad);
       PHASE(ci, 6);
       {
@@ -1002,7 +996,7 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         }
       }
       PHASE(ci, 7);
-      if (tid == 0) bulk_wait_read_all();  // the staged output tiles are free again
+      // every thread's TMEM reads of batch 1 are complete before batch 2 overwrites its columns
       operands_ready();
       if (tid == 0) {
         mma64(tV, sA, 1, sDO, 1, idesc_f16(64, 64, F, 1, 1), false);  // dv  = A^T do
@@ -1020,17 +1014,14 @@ __global__ void __launch_bounds__(NT + 32, 1) tc_bwd_kernel(
         float s2 = W.gp[0][tid] + W.gp[1][tid];
 #pragma unroll
         for (int j = 0; j < NG; ++j) s2 += W.hd[j][tid];
-        W.dgl[b][tid] = s2;
+        W.dgl[tid] = s2;
       }
       PHASE(ci, 9);
       ++ci;
-      pending = true;
-      prev = x;
-      prev_b = b;
+      finish(x);
     });
-    if (pending) finish(prev, prev_b);
   }
-  pipeline_end(tb, 512);
+  pipeline_end(tb, 256);
 }
 
 template <typename K_>
@@ -1211,9 +1202,9 @@ int tc_bwd(int dtype, int dtype_g, const void* q, const void* k, const void* v, 
     return rc;
   return SSLA_DISPATCH_TC(dtype, dtype_g, T_, Tg, [&] {
     auto kern = tc_bwd_kernel<T_, Tg>;
-    const size_t smem = BW_NS * bw_stage_bytes<Tg>() + 7 * TILE + sizeof(BwSmem) + kAlignSlack;
+    const size_t smem = BW_NS * bw_stage_bytes<Tg>() + 4 * TILE + sizeof(BwSmem) + kAlignSlack;
     unsigned grid = 0;
-    int rc2 = persistent_grid(kern, smem, 512, MC * H, grid, NT + 32);
+    int rc2 = persistent_grid(kern, smem, 256, MC * H, grid, NT + 32);
     if (rc2) return rc2;
     launch_pdl(kern, dim3(grid), dim3(NT + 32), smem, s, mq, mk, mv, mdo, mg, mh, mdh, mdq, mdk, mdv, chunk_tab,
                (int)MC, (int)H, scale, xflag, (T_*)dq, (T_*)dk, (T_*)dv, dg);
