@@ -384,14 +384,14 @@ __device__ __forceinline__ int toff32(int r, int c) {
 }
 
 // --------------------------------------------------------------------------- pipelined kernels
-// tc_fwd_o and tc_bwd run one CTA per SM: NT compute threads plus one producer warp.  The
+// tc_fwd_o and tc_bwd run two CTAs per SM: NT compute threads plus one producer warp each.  The
 // producer fills a ring of NS shared-memory stages by TMA, each once the consumer released it
 // (the `empty` barrier: the tensor core's completion of the last MMA batch that reads the
-// stage, or an arrive for items left to the exact kernels).  The compute threads run a
-// two-item software pipeline: item i's gating and first MMA batch are issued before item
+// stage, or an arrive for items left to the exact kernels).  In tc_fwd_o the compute threads
+// run a two-item software pipeline: item i's gating and first MMA batch are issued before item
 // i-1's last batch is waited for and its epilogue written, so the tensor core works on one
-// item while the CUDA cores work on the other; TMEM regions, gated operand tiles and gate
-// factors are double-buffered between the two items in flight.  Outputs of whole chunks are
+// item while the CUDA cores work on the other (TMEM regions double-buffered); tc_bwd runs its
+// items one after another and relies on the SM's other CTA for overlap.  Outputs of whole chunks are
 // staged in shared memory as swizzled tiles and written by TMA stores; rows of a partial chunk
 // (the next sequence's tokens follow them) are stored directly.
 
