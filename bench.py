@@ -50,7 +50,7 @@ ALG_FLOPS = 12 * 2 * K * V * TOKENS * H
 # DRAM bytes (read + write) of one ssla_chunk_gla_bwd call: dram__bytes_read.sum +
 # dram__bytes_write.sum of its launches (adjoint increments, reverse state scan, tensor-core
 # backward, exact path), from an ncu capture of `bench.py --leg profile-chunk` (cold L2).
-BWD_DRAM_BYTES = 105_900_000
+BWD_DRAM_BYTES = 106_900_000
 METRIC = "chunk-GLA fwd+bwd tokens/s"
 # fwd: chunk table, local state, state scan, tensor-core output, exact-path launch; bwd reuses the
 # saved chunk table: adjoint increments, reverse scan, tensor-core backward, exact path
