@@ -384,14 +384,11 @@ __device__ __forceinline__ int toff32(int r, int c) {
 }
 
 // --------------------------------------------------------------------------- pipelined kernels
-// tc_fwd_o and tc_bwd run two CTAs per SM: NT compute threads plus one producer warp each.  The
-// producer fills a ring of NS shared-memory stages by TMA, each once the consumer released it
-// (the `empty` barrier: the tensor core's completion of the last MMA batch that reads the
-// stage, or an arrive for items left to the exact kernels).  In tc_fwd_o the compute threads
-// run a two-item software pipeline: item i's gating and first MMA batch are issued before item
-// i-1's last batch is waited for and its epilogue written, so the tensor core works on one
-// item while the CUDA cores work on the other (TMEM regions double-buffered); tc_bwd runs its
-// items one after another and relies on the SM's other CTA for overlap.  Outputs of whole chunks are
+// tc_fwd_o (three CTAs per SM) and tc_bwd (two) run NT compute threads plus one producer warp
+// per CTA.  The producer fills a ring of NS shared-memory stages by TMA, each once the consumer
+// released it (the `empty` barrier: the tensor core's completion of the last MMA batch that
+// reads the stage, or an arrive for items left to the exact kernels).  The compute threads run
+// their items one after another; the other CTAs of the SM overlap their chains.  Outputs of whole chunks are
 // staged in shared memory as swizzled tiles and written by TMA stores; rows of a partial chunk
 // (the next sequence's tokens follow them) are stored directly.
 
@@ -618,13 +615,14 @@ __global__ void __launch_bounds__(NT + 32, 3) tc_local_state_kernel(
 
 // --------------------------------------------------------------------------- forward output
 // stage: q | k | v | H' tiles | raw gate.  Q^ and K^ are gated in place.
-// Two CTAs per SM (two independent item pipelines): two stages each, and the staged output
-// tile shares its buffer with the score tile A.
+// Three CTAs per SM (three independent item pipelines): one stage and 128 TMEM columns each;
+// a CTA runs its items one after another and the staged output tile shares its buffer with the
+// score tile A.
 template <typename Tg> __host__ __device__ constexpr int fo_stage_bytes() { return 4 * TILE + gate_bytes<Tg>(); }
-constexpr int FO_NS = 2;
+constexpr int FO_NS = 1;
 
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
+__global__ void __launch_bounds__(NT + 32, 3) tc_fwd_o_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mg,
     const __grid_constant__ CUtensorMap mh, const __grid_constant__ CUtensorMap mo,
@@ -644,7 +642,7 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
   uint64_t* full = bars + 2;
   uint64_t* empty = bars + 2 + NS;
   const int tid = threadIdx.x;
-  prologue<2 + 2 * NS>(&tbase_s, 256, bars, bad);
+  prologue<2 + 2 * NS>(&tbase_s, 128, bars, bad);
   const uint32_t tb = tbase_s;
   if (tid == 0)
     for (const CUtensorMap* m : {&mq, &mk, &mv, &mg, &mh, &mo}) prefetch_tensormap(m);
@@ -663,16 +661,13 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
     const Epi ep;
     const Own me;
     uint32_t ph1 = 0, ph2 = 0;
-    int ci = 0;             // items computed so far (TMEM region parity)
-    bool pending = false;   // an item whose last batch is issued and epilogue not yet written
-    Item prev{};
-    int prev_b = 0;
-    // epilogue of the pending item: O from TMEM region pb -> staged tile + TMA store (whole
-    // chunks) or direct stores (partial chunks)
-    auto finish = [&](const Item& x, int pb) {
+    const uint32_t tA = tb, tO = tb + 64;
+    // epilogue of the item: O from TMEM -> staged tile + TMA store (whole chunks) or direct
+    // stores (partial chunks)
+    auto finish = [&](const Item& x) {
       wait_mma(&bars[1], ph2, bad);
       float y[1][16];
-      ld_acc<1>(ep, {tb + 128 * pb + 64}, y);
+      ld_acc<1>(ep, {tO}, y);
       const bool poisoned = *bad;
       if (x.len == BT) {
 #pragma unroll
@@ -706,8 +701,6 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
         cbar();
       }
       if (exact || *bad) {  // left to the exact kernel (or the CTA gave up: NaN outputs)
-        if (pending) finish(prev, prev_b);
-        pending = false;
         if (*bad) {
           T* ob = o + (x.t0 * H + x.head) * D;
           for (int e = tid; e < x.len * D; e += NT) stf(ob + (int64_t)(e / D) * H * D + (e % D), kNaN);
@@ -716,8 +709,9 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
         if (tid == 0) mbar_arrive(&empty[st]);
         return;
       }
-      const int b = ci & 1;
-      const uint32_t tA = tb + 128 * b, tO = tA + 64;
+      // the previous item's output store has read A's buffer before the score epilogue below
+      // writes it (gate_prep's barriers order it for every thread)
+      if (tid == 0) bulk_wait_read_all();
       gate_prep<Tg>(G.E, G.part, sH + TILE);
       gate_qk<T>(sQ, sK, sQ, sK, G.E, me, scale);
       operands_ready();
@@ -726,13 +720,10 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
         mma64(tO, sQ, 0, sH, 1, idesc_f16(64, 64, F, 0, 1), false);  // O = Q^ H'
         commit(&bars[0]);
       }
-      if (pending) finish(prev, prev_b);
-      if (tid == 0) bulk_wait_read_all();  // the staged output (same buffer as A) has been read
       wait_mma(&bars[0], ph1, bad);
       {
         float a[1][16];
         ld_acc<1>(ep, {tA}, a);
-        cbar();  // thread 0's wait above covers every thread's writes to A below
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
           const int r = ep.row(p), c = ep.col(p);
@@ -745,14 +736,10 @@ __global__ void __launch_bounds__(NT + 32, 2) tc_fwd_o_kernel(
         commit(&bars[1]);
         commit(&empty[st]);  // the stage is free once this batch has read it
       }
-      ++ci;
-      pending = true;
-      prev = x;
-      prev_b = b;
+      finish(x);
     });
-    if (pending) finish(prev, prev_b);
   }
-  pipeline_end(tb, 256);
+  pipeline_end(tb, 128);
 }
 
 // --------------------------------------------------------------------------- backward
@@ -1177,7 +1164,7 @@ int tc_fwd_o(int dtype, int dtype_g, const void* q, const void* k, const void* v
     auto kern = tc_fwd_o_kernel<T_, Tg>;
     const size_t smem = FO_NS * fo_stage_bytes<Tg>() + TILE + sizeof(GateSmem) + kAlignSlack;
     unsigned grid = 0;
-    int rc2 = persistent_grid(kern, smem, 256, MC * H, grid, NT + 32);
+    int rc2 = persistent_grid(kern, smem, 128, MC * H, grid, NT + 32);
     if (rc2) return rc2;
     launch_pdl(kern, dim3(grid), dim3(NT + 32), smem, s, mq, mk, mv, mg, mh, mo, chunk_tab, (int)MC, (int)H, scale,
                xflag, (T_*)o);
