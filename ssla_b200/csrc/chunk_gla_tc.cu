@@ -449,15 +449,15 @@ __device__ __forceinline__ void pipeline_end(uint32_t tb, uint32_t ncols) {
 }
 
 // --------------------------------------------------------------------------- local state (pipelined)
-// Two CTAs per SM, each NT compute threads + a producer warp keeping LS_NS stages of (a tile,
+// Four CTAs per SM, each NT compute threads + a producer warp keeping LS_NS stages of (a tile,
 // b tile, raw gate) in flight; a stage is released by the tensor core's commit of the item's
 // MMA.  Per item: gate prefix sums fused with the in-place scaling of the a tile, one 64x64x64
 // MMA, the fp32 increment staged from TMEM into shared memory and written by a TMA store (the
 // load/store unit stays free for the next item's shared-memory work).
-constexpr int LS_NS = 2;
+constexpr int LS_NS = 1;
 
 template <typename T, typename Tg>
-__global__ void __launch_bounds__(NT + 32, 3) tc_local_state_kernel(
+__global__ void __launch_bounds__(NT + 32, 4) tc_local_state_kernel(
     const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
     const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mds, int mode,
     const longlong2* __restrict__ chunk_tab, int MC, int H, float scale, float* __restrict__ dS,
