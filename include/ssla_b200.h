@@ -293,8 +293,9 @@ int ssla_dat_decode_windows(const uint32_t* words, const int64_t* rec_start, con
  * layers' per-position projections (layers/mos_attention.py:148-167, fp32 F.linear there).
  * B is given pre-split (ssla_split_tf32 of the fp32 weights, same [N, ldb] layout).  A, B_hi,
  * B_lo 16-byte aligned with lda, ldb multiples of 4; *err (device int) is set to 1 if a
- * pipeline wait timed out.  With K < 32, B rows may be padded to ldb >= 32 columns (faster
- * copies); the padding is read and must be finite. */
+ * pipeline wait timed out.  With K < 32 and ldb == 32, B rows are read whole (faster copies):
+ * the padding columns K..31 must be finite (zero, as ssla_b200's weight preparation writes);
+ * any other ldb reads only K columns. */
 int ssla_split_tf32(const float* x, int64_t n, float* hi, float* lo, ssla_stream_t stream);
 int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* B_hi, const float* B_lo,
                      int64_t N, int64_t ldb, float* C, int64_t ldc, int* err, ssla_stream_t stream);

@@ -418,9 +418,10 @@ extern "C" int ssla_gemm_f32_tc(const float* A, int64_t M, int64_t K, int64_t ld
   // A narrower than one k block (the first layers' 12 / 24 features): whole packed rows per
   // copy instead of 32-column boxes that read mostly outside the matrix
   const int a_cols = K < gemm::BK ? (int)K : 0;
-  // B rows padded to a whole k block (ldb >= 32 with K < 32) are read whole: their extra
-  // columns meet the zero columns of A and must only be finite
-  const int64_t bcols = (K < gemm::BK && ldb >= gemm::BK) ? gemm::BK : K;
+  // B rows padded to exactly one k block (ldb == 32 with K < 32, the layout the projection
+  // weights are prepared in) are read whole: their extra columns meet the zero columns of A and
+  // must only be finite.  Any other ldb reads K columns and lets TMA fill the rest with zeros.
+  const int64_t bcols = (K < gemm::BK && ldb == gemm::BK) ? gemm::BK : K;
   if ((rc = gemm::make_map(&ma, A, M, K, lda, gemm::BM, a_cols ? a_cols : gemm::BK)) || (rc = gemm::make_map(&mbh, B_hi, N, bcols, ldb, brows)) ||
       (rc = gemm::make_map(&mbl, B_lo, N, bcols, ldb, brows)))
     return rc;
